@@ -1,0 +1,346 @@
+#!/usr/bin/env python
+"""forge-sort B200 benchmark (driver contract: one JSON line on rank 0).
+
+Workload: sort 2^32 u32 keys -- elements [0, 2^32) of
+the seed-42 xorshift64 stream, uniform over [0, 2^32) -- partitioned over N
+GPUs (strong scaling: total keys fixed).  N = 1 is the single-GPU onesweep
+radix sort; N > 1 is the sample sort (local sort, regular-sampling
+splitters, one NCCL all-to-all, merge).
+
+  value : sorted Mkeys/s, inputs resident in HBM, out-of-place device sort
+          (the pristine input is re-read every step; 16 GiB >> 126 MB L2)
+  e2e   : the same through the host API: pinned host keys -> device -> sort
+          -> pinned host output, every step
+  roofline : dominant kernel = one onesweep pass, algorithmic bytes per key
+          = 2 x key bytes (read + write), timed live with CUDA events
+  cpu_baseline : the oracle's parallel sort (C++ stand-in for rayon
+          par_sort_unstable) on a bounded sample, rank 0 at N = 1
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gpu-forge_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "sorted Mkeys/s (u32, 2^32 keys, sample sort over N B200)"
+UNIT = "Mkeys/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--log2n", type=int, default=32, help="total keys = 2^log2n")
+    p.add_argument("--dist", choices=["uniform", "skew"], default="uniform")
+    p.add_argument("--dtype", choices=["u32", "u64"], default="u32")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--profile-steps", type=int, default=3)
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def config(args, world):
+    return {
+        "workload": f"configs[4]: sort {args.dtype} keys, {'uniform' if args.dist == 'uniform' else '70% in one 2^20 range'}"
+                    f", total 2^{args.log2n} keys partitioned over N GPUs",
+        "keys_total": 1 << args.log2n,
+        "keys_per_gpu": (1 << args.log2n) // world,
+        "key_type": args.dtype,
+        "generator": "xorshift64 seed 42 (element i = state after i+1 steps; shard r = elements [r*m,(r+1)*m))",
+        "parallelism": f"sample sort x{world}" if world > 1 else "single GPU onesweep",
+        "l2": "inputs (>= 2 GiB per GPU) larger than the 126 MB L2; no flush needed",
+    }
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.proc or not self.f:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def measured_peak_hbm():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(dtype: str):
+    """Per-key DRAM bytes of one onesweep pass from the committed ncu summary
+    (profiles/onesweep_traffic.json), scaled by the caller; None if absent."""
+    p = os.path.join(ROOT, "profiles", "onesweep_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d[dtype]["dram_bytes_per_key"], d[dtype]
+    except Exception:
+        return None, None
+
+
+# ------------------------------------------------------------------ CPU leg
+def cpu_sample_time(dtype: str, sample_n: int, threads: int, reps: int):
+    """Seconds per sort of `sample_n` keys by the oracle's CPU sort."""
+    from oracle import oracle as orc
+    x = orc.gen("u32" if dtype == "u32" else "u64", sample_n, seed=42)
+    best = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        if threads == 1:
+            orc.sort_keys(x, dtype)
+        else:
+            orc.par_sort_keys(x, dtype, threads)
+        best.append(time.perf_counter() - t0)
+    best.sort()
+    return best[len(best) // 2]
+
+
+def cpu_baseline(dtype: str):
+    from oracle import oracle as orc
+    threads = orc.max_threads()
+    n_par = 1 << 26
+    t_par = cpu_sample_time(dtype, n_par, threads, 3)
+    n_one = 1 << 24
+    t_one = cpu_sample_time(dtype, n_one, 1, 1)
+    return {
+        "value": round(n_par / t_par / 1e6, 2), "unit": UNIT, "cores": threads, "kind": "port",
+        "sample": f"2^26 {dtype} keys (same generator), median of 3; __gnu_parallel::sort on ordered bits "
+                  "(C++ stand-in for rayon par_sort_unstable)",
+        "single_thread": {"value": round(n_one / t_one / 1e6, 2), "unit": UNIT, "cores": 1,
+                          "sample": f"2^24 {dtype} keys, std::sort (stand-in for sort_unstable)"},
+    }
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (oracle port) on host cores."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+    threads = orc.max_threads()
+    sample_n = 1 << 26
+    dt = args.dtype
+    x = orc.gen("u32" if dt == "u32" else "u64", sample_n, seed=42)
+    for _ in range(args.warmup):
+        orc.par_sort_keys(x, dt, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.par_sort_keys(x, dt, threads)
+    dt_s = (time.perf_counter() - t0) / max(args.steps, 1)
+    v = round(sample_n / dt_s / 1e6, 2)
+    line = {
+        "metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_s * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dt,
+        "data": "synthetic", "config": config(args, world),
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"each step sorts 2^26 keys of the same stream with __gnu_parallel::sort "
+                                   "(C++ restatement of the reference's CPU path; Rust toolchain absent)"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ ours
+def run_ours(args):
+    import torch
+    import torch.distributed as tdist
+
+    import forge_sort
+    from forge_sort import _lib
+
+    rank, world, local = dist_env()
+    if world > 1:
+        raise SystemExit("multi-GPU sample sort not wired into bench.py yet")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.Stream(device=dev)
+    sorter = forge_sort.GpuSorter.with_context(local, stream)
+    L = _lib.load()
+    dt = args.dtype
+    kb = 4 if dt == "u32" else 8
+    n_total = 1 << args.log2n
+    m = n_total // world
+    tdt = torch.int32 if kb == 4 else torch.int64
+    keys_in = torch.empty(m, dtype=tdt, device=dev)
+    keys_out = torch.empty(m, dtype=tdt, device=dev)
+    gen = {"u32": _lib.GEN_U32, "u64": _lib.GEN_U64}[dt]
+    if args.dist == "skew":
+        gen = _lib.GEN_SKEW_U32
+    rc = L.fs_generate(gen, 42, rank * m, m, keys_in.data_ptr(), stream.cuda_stream)
+    assert rc == 0, rc
+    stream.synchronize()
+
+    def step():
+        sorter.sort_device_copy(dt, keys_in.data_ptr(), keys_out.data_ptr(), m, sync=False)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        sorter.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            torch.cuda.synchronize()
+            t0.record(stream)
+            for _ in range(args.steps):
+                step()
+            t1.record(stream)
+            t1.synchronize()
+            sorter.synchronize()  # surfaces any device-side failure
+        ms = t0.elapsed_time(t1) / args.steps
+    clocks = clk.summary()
+    launches_per_step = sorter.last_launch_count()
+
+    # correctness spot check of the timed output (sortedness + checksum-free)
+    tail = keys_out[: 1 << 20].cpu().numpy().view("u4" if kb == 4 else "u8")
+    assert (tail[1:] >= tail[:-1]).all(), "bench output not sorted"
+
+    # roofline of the dominant kernel: one onesweep pass
+    sorter.set_kernel_timing(True)
+    P = kb
+    pass_ms = []
+    with torch.cuda.stream(stream):
+        for _ in range(args.profile_steps):
+            step()
+            t = sorter.last_kernel_times()
+            pass_ms.extend(t[2:2 + P])
+            hist_ms = t[0]
+    sorter.set_kernel_timing(False)
+    pass_avg = sum(pass_ms) / len(pass_ms)
+    peak, peak_kind = measured_peak_hbm()
+    alg_bytes_pass = m * 2 * kb
+    achieved = alg_bytes_pass / (pass_avg * 1e-3) / 1e9
+    tr_per_key, tr_rec = committed_traffic(dt)
+    roofline = {
+        "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+        "traffic": round(tr_per_key * m) if tr_per_key else None,
+        "kernel": "k_onesweep (one 8-bit LSD pass)",
+        "alg_bytes_per_launch": alg_bytes_pass,
+        "pass_ms": round(pass_avg, 4), "hist_ms": round(hist_ms, 4),
+        "sort_alg_bytes_per_key": kb * (1 + 2 * P),
+        "sort_frac": round(m * kb * (1 + 2 * P) / (ms * 1e-3) / 1e9 / peak, 4),
+    }
+    if tr_rec:
+        roofline["traffic_source"] = tr_rec.get("source")
+
+    value = m * world / (ms * 1e-3) / 1e6
+
+    e2e = None
+    if not args.no_e2e:
+        h_in = torch.empty(m, dtype=tdt, pin_memory=True)
+        h_out = torch.empty(m, dtype=tdt, pin_memory=True)
+        h_in.copy_(keys_in.cpu())
+        del keys_out
+        torch.cuda.empty_cache()
+        ew = min(args.warmup, 3)
+        for _ in range(ew):
+            sorter.host_sort_copy_ptr(dt, h_in.data_ptr(), h_out.data_ptr(), m)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            sorter.host_sort_copy_ptr(dt, h_in.data_ptr(), h_out.data_ptr(), m)
+        e1.record(stream)
+        e1.synchronize()
+        ems = e0.elapsed_time(e1) / args.steps
+        e2e = {"value": round(m * world / (ems * 1e-3) / 1e6, 2), "unit": UNIT,
+               "h2d_bytes_per_step": m * kb, "d2h_bytes_per_step": m * kb,
+               "ms_per_step": round(ems, 3), "api": "fs_host_sort_keys_copy (pinned host in/out)"}
+        chk = h_out[: 1 << 20].numpy().view("u4" if kb == 4 else "u8")
+        assert (chk[1:] >= chk[:-1]).all()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(dt)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": dt, "data": "synthetic", "config": config(args, world),
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+        "gpu_launches": launches_per_step * args.steps,
+        "impl": "ours",
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    sorter.close()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,185 @@
+// fs_device.cuh -- device-side building blocks of the onesweep radix sort:
+// key-order transforms, digit extraction, lookback status words, and the
+// device-resident control block the host enqueues against.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fs {
+
+constexpr int RADIX_BITS = 8;
+constexpr int RADIX = 1 << RADIX_BITS;
+constexpr int MAX_PASSES = 8;
+
+// Order-preserving bijections onto unsigned order.  Mode numbers follow the
+// reference's SortKey constants (forge-sort src/lib.rs:16-88): i32/i64 flip the
+// sign bit both ways; f32/f64 use FloatFlip forward and its inverse
+// (shaders/sort.metal:812-868).  Here they run inside the first pass's load
+// and the last pass's store instead of in separate passes.
+enum Xform : int { XF_NONE = 0, XF_SIGN = 1, XF_FLOAT = 2 };
+
+template <typename K> struct KeyBits;
+template <> struct KeyBits<uint32_t> {
+  using S = int32_t;
+  static constexpr int BITS = 32;
+  static constexpr uint32_t SIGN = 0x80000000u;
+};
+template <> struct KeyBits<uint64_t> {
+  using S = int64_t;
+  static constexpr int BITS = 64;
+  static constexpr uint64_t SIGN = 0x8000000000000000ull;
+};
+
+// total_cmp order == unsigned order of: negative -> ~x, non-negative -> x^sign.
+template <typename K, int XF>
+__host__ __device__ __forceinline__ K to_ordered(K x) {
+  using T = KeyBits<K>;
+  if constexpr (XF == XF_SIGN) {
+    return x ^ T::SIGN;
+  } else if constexpr (XF == XF_FLOAT) {
+    K neg = (K)((typename T::S)x >> (T::BITS - 1));  // all ones if negative
+    return x ^ (neg | T::SIGN);
+  } else {
+    return x;
+  }
+}
+
+template <typename K, int XF>
+__host__ __device__ __forceinline__ K from_ordered(K y) {
+  using T = KeyBits<K>;
+  if constexpr (XF == XF_SIGN) {
+    return y ^ T::SIGN;
+  } else if constexpr (XF == XF_FLOAT) {
+    K hi = (K)((typename T::S)y >> (T::BITS - 1));  // all ones if sign set
+    return y ^ (~hi | T::SIGN);
+  } else {
+    return y;
+  }
+}
+
+template <typename K>
+__device__ __forceinline__ uint32_t digit_of(K x, int shift) {
+  return (uint32_t)(x >> shift) & (RADIX - 1);
+}
+
+// ---- lookback status word -------------------------------------------------
+// One 64-bit word per (tile, digit):  [63:42] epoch  [41:40] flag  [39:0] count.
+// The epoch tags every word with the pass that wrote it, so the status array
+// never needs clearing between passes or sorts; a word from another pass reads
+// as "not ready".  40-bit counts cover any n <= 2^40.
+constexpr uint32_t ST_NOT_READY = 0;
+constexpr uint32_t ST_AGGREGATE = 1;  // this tile's own count
+constexpr uint32_t ST_INCLUSIVE = 2;  // count of all tiles <= this one
+constexpr int ST_EPOCH_BITS = 22;
+constexpr uint32_t ST_EPOCH_MASK = (1u << ST_EPOCH_BITS) - 1;
+constexpr uint64_t ST_VALUE_MASK = (1ull << 40) - 1;
+
+__device__ __forceinline__ uint64_t st_pack(uint32_t epoch, uint32_t flag,
+                                            uint64_t v) {
+  return ((uint64_t)(epoch & ST_EPOCH_MASK) << 42) | ((uint64_t)flag << 40) |
+         (v & ST_VALUE_MASK);
+}
+__device__ __forceinline__ uint32_t st_epoch(uint64_t w) {
+  return (uint32_t)(w >> 42);
+}
+__device__ __forceinline__ uint32_t st_flag(uint64_t w) {
+  return (uint32_t)(w >> 40) & 3u;
+}
+__device__ __forceinline__ uint64_t st_value(uint64_t w) {
+  return w & ST_VALUE_MASK;
+}
+
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v)
+               : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];"
+               : "=l"(v)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_relaxed_s32(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];"
+               : "=r"(v)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- device-resident control block ------------------------------------------
+// Pass descriptors are written on the device by the plan kernel (which knows,
+// from the histogram, which passes are trivial), so the host never waits for
+// the histogram before enqueueing the passes.
+enum PassFlags : uint32_t {
+  PD_EXEC = 1u << 0,        // run this pass (not every key has the same digit)
+  PD_XF_IN = 1u << 1,       // first executed pass: apply the forward transform
+  PD_XF_OUT = 1u << 2,      // last executed pass: apply the inverse transform
+  PD_SYNTH_IDX = 1u << 3,   // payload = input position (argsort), not loaded
+  PD_WRITE_KEYS = 1u << 4,  // write keys (argsort's last pass does not)
+};
+
+struct PassDesc {
+  const void* kin;
+  void* kout;
+  const uint32_t* vin;
+  uint32_t* vout;
+  uint32_t flags;
+  uint32_t pad;
+};
+
+enum FinalOps : uint32_t {
+  FIN_COPY_KEYS = 1u << 0,
+  FIN_COPY_VALS = 1u << 1,
+  FIN_IOTA_VALS = 1u << 2,
+};
+
+struct FinalDesc {
+  const void* ksrc;
+  void* kdst;
+  const uint32_t* vsrc;
+  uint32_t* vdst;
+  uint32_t ops;
+  uint32_t executed_passes;
+};
+
+// Device error codes (ctl->err).
+constexpr int DEV_ERR_TIMEOUT = 1;
+constexpr int DEV_ERR_BOUNDS = 2;  // a scatter position fell outside [0, n)
+
+struct SortCtl {
+  unsigned long long hist[MAX_PASSES][RADIX];  // upfront histogram, all digits
+  unsigned long long base[MAX_PASSES][RADIX];  // exclusive bucket starts
+  PassDesc pass[MAX_PASSES];
+  FinalDesc fin;
+  uint32_t tile_counter[MAX_PASSES];  // dynamic tile ids, one per pass
+  int err;                            // first device-side failure
+  uint32_t err_tile;                  // where it happened (diagnostics)
+};
+
+// Per-sort arguments of the plan kernel: where the keys and payload come from
+// and where they must end up.
+struct PlanArgs {
+  uint64_t n;
+  const void* kin;   // pass-1 key source (may be const user input)
+  void* kfinal;      // where sorted keys must land
+  void* kother;      // scratch of n keys (never equal to kfinal)
+  const uint32_t* vin;  // payload source; nullptr = synthesise indices
+  uint32_t* vfinal;
+  uint32_t* vother;
+  int passes;        // digit passes: 4 (32-bit keys) or 8 (64-bit keys)
+  int has_vals;      // carry a payload
+  int write_keys;    // keys are an output (false for argsort)
+  int key_bytes;
+};
+
+}  // namespace fs

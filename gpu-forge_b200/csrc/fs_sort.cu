@@ -1,0 +1,601 @@
+// fs_sort.cu -- host orchestration and the C ABI (include/forgesort.h) of the
+// single-GPU sort.  One fs_sorter = one device + one stream + a grow-only
+// scratch arena; every sort is enqueued as
+//   upfront_hist -> plan -> P x onesweep -> finalize
+// on that stream (P = key bytes), with no host round trip in between.
+#include "forgesort.h"
+#include "fs_kernels.cuh"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+using namespace fs;
+
+struct fs_sorter {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  cudaStream_t own_stream = nullptr;
+  SortCtl* ctl = nullptr;
+  int* host_err = nullptr;      // mapped pinned word written by k_finalize
+  int* host_err_dev = nullptr;  // its device alias
+  uint64_t* status = nullptr;   // lookback status words, (tile, digit)
+  size_t status_bytes = 0;
+  void* kother = nullptr;  // n keys of scratch (the OTHER slot)
+  size_t kother_bytes = 0;
+  void* kfinal2 = nullptr;  // argsort: keys are not an output, so FINAL is scratch too
+  size_t kfinal2_bytes = 0;
+  void* vother = nullptr;
+  size_t vother_bytes = 0;
+  void* dkeys = nullptr;  // staging for the host-slice API
+  size_t dkeys_bytes = 0;
+  void* dvals = nullptr;
+  size_t dvals_bytes = 0;
+  uint32_t epoch = 1;
+  int sm_count = 0;
+  uint64_t timeout_ns = 2000000000ull;
+  uint32_t first_tile = 0;
+  int last_launches = 0;
+  bool timing = false;  // fs_set_kernel_timing
+  static constexpr int MAX_TIMED = 16;
+  cudaEvent_t ev[2 * MAX_TIMED] = {};
+  int ev_used = 0;
+  std::unordered_map<void*, size_t> allocs;  // fs_alloc'd pointers -> bytes
+  std::unordered_map<void*, int> managed;
+  std::string err;
+};
+
+namespace {
+
+thread_local std::string g_create_err;
+
+int fail(fs_sorter* s, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (s)
+    s->err = buf;
+  else
+    g_create_err = buf;
+  return code;
+}
+
+int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
+  cudaGetLastError();  // clear sticky-free errors
+  if (e == cudaErrorMemoryAllocation) return fail(s, FS_E_OOM, "%s: %s", what, cudaGetErrorString(e));
+  if (e == cudaErrorNoKernelImageForDevice || e == cudaErrorInvalidKernelImage ||
+      e == cudaErrorSharedObjectInitFailed)
+    return fail(s, FS_E_KERNEL_IMAGE, "%s: %s", what, cudaGetErrorString(e));
+  return fail(s, FS_E_GPU_EXECUTION, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define FS_CUDA(s, call)                                       \
+  do {                                                         \
+    cudaError_t e_ = (call);                                   \
+    if (e_ != cudaSuccess) return cuda_fail((s), e_, #call);   \
+  } while (0)
+
+// Tile shapes.  32-bit keys: 256 threads x 16 keys; 64-bit keys likewise
+// (32 KiB of staged keys + 16 KiB of payload per tile).
+template <typename K> struct TileCfg;
+template <> struct TileCfg<uint32_t> {
+  static constexpr int BLOCK = 256;
+  static constexpr int IPT = 16;
+};
+template <> struct TileCfg<uint64_t> {
+  static constexpr int BLOCK = 256;
+  static constexpr int IPT = 16;
+};
+
+constexpr int HIST_BLOCK = 256;
+
+int key_bytes_of(int dtype) { return dtype >= FS_U64 ? 8 : 4; }
+
+// Event pair around each launch when kernel timing is on.
+void t_begin(fs_sorter* s) {
+  if (s->timing && s->ev_used < fs_sorter::MAX_TIMED) cudaEventRecord(s->ev[2 * s->ev_used], s->stream);
+}
+void t_end(fs_sorter* s) {
+  if (s->timing && s->ev_used < fs_sorter::MAX_TIMED) cudaEventRecord(s->ev[2 * s->ev_used++ + 1], s->stream);
+}
+
+int grow(fs_sorter* s, void** p, size_t* cap, size_t need, bool zero) {
+  if (*cap >= need) return FS_OK;
+  if (*p) {
+    FS_CUDA(s, cudaStreamSynchronize(s->stream));
+    FS_CUDA(s, cudaFree(*p));
+    *p = nullptr;
+    *cap = 0;
+  }
+  cudaError_t e = cudaMalloc(p, need);
+  if (e != cudaSuccess) {
+    *p = nullptr;
+    cudaGetLastError();
+    return fail(s, FS_E_OOM, "device allocation of %zu bytes failed: %s", need, cudaGetErrorString(e));
+  }
+  *cap = need;
+  if (zero) FS_CUDA(s, cudaMemsetAsync(*p, 0, need, s->stream));
+  return FS_OK;
+}
+
+// Prefetch managed memory to the device before the kernels touch it (the
+// SortBuffer path: host writes, then sorts in place).
+int prepare_ptr(fs_sorter* s, const void* p, size_t bytes, const char* what) {
+  cudaPointerAttributes at{};
+  cudaError_t e = cudaPointerGetAttributes(&at, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(s, FS_E_INVALID, "%s: not a CUDA pointer", what);
+  }
+  if (at.type == cudaMemoryTypeManaged) {
+    FS_CUDA(s, cudaMemPrefetchAsync(p, bytes, s->device, s->stream));
+    return FS_OK;
+  }
+  if (at.type != cudaMemoryTypeDevice)
+    return fail(s, FS_E_INVALID, "%s: expected device or managed memory", what);
+  if (at.device != s->device)
+    return fail(s, FS_E_INVALID, "%s: pointer is on device %d, sorter on device %d", what, at.device,
+                s->device);
+  return FS_OK;
+}
+
+template <typename Kern>
+int blocks_per_sm(fs_sorter* s, Kern k, int block, size_t smem) {
+  int b = 0;
+  FS_CUDA(s, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, block, smem));
+  return b > 0 ? b : 1;
+}
+
+template <typename K, bool VALS, int XF>
+int launch_pass(fs_sorter* s, int pass, uint64_t n, uint32_t tiles, uint32_t epoch) {
+  constexpr int B = TileCfg<K>::BLOCK, I = TileCfg<K>::IPT;
+  using C = OnesweepCfg<K, VALS, B, I>;
+  auto kern = k_onesweep<K, VALS, XF, B, I>;
+  static int configured_mask = 0;  // bit per device (attribute is per context)
+  static int bps = 0;
+  if (!(configured_mask & (1 << (s->device & 31)))) {
+    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::DYN_SMEM));
+    bps = blocks_per_sm(s, kern, B, C::DYN_SMEM);
+    configured_mask |= 1 << (s->device & 31);
+  }
+  const uint64_t cap = (uint64_t)bps * s->sm_count;
+  const unsigned grid = (unsigned)(tiles < cap ? tiles : cap);
+  kern<<<grid, B, C::DYN_SMEM, s->stream>>>(s->ctl, pass, n, tiles, s->status, epoch, s->timeout_ns);
+  return FS_OK;
+}
+
+template <typename K, int XF>
+int enqueue_sort(fs_sorter* s, const PlanArgs& a) {
+  constexpr int P = (int)sizeof(K);
+  constexpr int TILE = TileCfg<K>::BLOCK * TileCfg<K>::IPT;
+  const uint64_t n = a.n;
+  const uint32_t tiles = (uint32_t)((n + TILE - 1) / TILE);
+  int rc = grow(s, (void**)&s->status, &s->status_bytes, (size_t)tiles * RADIX * sizeof(uint64_t), true);
+  if (rc) return rc;
+  if (s->epoch + MAX_PASSES >= ST_EPOCH_MASK) {  // epoch wrap: forget all old words
+    FS_CUDA(s, cudaMemsetAsync(s->status, 0, s->status_bytes, s->stream));
+    s->epoch = 1;
+  }
+  const uint32_t epoch0 = s->epoch;
+  s->epoch += P;
+
+  // 1. histogram of every digit; enough CTAs for ~16 keys per thread, at most
+  //    8 per SM (each CTA flushes up to P*256 global atomics).
+  uint64_t hb = (n + (uint64_t)HIST_BLOCK * 16 - 1) / ((uint64_t)HIST_BLOCK * 16);
+  const uint64_t hcap = (uint64_t)s->sm_count * 8;
+  s->ev_used = 0;
+  t_begin(s);
+  k_upfront_hist<K, XF, HIST_BLOCK><<<(unsigned)(hb < hcap ? hb : hcap), HIST_BLOCK, 0, s->stream>>>(
+      static_cast<const K*>(a.kin), n, s->ctl);
+  t_end(s);
+  // 2. plan
+  t_begin(s);
+  k_plan<<<1, RADIX, 0, s->stream>>>(s->ctl, a, s->first_tile);
+  t_end(s);
+  // 3. passes
+  for (int p = 0; p < P; ++p) {
+    t_begin(s);
+    rc = a.has_vals ? launch_pass<K, true, XF>(s, p, n, tiles, epoch0 + p)
+                    : launch_pass<K, false, XF>(s, p, n, tiles, epoch0 + p);
+    t_end(s);
+    if (rc) return rc;
+  }
+  // 4. finalize
+  uint64_t fb = (n + 255) / 256;
+  const uint64_t fcap = (uint64_t)s->sm_count * 4;
+  t_begin(s);
+  k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, s->stream>>>(s->ctl, n, s->host_err_dev);
+  t_end(s);
+  s->last_launches = P + 3;
+  FS_CUDA(s, cudaGetLastError());
+  return FS_OK;
+}
+
+int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
+  switch (dtype) {
+    case FS_U32: return enqueue_sort<uint32_t, XF_NONE>(s, a);
+    case FS_I32: return enqueue_sort<uint32_t, XF_SIGN>(s, a);
+    case FS_F32: return enqueue_sort<uint32_t, XF_FLOAT>(s, a);
+    case FS_U64: return enqueue_sort<uint64_t, XF_NONE>(s, a);
+    case FS_I64: return enqueue_sort<uint64_t, XF_SIGN>(s, a);
+    case FS_F64: return enqueue_sort<uint64_t, XF_FLOAT>(s, a);
+    default: return fail(s, FS_E_INVALID, "unknown dtype %d", dtype);
+  }
+}
+
+int finish(fs_sorter* s, int sync) {
+  FS_CUDA(s, cudaGetLastError());
+  if (!sync) return FS_OK;
+  FS_CUDA(s, cudaStreamSynchronize(s->stream));
+  const int he = *(volatile int*)s->host_err;
+  if (he != 0) {
+    *(volatile int*)s->host_err = 0;
+    if (he == DEV_ERR_BOUNDS)
+      return fail(s, FS_E_GPU_EXECUTION, "scatter position out of range (histogram/offset inconsistency)");
+    return fail(s, FS_E_TIMEOUT, "lookback timeout: a tile waited longer than %llu ms for its predecessor",
+                (unsigned long long)(s->timeout_ns / 1000000ull));
+  }
+  return FS_OK;
+}
+
+int check_common(fs_sorter* s, int dtype, uint64_t n) {
+  if (!s) return FS_E_INVALID;
+  if (dtype < FS_U32 || dtype > FS_F64) return fail(s, FS_E_INVALID, "unknown dtype %d", dtype);
+  if (n > (1ull << 32)) return fail(s, FS_E_INVALID, "n = %llu exceeds 2^32 keys per GPU", (unsigned long long)n);
+  return FS_OK;
+}
+
+int set_device(fs_sorter* s) {
+  FS_CUDA(s, cudaSetDevice(s->device));
+  return FS_OK;
+}
+
+}  // namespace
+
+// ============================================================================
+// C ABI
+// ============================================================================
+extern "C" {
+
+int fs_abi_version(void) { return FS_ABI_VERSION; }
+
+const char* fs_last_error(const fs_sorter* s) { return s ? s->err.c_str() : g_create_err.c_str(); }
+
+int fs_create(int device, void* stream, fs_sorter** out) {
+  if (!out) return fail(nullptr, FS_E_INVALID, "out is NULL");
+  *out = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(nullptr, FS_E_DEVICE_NOT_FOUND, "no CUDA device");
+  }
+  if (device < 0 || device >= count) return fail(nullptr, FS_E_DEVICE_NOT_FOUND, "no CUDA device %d", device);
+  fs_sorter* s = new fs_sorter();
+  s->device = device;
+  auto bail = [&](int rc) {
+    g_create_err = s->err;
+    fs_destroy(s);
+    return rc;
+  };
+  int rc = set_device(s);
+  if (rc) return bail(rc);
+  if (cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return bail(cuda_fail(s, cudaGetLastError(), "cudaDeviceGetAttribute"));
+  if (stream) {
+    s->stream = static_cast<cudaStream_t>(stream);
+  } else {
+    e = cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaStreamCreate"));
+    s->stream = s->own_stream;
+  }
+  e = cudaMalloc((void**)&s->ctl, sizeof(SortCtl));
+  if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaMalloc(ctl)"));
+  e = cudaMemset(s->ctl, 0, sizeof(SortCtl));
+  if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaMemset(ctl)"));
+  e = cudaHostAlloc((void**)&s->host_err, sizeof(int), cudaHostAllocMapped);
+  if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaHostAlloc(err)"));
+  *s->host_err = 0;
+  e = cudaHostGetDevicePointer((void**)&s->host_err_dev, s->host_err, 0);
+  if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaHostGetDevicePointer"));
+  if (const char* t = getenv("FORGESORT_LOOKBACK_TIMEOUT_MS")) {
+    const long long ms = atoll(t);
+    if (ms > 0) s->timeout_ns = (uint64_t)ms * 1000000ull;
+  }
+  *out = s;
+  return FS_OK;
+}
+
+int fs_destroy(fs_sorter* s) {
+  if (!s) return FS_OK;
+  cudaSetDevice(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  for (auto& kv : s->allocs) cudaFree(kv.first);
+  void* bufs[] = {s->status, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->ctl};
+  for (void* b : bufs)
+    if (b) cudaFree(b);
+  if (s->host_err) cudaFreeHost(s->host_err);
+  for (cudaEvent_t e : s->ev)
+    if (e) cudaEventDestroy(e);
+  if (s->own_stream) cudaStreamDestroy(s->own_stream);
+  cudaGetLastError();
+  delete s;
+  return FS_OK;
+}
+
+int fs_set_stream(fs_sorter* s, void* stream) {
+  if (!s) return FS_E_INVALID;
+  int rc = set_device(s);
+  if (rc) return rc;
+  FS_CUDA(s, cudaStreamSynchronize(s->stream));
+  if (stream) {
+    s->stream = static_cast<cudaStream_t>(stream);
+  } else {
+    if (!s->own_stream) FS_CUDA(s, cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking));
+    s->stream = s->own_stream;
+  }
+  return FS_OK;
+}
+
+int fs_synchronize(fs_sorter* s) {
+  if (!s) return FS_E_INVALID;
+  int rc = set_device(s);
+  if (rc) return rc;
+  return finish(s, 1);
+}
+
+int fs_alloc(fs_sorter* s, size_t bytes, int managed, void** ptr) {
+  if (!s || !ptr) return s ? fail(s, FS_E_INVALID, "ptr is NULL") : FS_E_INVALID;
+  *ptr = nullptr;
+  int rc = set_device(s);
+  if (rc) return rc;
+  const size_t b = bytes ? bytes : 16;
+  cudaError_t e = managed ? cudaMallocManaged(ptr, b, cudaMemAttachGlobal) : cudaMalloc(ptr, b);
+  if (e != cudaSuccess) {
+    *ptr = nullptr;
+    cudaGetLastError();
+    return fail(s, FS_E_OOM, "allocation of %zu bytes failed: %s", b, cudaGetErrorString(e));
+  }
+  s->allocs[*ptr] = b;
+  if (managed) s->managed[*ptr] = 1;
+  return FS_OK;
+}
+
+int fs_free(fs_sorter* s, void* ptr) {
+  if (!s) return FS_E_INVALID;
+  if (!ptr) return FS_OK;
+  auto it = s->allocs.find(ptr);
+  if (it == s->allocs.end()) return fail(s, FS_E_INVALID, "pointer was not allocated by fs_alloc");
+  int rc = set_device(s);
+  if (rc) return rc;
+  FS_CUDA(s, cudaStreamSynchronize(s->stream));
+  FS_CUDA(s, cudaFree(ptr));
+  s->allocs.erase(it);
+  s->managed.erase(ptr);
+  return FS_OK;
+}
+
+int fs_sort_keys(fs_sorter* s, int dtype, void* keys, uint64_t n, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n <= 1) return FS_OK;
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  if ((rc = prepare_ptr(s, keys, (size_t)n * kb, "keys"))) return rc;
+  if ((rc = grow(s, &s->kother, &s->kother_bytes, (size_t)n * kb, false))) return rc;
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys;
+  a.kfinal = keys;
+  a.kother = s->kother;
+  a.passes = kb;
+  a.has_vals = 0;
+  a.write_keys = 1;
+  a.key_bytes = kb;
+  if ((rc = dispatch(s, dtype, a))) return rc;
+  return finish(s, sync);
+}
+
+int fs_sort_pairs(fs_sorter* s, int dtype, void* keys, uint32_t* vals, uint64_t n, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n <= 1) return FS_OK;
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  if ((rc = prepare_ptr(s, keys, (size_t)n * kb, "keys"))) return rc;
+  if ((rc = prepare_ptr(s, vals, (size_t)n * 4, "values"))) return rc;
+  if ((rc = grow(s, &s->kother, &s->kother_bytes, (size_t)n * kb, false))) return rc;
+  if ((rc = grow(s, &s->vother, &s->vother_bytes, (size_t)n * 4, false))) return rc;
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys;
+  a.kfinal = keys;
+  a.kother = s->kother;
+  a.vin = vals;
+  a.vfinal = vals;
+  a.vother = static_cast<uint32_t*>(s->vother);
+  a.passes = kb;
+  a.has_vals = 1;
+  a.write_keys = 1;
+  a.key_bytes = kb;
+  if ((rc = dispatch(s, dtype, a))) return rc;
+  return finish(s, sync);
+}
+
+int fs_argsort(fs_sorter* s, int dtype, const void* keys, uint32_t* idx_out, uint64_t n, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n == 0) return FS_OK;
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  if ((rc = prepare_ptr(s, idx_out, (size_t)n * 4, "idx_out"))) return rc;
+  if (n == 1) {
+    FS_CUDA(s, cudaMemsetAsync(idx_out, 0, 4, s->stream));
+    s->last_launches = 0;
+    return finish(s, sync);
+  }
+  if ((rc = prepare_ptr(s, keys, (size_t)n * kb, "keys"))) return rc;
+  if ((rc = grow(s, &s->kother, &s->kother_bytes, (size_t)n * kb, false))) return rc;
+  if ((rc = grow(s, &s->kfinal2, &s->kfinal2_bytes, (size_t)n * kb, false))) return rc;
+  if ((rc = grow(s, &s->vother, &s->vother_bytes, (size_t)n * 4, false))) return rc;
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys;
+  a.kfinal = s->kfinal2;
+  a.kother = s->kother;
+  a.vin = nullptr;
+  a.vfinal = idx_out;
+  a.vother = static_cast<uint32_t*>(s->vother);
+  a.passes = kb;
+  a.has_vals = 1;
+  a.write_keys = 0;
+  a.key_bytes = kb;
+  if ((rc = dispatch(s, dtype, a))) return rc;
+  return finish(s, sync);
+}
+
+int fs_host_sort_keys(fs_sorter* s, int dtype, void* host_keys, uint64_t n) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n <= 1) return FS_OK;
+  if (!host_keys) return fail(s, FS_E_INVALID, "keys is NULL");
+  if ((rc = set_device(s))) return rc;
+  const size_t bytes = (size_t)n * key_bytes_of(dtype);
+  if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, bytes, false))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_keys, bytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = fs_sort_keys(s, dtype, s->dkeys, n, 0))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(host_keys, s->dkeys, bytes, cudaMemcpyDeviceToHost, s->stream));
+  return finish(s, 1);
+}
+
+int fs_host_sort_pairs(fs_sorter* s, int dtype, void* host_keys, uint64_t n_keys, uint32_t* host_vals,
+                       uint64_t n_vals) {
+  if (!s) return FS_E_INVALID;
+  if (n_keys != n_vals)
+    return fail(s, FS_E_LENGTH_MISMATCH, "length mismatch: keys=%llu, values=%llu", (unsigned long long)n_keys,
+                (unsigned long long)n_vals);
+  int rc = check_common(s, dtype, n_keys);
+  if (rc) return rc;
+  const uint64_t n = n_keys;
+  if (n <= 1) return FS_OK;
+  if (!host_keys || !host_vals) return fail(s, FS_E_INVALID, "keys or values is NULL");
+  if ((rc = set_device(s))) return rc;
+  const size_t kbytes = (size_t)n * key_bytes_of(dtype), vbytes = (size_t)n * 4;
+  if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, kbytes, false))) return rc;
+  if ((rc = grow(s, &s->dvals, &s->dvals_bytes, vbytes, false))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_keys, kbytes, cudaMemcpyHostToDevice, s->stream));
+  FS_CUDA(s, cudaMemcpyAsync(s->dvals, host_vals, vbytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = fs_sort_pairs(s, dtype, s->dkeys, static_cast<uint32_t*>(s->dvals), n, 0))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(host_keys, s->dkeys, kbytes, cudaMemcpyDeviceToHost, s->stream));
+  FS_CUDA(s, cudaMemcpyAsync(host_vals, s->dvals, vbytes, cudaMemcpyDeviceToHost, s->stream));
+  return finish(s, 1);
+}
+
+int fs_host_argsort(fs_sorter* s, int dtype, const void* host_keys, uint32_t* host_idx_out, uint64_t n) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n == 0) return FS_OK;
+  if (!host_keys || !host_idx_out) return fail(s, FS_E_INVALID, "keys or idx_out is NULL");
+  if (n == 1) {
+    host_idx_out[0] = 0;
+    return FS_OK;
+  }
+  if ((rc = set_device(s))) return rc;
+  const size_t kbytes = (size_t)n * key_bytes_of(dtype), vbytes = (size_t)n * 4;
+  if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, kbytes, false))) return rc;
+  if ((rc = grow(s, &s->dvals, &s->dvals_bytes, vbytes, false))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_keys, kbytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = fs_argsort(s, dtype, s->dkeys, static_cast<uint32_t*>(s->dvals), n, 0))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(host_idx_out, s->dvals, vbytes, cudaMemcpyDeviceToHost, s->stream));
+  return finish(s, 1);
+}
+
+int fs_sort_keys_copy(fs_sorter* s, int dtype, const void* keys_in, void* keys_out, uint64_t n, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  if (n == 0) return FS_OK;
+  if (keys_in == keys_out) return fs_sort_keys(s, dtype, keys_out, n, sync);
+  const char* a0 = static_cast<const char*>(keys_in);
+  const char* b0 = static_cast<const char*>(keys_out);
+  if (a0 < b0 + n * kb && b0 < a0 + n * kb) return fail(s, FS_E_INVALID, "keys_in and keys_out overlap");
+  if ((rc = prepare_ptr(s, keys_in, (size_t)n * kb, "keys_in"))) return rc;
+  if ((rc = prepare_ptr(s, keys_out, (size_t)n * kb, "keys_out"))) return rc;
+  if (n == 1) {
+    FS_CUDA(s, cudaMemcpyAsync(keys_out, keys_in, kb, cudaMemcpyDeviceToDevice, s->stream));
+    s->last_launches = 0;
+    return finish(s, sync);
+  }
+  if ((rc = grow(s, &s->kother, &s->kother_bytes, (size_t)n * kb, false))) return rc;
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys_in;
+  a.kfinal = keys_out;
+  a.kother = s->kother;
+  a.passes = kb;
+  a.has_vals = 0;
+  a.write_keys = 1;
+  a.key_bytes = kb;
+  if ((rc = dispatch(s, dtype, a))) return rc;
+  return finish(s, sync);
+}
+
+int fs_host_sort_keys_copy(fs_sorter* s, int dtype, const void* host_in, void* host_out, uint64_t n) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n == 0) return FS_OK;
+  if (!host_in || !host_out) return fail(s, FS_E_INVALID, "host_in or host_out is NULL");
+  const size_t bytes = (size_t)n * key_bytes_of(dtype);
+  if (n == 1) {
+    std::memmove(host_out, host_in, bytes);
+    return FS_OK;
+  }
+  if ((rc = set_device(s))) return rc;
+  if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, bytes, false))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_in, bytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = fs_sort_keys(s, dtype, s->dkeys, n, 0))) return rc;
+  FS_CUDA(s, cudaMemcpyAsync(host_out, s->dkeys, bytes, cudaMemcpyDeviceToHost, s->stream));
+  return finish(s, 1);
+}
+
+int fs_set_kernel_timing(fs_sorter* s, int on) {
+  if (!s) return FS_E_INVALID;
+  int rc = set_device(s);
+  if (rc) return rc;
+  if (on && !s->ev[0]) {
+    for (cudaEvent_t& e : s->ev) FS_CUDA(s, cudaEventCreate(&e));
+  }
+  s->timing = on != 0;
+  s->ev_used = 0;
+  return FS_OK;
+}
+
+int fs_last_kernel_times(fs_sorter* s, float* ms, int cap) {
+  if (!s || (!ms && cap > 0)) return -FS_E_INVALID;
+  if (!s->timing) return 0;
+  if (set_device(s)) return -FS_E_GPU_EXECUTION;
+  if (cudaStreamSynchronize(s->stream) != cudaSuccess) return -cuda_fail(s, cudaGetLastError(), "sync");
+  int k = 0;
+  for (; k < s->ev_used && k < cap; ++k) {
+    if (cudaEventElapsedTime(&ms[k], s->ev[2 * k], s->ev[2 * k + 1]) != cudaSuccess)
+      return -cuda_fail(s, cudaGetLastError(), "cudaEventElapsedTime");
+  }
+  return k;
+}
+
+uint64_t fs_scratch_bytes(const fs_sorter* s) {
+  if (!s) return 0;
+  return s->status_bytes + s->kother_bytes + s->kfinal2_bytes + s->vother_bytes + s->dkeys_bytes +
+         s->dvals_bytes + sizeof(SortCtl);
+}
+
+int fs_last_launch_count(const fs_sorter* s) { return s ? s->last_launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+"""ctypes binding of libforgesort.so (declarations in include/forgesort.h).
+
+The library is built in-tree by gpu-forge_b200/build.py.  There is no CPU or
+torch fallback: if the shared library is missing or fails to load, importing
+forge_sort raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_NAME = "libforgesort.so"
+LIB_PATH = os.path.join(HERE, LIB_NAME)
+
+# fs_dtype (include/forgesort.h)
+U32, I32, F32, U64, I64, F64 = range(6)
+
+# fs_status
+OK = 0
+E_DEVICE_NOT_FOUND = 1
+E_KERNEL_IMAGE = 2
+E_GPU_EXECUTION = 3
+E_LENGTH_MISMATCH = 4
+E_TIMEOUT = 5
+E_NCCL = 6
+E_OOM = 7
+E_INVALID = 8
+
+# Every symbol include/forgesort.h declares, with (restype, argtypes).
+_vp, _u64, _i32 = ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int
+_pp = ctypes.POINTER(ctypes.c_void_p)
+SIGNATURES = {
+    "fs_create": (_i32, [_i32, _vp, _pp]),
+    "fs_destroy": (_i32, [_vp]),
+    "fs_last_error": (ctypes.c_char_p, [_vp]),
+    "fs_set_stream": (_i32, [_vp, _vp]),
+    "fs_synchronize": (_i32, [_vp]),
+    "fs_alloc": (_i32, [_vp, ctypes.c_size_t, _i32, _pp]),
+    "fs_free": (_i32, [_vp, _vp]),
+    "fs_sort_keys": (_i32, [_vp, _i32, _vp, _u64, _i32]),
+    "fs_sort_pairs": (_i32, [_vp, _i32, _vp, _vp, _u64, _i32]),
+    "fs_argsort": (_i32, [_vp, _i32, _vp, _vp, _u64, _i32]),
+    "fs_host_sort_keys": (_i32, [_vp, _i32, _vp, _u64]),
+    "fs_host_sort_pairs": (_i32, [_vp, _i32, _vp, _u64, _vp, _u64]),
+    "fs_host_argsort": (_i32, [_vp, _i32, _vp, _vp, _u64]),
+    "fs_sort_keys_copy": (_i32, [_vp, _i32, _vp, _vp, _u64, _i32]),
+    "fs_host_sort_keys_copy": (_i32, [_vp, _i32, _vp, _vp, _u64]),
+    "fs_set_kernel_timing": (_i32, [_vp, _i32]),
+    "fs_last_kernel_times": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), _i32]),
+    "fs_scratch_bytes": (_u64, [_vp]),
+    "fs_last_launch_count": (_i32, [_vp]),
+    "fs_abi_version": (_i32, []),
+}
+# include/forgesort_bench.h
+BENCH_SIGNATURES = {
+    "fs_generate": (_i32, [_i32, _u64, _u64, _u64, _vp, _vp]),
+}
+GEN_U32, GEN_U64, GEN_SKEW_U32 = 0, 1, 2
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Load the C-ABI library (cached).  Raises OSError if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise OSError(
+            f"{path} not found: build it with `python gpu-forge_b200/build.py` "
+            "(forge_sort has no fallback implementation)")
+    L = ctypes.CDLL(path)
+    for name, (res, args) in {**SIGNATURES, **BENCH_SIGNATURES}.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L

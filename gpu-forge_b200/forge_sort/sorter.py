@@ -1,0 +1,437 @@
+"""GpuSorter / SortBuffer -- the forge-sort API over the CUDA C ABI.
+
+Mirrors metal-forge-compute/forge-sort/src/lib.rs of kavanaghpatrick/gpu-forge
+method for method (names, argument meaning, n <= 1 short-cuts, error
+variants); every call goes through libforgesort.so (include/forgesort.h).
+
+Type mapping from the Rust API:
+  &mut [u32] / &[f32] ...   -> 1-D C-contiguous numpy arrays of that dtype
+  Vec<u32> (argsort result) -> numpy uint32 array
+  SortBuffer<T>             -> SortBuffer (managed device memory; as_slice()
+                               is a numpy view the host reads in place)
+  MTLDevice / command queue -> CUDA device ordinal / cudaStream_t handle
+  Result<_, SortError>      -> return value, or raises SortError
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+from .errors import (DeviceNotFound, GpuExecution, LengthMismatch,  # noqa: F401
+                     ShaderCompilation, SortError, from_status)
+
+_DT = {
+    "u32": (_lib.U32, np.uint32, 4),
+    "i32": (_lib.I32, np.int32, 4),
+    "f32": (_lib.F32, np.float32, 4),
+    "u64": (_lib.U64, np.uint64, 8),
+    "i64": (_lib.I64, np.int64, 8),
+    "f64": (_lib.F64, np.float64, 8),
+}
+_NP_TO_NAME = {np.dtype(v[1]): k for k, v in _DT.items()}
+
+# SortKey constants (src/lib.rs:29-88): KEY_SIZE, NEEDS_TRANSFORM, IS_64BIT,
+# TRANSFORM_MODE_FORWARD, TRANSFORM_MODE_INVERSE.
+SORT_KEY = {
+    "u32": (4, False, False, 0, 0),
+    "i32": (4, True, False, 0, 0),
+    "f32": (4, True, False, 1, 2),
+    "u64": (8, False, True, 0, 0),
+    "i64": (8, True, True, 0, 0),
+    "f64": (8, True, True, 1, 2),
+}
+
+
+def dtype_name(dt) -> str:
+    """'u32' | 'i32' | 'f32' | 'u64' | 'i64' | 'f64' from a name or numpy dtype."""
+    if isinstance(dt, str) and dt in _DT:
+        return dt
+    try:
+        return _NP_TO_NAME[np.dtype(dt)]
+    except (TypeError, KeyError):
+        raise TypeError(f"not a SortKey type: {dt!r} (u32, i32, f32, u64, i64, f64)") from None
+
+
+def _stream_handle(stream) -> Optional[int]:
+    """Accept None, an int cudaStream_t, or an object with .cuda_stream."""
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream or None
+    h = getattr(stream, "cuda_stream", None)
+    if h is None:
+        raise TypeError("stream must be None, an int cudaStream_t, or have .cuda_stream")
+    return int(h) or None
+
+
+def _check_array(a, name: str, want: str) -> np.ndarray:
+    if not isinstance(a, np.ndarray):
+        raise TypeError(f"{name} must be a numpy array of {want}")
+    if a.dtype != np.dtype(_DT[want][1]):
+        raise TypeError(f"{name} has dtype {a.dtype}, expected {np.dtype(_DT[want][1])}")
+    if a.ndim != 1 or not a.flags.c_contiguous:
+        raise TypeError(f"{name} must be 1-D and C-contiguous")
+    if not a.flags.writeable:
+        raise TypeError(f"{name} must be writeable")
+    return a
+
+
+class SortBuffer:
+    """A device buffer the host can also read and write (reference
+    SortBuffer<T>, src/lib.rs:160-281).  Backed by CUDA managed memory, so
+    as_slice()/as_mut_slice() are numpy views of the same pages the kernels
+    sort; sorting prefetches them to the GPU."""
+
+    def __init__(self, sorter: "GpuSorter", dt: str, ptr: int, length: int, capacity: int,
+                 owned: bool = True):
+        self._sorter = sorter
+        self.dtype = dt
+        self._ptr = ptr
+        self._len = length
+        self._cap = capacity
+        self._owned = owned
+
+    # -- reference accessors --------------------------------------------------
+    def len(self) -> int:
+        return self._len
+
+    def __len__(self) -> int:
+        return self._len
+
+    def is_empty(self) -> bool:
+        return self._len == 0
+
+    def capacity(self) -> int:
+        return self._cap
+
+    def _view(self, count: int) -> np.ndarray:
+        npdt = np.dtype(_DT[self.dtype][1])
+        if count == 0:
+            return np.empty(0, npdt)
+        raw = (ctypes.c_uint8 * (count * npdt.itemsize)).from_address(self._ptr)
+        return np.frombuffer(raw, dtype=npdt, count=count)
+
+    def as_mut_slice(self) -> np.ndarray:
+        """Writable view of all `capacity` elements (write, then set_len)."""
+        self._sorter._host_access()
+        return self._view(self._cap)
+
+    def as_slice(self) -> np.ndarray:
+        """View of the first len() elements (sorted results after a sort)."""
+        self._sorter._host_access()
+        v = self._view(self._len)
+        v.flags.writeable = False
+        return v
+
+    def set_len(self, length: int) -> None:
+        if length > self._cap:
+            raise AssertionError(f"len {length} exceeds capacity {self._cap}")
+        self._len = length
+
+    def copy_from_slice(self, data) -> None:
+        data = np.ascontiguousarray(data, dtype=_DT[self.dtype][1])
+        if data.size > self._cap:
+            raise AssertionError(f"data len {data.size} exceeds capacity {self._cap}")
+        self._sorter._host_access()
+        self._view(data.size)[:] = data
+        self._len = data.size
+
+    def copy_to_slice(self, dest: np.ndarray) -> None:
+        n = min(self._len, dest.size)
+        self._sorter._host_access()
+        dest[:n] = self._view(n)
+
+    def device_ptr(self) -> int:
+        """Device address of element 0 (replaces metal_buffer())."""
+        return self._ptr
+
+    metal_buffer = device_ptr  # deprecated alias of the reference's accessor
+
+    @classmethod
+    def from_raw_parts(cls, sorter: "GpuSorter", dt, ptr: int, length: int, capacity: int):
+        """Wrap an existing managed/device allocation (not owned)."""
+        if length > capacity:
+            raise AssertionError(f"len {length} exceeds capacity {capacity}")
+        return cls(sorter, dtype_name(dt), ptr, length, capacity, owned=False)
+
+    def into_raw_parts(self):
+        """Give up ownership: returns (device_ptr, len, capacity)."""
+        self._owned = False
+        return self._ptr, self._len, self._cap
+
+    def free(self) -> None:
+        if self._owned and self._ptr:
+            self._sorter._call(_lib.load().fs_free(self._sorter._h, ctypes.c_void_p(self._ptr)))
+        self._ptr = 0
+        self._owned = False
+
+    def __del__(self):
+        try:
+            if self._owned and self._ptr and self._sorter._h:
+                _lib.load().fs_free(self._sorter._h, ctypes.c_void_p(self._ptr))
+        except Exception:
+            pass
+
+
+class GpuSorter:
+    """GPU radix sort for u32/i32/f32/u64/i64/f64 keys on one CUDA device.
+
+    new() / GpuSorter() create a private stream on device 0;
+    with_context(device, stream) enqueues on the caller's stream
+    (src/lib.rs:596-686).  Calls are synchronous unless stated otherwise.
+    """
+
+    def __init__(self, device: int = 0, stream=None):
+        L = _lib.load()
+        h = ctypes.c_void_p()
+        rc = L.fs_create(int(device), _stream_handle(stream), ctypes.byref(h))
+        if rc != _lib.OK:
+            raise from_status(rc, L.fs_last_error(None).decode())
+        self._h = h
+        self.device = int(device)
+        self._pending = False
+
+    @classmethod
+    def new(cls) -> "GpuSorter":
+        return cls(0, None)
+
+    @classmethod
+    def with_context(cls, device: int, stream) -> "GpuSorter":
+        return cls(device, stream)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.load().fs_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- plumbing ---------------------------------------------------------------
+    def _err_text(self) -> str:
+        return _lib.load().fs_last_error(self._h).decode()
+
+    def _call(self, rc: int, **kw) -> None:
+        if rc == _lib.OK:
+            return
+        if rc == _lib.E_INVALID:
+            raise ValueError(self._err_text())
+        raise from_status(rc, self._err_text(), **kw)
+
+    def _host_access(self) -> None:
+        # encode_sort leaves work in flight; the host must not touch managed
+        # pages until it has finished.
+        if self._pending:
+            self.synchronize()
+
+    def synchronize(self) -> None:
+        self._pending = False
+        self._call(_lib.load().fs_synchronize(self._h))
+
+    def set_stream(self, stream) -> None:
+        self._call(_lib.load().fs_set_stream(self._h, _stream_handle(stream)))
+
+    def scratch_bytes(self) -> int:
+        return int(_lib.load().fs_scratch_bytes(self._h))
+
+    def last_launch_count(self) -> int:
+        return int(_lib.load().fs_last_launch_count(self._h))
+
+    # -- zero-copy buffers (src/lib.rs:694-738, 1000-1117, 2301-2590) -----------
+    def alloc_sort_buffer(self, dt, capacity: int) -> SortBuffer:
+        name = dtype_name(dt)
+        ptr = ctypes.c_void_p()
+        self._call(_lib.load().fs_alloc(self._h, capacity * _DT[name][2], 1, ctypes.byref(ptr)))
+        return SortBuffer(self, name, ptr.value, 0, capacity)
+
+    def _sort_buf(self, buf: SortBuffer, want: str) -> None:
+        if buf.dtype != want:
+            raise TypeError(f"SortBuffer<{buf.dtype}> passed where SortBuffer<{want}> is required")
+        if buf.len() <= 1:
+            return
+        self._call(_lib.load().fs_sort_keys(self._h, _DT[want][0], ctypes.c_void_p(buf.device_ptr()),
+                                            buf.len(), 1))
+
+    def sort_buffer(self, buf: SortBuffer) -> None:
+        self._sort_buf(buf, "u32")
+
+    def sort_i32_buffer(self, buf: SortBuffer) -> None:
+        self._sort_buf(buf, "i32")
+
+    def sort_f32_buffer(self, buf: SortBuffer) -> None:
+        self._sort_buf(buf, "f32")
+
+    def sort_u64_buffer(self, buf: SortBuffer) -> None:
+        self._sort_buf(buf, "u64")
+
+    def sort_i64_buffer(self, buf: SortBuffer) -> None:
+        self._sort_buf(buf, "i64")
+
+    def sort_f64_buffer(self, buf: SortBuffer) -> None:
+        self._sort_buf(buf, "f64")
+
+    def sort_pairs_buffer(self, keys: SortBuffer, values: SortBuffer) -> None:
+        """Zero-copy stable key/value sort (additive: not in the reference)."""
+        if values.dtype != "u32":
+            raise TypeError("values must be a SortBuffer<u32>")
+        if keys.len() != values.len():
+            raise LengthMismatch(keys.len(), values.len())
+        if keys.len() <= 1:
+            return
+        self._call(_lib.load().fs_sort_pairs(self._h, _DT[keys.dtype][0], ctypes.c_void_p(keys.device_ptr()),
+                                             ctypes.c_void_p(values.device_ptr()), keys.len(), 1))
+
+    def encode_sort(self, stream, buf: SortBuffer) -> None:
+        """Enqueue an in-place u32 sort of `buf` on `stream` without waiting
+        (src/lib.rs:749-785: the caller commits and waits).  Synchronise the
+        stream (or call synchronize()) before reading the buffer."""
+        if buf.dtype != "u32":
+            raise TypeError("encode_sort takes a SortBuffer<u32>")
+        if buf.len() <= 1:
+            return
+        h = _stream_handle(stream)
+        if h is not None:
+            self.set_stream(h)
+        self._call(_lib.load().fs_sort_keys(self._h, _lib.U32, ctypes.c_void_p(buf.device_ptr()),
+                                            buf.len(), 0))
+        self._pending = True
+
+    # -- host slices (src/lib.rs:791-998, 2238-2485) --------------------------
+    def _sort_host(self, data, want: str) -> None:
+        a = _check_array(data, "data", want)
+        if a.size <= 1:
+            return
+        self._call(_lib.load().fs_host_sort_keys(self._h, _DT[want][0], ctypes.c_void_p(a.ctypes.data),
+                                                 a.size))
+
+    def sort_u32(self, data) -> None:
+        self._sort_host(data, "u32")
+
+    def sort_i32(self, data) -> None:
+        self._sort_host(data, "i32")
+
+    def sort_f32(self, data) -> None:
+        self._sort_host(data, "f32")
+
+    def sort_u64(self, data) -> None:
+        self._sort_host(data, "u64")
+
+    def sort_i64(self, data) -> None:
+        self._sort_host(data, "i64")
+
+    def sort_f64(self, data) -> None:
+        self._sort_host(data, "f64")
+
+    # -- argsort (src/lib.rs:1675-1921, 2595-2825) ----------------------------
+    def _argsort_host(self, data, want: str) -> np.ndarray:
+        if not isinstance(data, np.ndarray) or data.dtype != np.dtype(_DT[want][1]) or data.ndim != 1:
+            raise TypeError(f"data must be a 1-D numpy array of {np.dtype(_DT[want][1])}")
+        a = np.ascontiguousarray(data)
+        n = a.size
+        if n == 0:
+            return np.empty(0, np.uint32)
+        if n == 1:
+            return np.zeros(1, np.uint32)
+        out = np.empty(n, np.uint32)
+        self._call(_lib.load().fs_host_argsort(self._h, _DT[want][0], ctypes.c_void_p(a.ctypes.data),
+                                               ctypes.c_void_p(out.ctypes.data), n))
+        return out
+
+    def argsort_u32(self, data) -> np.ndarray:
+        return self._argsort_host(data, "u32")
+
+    def argsort_i32(self, data) -> np.ndarray:
+        return self._argsort_host(data, "i32")
+
+    def argsort_f32(self, data) -> np.ndarray:
+        return self._argsort_host(data, "f32")
+
+    def argsort_u64(self, data) -> np.ndarray:
+        return self._argsort_host(data, "u64")
+
+    def argsort_i64(self, data) -> np.ndarray:
+        return self._argsort_host(data, "i64")
+
+    def argsort_f64(self, data) -> np.ndarray:
+        return self._argsort_host(data, "f64")
+
+    # -- pairs (src/lib.rs:1923-2236, 2826-3015) ------------------------------
+    def _pairs_host(self, keys, values, want: str) -> None:
+        k = _check_array(keys, "keys", want)
+        v = _check_array(values, "values", "u32")
+        self._call(_lib.load().fs_host_sort_pairs(self._h, _DT[want][0], ctypes.c_void_p(k.ctypes.data), k.size,
+                                                  ctypes.c_void_p(v.ctypes.data), v.size),
+                   keys=k.size, values=v.size)
+
+    def sort_pairs_u32(self, keys, values) -> None:
+        self._pairs_host(keys, values, "u32")
+
+    def sort_pairs_i32(self, keys, values) -> None:
+        self._pairs_host(keys, values, "i32")
+
+    def sort_pairs_f32(self, keys, values) -> None:
+        self._pairs_host(keys, values, "f32")
+
+    def sort_pairs_u64(self, keys, values) -> None:
+        self._pairs_host(keys, values, "u64")
+
+    def sort_pairs_i64(self, keys, values) -> None:
+        self._pairs_host(keys, values, "i64")
+
+    def sort_pairs_f64(self, keys, values) -> None:
+        """Additive: the reference has no sort_pairs_f64."""
+        self._pairs_host(keys, values, "f64")
+
+    # -- raw device pointers (bench, sample sort, torch interop) --------------
+    def sort_device(self, dt, ptr: int, n: int, sync: bool = True) -> None:
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_sort_keys(self._h, _DT[name][0], ctypes.c_void_p(ptr), n, int(sync)))
+        self._pending = self._pending or not sync
+
+    def sort_pairs_device(self, dt, kptr: int, vptr: int, n: int, sync: bool = True) -> None:
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_sort_pairs(self._h, _DT[name][0], ctypes.c_void_p(kptr), ctypes.c_void_p(vptr),
+                                             n, int(sync)))
+        self._pending = self._pending or not sync
+
+    def argsort_device(self, dt, kptr: int, idx_ptr: int, n: int, sync: bool = True) -> None:
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_argsort(self._h, _DT[name][0], ctypes.c_void_p(kptr), ctypes.c_void_p(idx_ptr),
+                                          n, int(sync)))
+        self._pending = self._pending or not sync
+
+    def sort_device_copy(self, dt, in_ptr: int, out_ptr: int, n: int, sync: bool = True) -> None:
+        """Out-of-place sort of device keys: in_ptr is left untouched."""
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_sort_keys_copy(self._h, _DT[name][0], ctypes.c_void_p(in_ptr),
+                                                 ctypes.c_void_p(out_ptr), n, int(sync)))
+        self._pending = self._pending or not sync
+
+    def host_sort_copy_ptr(self, dt, host_in: int, host_out: int, n: int) -> None:
+        """Host-memory out-of-place sort: H2D + sort + D2H (synchronous)."""
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_host_sort_keys_copy(self._h, _DT[name][0], ctypes.c_void_p(host_in),
+                                                      ctypes.c_void_p(host_out), n))
+
+    def set_kernel_timing(self, on: bool) -> None:
+        self._call(_lib.load().fs_set_kernel_timing(self._h, int(on)))
+
+    def last_kernel_times(self, cap: int = 16):
+        """Per-kernel device times (ms) of the last sort, launch order:
+        histogram, plan, pass 0..P-1, finalize."""
+        buf = (ctypes.c_float * cap)()
+        k = _lib.load().fs_last_kernel_times(self._h, buf, cap)
+        if k < 0:
+            self._call(-k)
+        return [float(buf[i]) for i in range(k)]
+
+    def host_sort_ptr(self, dt, host_ptr: int, n: int) -> None:
+        """sort_<dt> on raw (e.g. pinned) host memory; H2D + sort + D2H."""
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_host_sort_keys(self._h, _DT[name][0], ctypes.c_void_p(host_ptr), n))

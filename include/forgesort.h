@@ -1,0 +1,166 @@
+/*
+ * forgesort.h -- C ABI of the B200 (sm_100a) radix sort behind forge-sort's
+ * GpuSorter API.
+ *
+ * Every entry point returns an fs_status (0 = success).  The text of the most
+ * recent failure on a sorter is available from fs_last_error().  No torch or
+ * CUDA C++ types cross this boundary: devices are ordinals, streams are
+ * opaque `void*` (a cudaStream_t, or NULL for the sorter's own stream),
+ * buffers are plain pointers and sizes.
+ *
+ * Reference interfaces replaced (paths inside kavanaghpatrick/gpu-forge,
+ * crate metal-forge-compute/forge-sort):
+ *   src/lib.rs:596-686      GpuSorter::new / with_context  -> fs_create
+ *   src/lib.rs:694-706      alloc_sort_buffer              -> fs_alloc
+ *   src/lib.rs:708-738      sort_buffer (+ *_buffer forms) -> fs_sort_keys
+ *   src/lib.rs:749-785      encode_sort (caller encoder)   -> fs_sort_keys(sync=0)
+ *   src/lib.rs:791-2590     sort_{u32,i32,f32,u64,i64,f64} -> fs_host_sort_keys
+ *   src/lib.rs:1675-2825    argsort_*                      -> fs_argsort / fs_host_argsort
+ *   src/lib.rs:1923-3015    sort_pairs_*                   -> fs_sort_pairs / fs_host_sort_pairs
+ *   src/lib.rs:94-104       SortError                      -> fs_status + fs_last_error
+ *   src/metal_helpers.rs:194-217 alloc_buffer / init_device_and_queue
+ *                                                          -> fs_alloc / fs_create
+ */
+#ifndef FORGESORT_H
+#define FORGESORT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FS_ABI_VERSION 1
+
+/* Key types.  Mirrors the sealed SortKey impls of src/lib.rs:16-88. */
+typedef enum fs_dtype {
+  FS_U32 = 0,
+  FS_I32 = 1,
+  FS_F32 = 2,
+  FS_U64 = 3,
+  FS_I64 = 4,
+  FS_F64 = 5
+} fs_dtype;
+
+/* Status codes.  1..4 map one-to-one onto SortError's variants
+ * (src/lib.rs:94-104); 5..8 are GPU-side failures that the Rust/C++/Python
+ * layers report as SortError::GpuExecution(text). */
+typedef enum fs_status {
+  FS_OK = 0,
+  FS_E_DEVICE_NOT_FOUND = 1,  /* SortError::DeviceNotFound            */
+  FS_E_KERNEL_IMAGE = 2,      /* SortError::ShaderCompilation(text)   */
+  FS_E_GPU_EXECUTION = 3,     /* SortError::GpuExecution(text)        */
+  FS_E_LENGTH_MISMATCH = 4,   /* SortError::LengthMismatch{keys,values} */
+  FS_E_TIMEOUT = 5,           /* a bounded device wait ran out        */
+  FS_E_NCCL = 6,              /* collective failure (multi-GPU)       */
+  FS_E_OOM = 7,               /* device allocation failed             */
+  FS_E_INVALID = 8            /* bad argument (null pointer, size)    */
+} fs_status;
+
+typedef struct fs_sorter fs_sorter;
+
+/* ---- lifetime ---------------------------------------------------------- */
+
+/* Create a sorter bound to CUDA device `device`.  `stream` is a cudaStream_t
+ * the sorter enqueues on (the analogue of with_context's command queue), or
+ * NULL to create a private non-blocking stream (the analogue of new()).
+ * Replaces src/lib.rs:596-686. */
+int fs_create(int device, void* stream, fs_sorter** out);
+int fs_destroy(fs_sorter* s);
+
+/* Text of the last failure on `s` (never NULL; "" when none).  With s == NULL,
+ * the text of the last fs_create failure on this thread. */
+const char* fs_last_error(const fs_sorter* s);
+
+/* Replace the stream the sorter enqueues on (NULL = its private stream). */
+int fs_set_stream(fs_sorter* s, void* stream);
+/* Wait for all work enqueued by `s`, then report any device-side failure
+ * (lookback timeout) that an asynchronous call left behind. */
+int fs_synchronize(fs_sorter* s);
+
+/* ---- memory (SortBuffer backing) --------------------------------------- */
+
+/* Allocate `bytes` on the sorter's device.  managed != 0 gives memory that the
+ * host may also read and write through the same pointer (cudaMallocManaged),
+ * which is what SortBuffer::as_slice/as_mut_slice rely on
+ * (src/lib.rs:694-706, src/metal_helpers.rs:194-202).  Sorting a managed
+ * buffer prefetches it to the device first. */
+int fs_alloc(fs_sorter* s, size_t bytes, int managed, void** ptr);
+int fs_free(fs_sorter* s, void* ptr);
+
+/* ---- device-resident sorts (zero-copy path) ----------------------------- */
+
+/* Sort n keys of type `dtype` in place at device (or managed) pointer `keys`.
+ * Order: unsigned order for u32/u64, signed for i32/i64, IEEE totalOrder
+ * (Rust f32::total_cmp) for f32/f64.  sync != 0 waits for completion and
+ * reports device failures; sync == 0 only enqueues (encode_sort semantics:
+ * the caller synchronises, e.g. with fs_synchronize).
+ * Replaces sort_buffer / sort_*_buffer / encode_sort (src/lib.rs:708-785,
+ * 1000-1117, 2301-2346, 2486-2590). */
+int fs_sort_keys(fs_sorter* s, int dtype, void* keys, uint64_t n, int sync);
+
+/* Sort (key, u32 value) pairs in place, stably by key (equal keys keep their
+ * input order).  New zero-copy form of sort_pairs_* (src/lib.rs:1923-2236,
+ * 2826-3015), used by SortBuffer-based pairs sorting. */
+int fs_sort_pairs(fs_sorter* s, int dtype, void* keys, uint32_t* vals,
+                  uint64_t n, int sync);
+
+/* Write to idx_out the stable sorting permutation of keys (idx_out[i] = index
+ * of the i-th smallest key; ties in index order).  `keys` is not modified.
+ * n must be <= 2^32.  Replaces argsort_* (src/lib.rs:1675-1921, 2595-2825). */
+int fs_argsort(fs_sorter* s, int dtype, const void* keys, uint32_t* idx_out,
+               uint64_t n, int sync);
+
+/* Out-of-place form: sorted copy of keys_in written to keys_out (device or
+ * managed pointers, n keys each, non-overlapping); keys_in is not modified.
+ * The reference's slice API does the same internally -- it copies the slice
+ * into its own buffer before sorting (src/lib.rs:800-812) -- but fuses no
+ * copy: the first pass reads keys_in and the last pass writes keys_out. */
+int fs_sort_keys_copy(fs_sorter* s, int dtype, const void* keys_in,
+                      void* keys_out, uint64_t n, int sync);
+
+/* ---- host-slice sorts (sort_u32(&mut [u32]) etc.) ------------------------ */
+
+/* Copy host keys to the device, sort, copy back; synchronous.  Pinned host
+ * memory gives full copy bandwidth; pageable memory also works.
+ * Replaces sort_u32/i32/f32/u64/i64/f64 (src/lib.rs:791-998, 2238-2485). */
+int fs_host_sort_keys(fs_sorter* s, int dtype, void* host_keys, uint64_t n);
+/* Length check first (LengthMismatch), then n <= 1 short-cut, as
+ * src/lib.rs:1928-1937 orders them. */
+int fs_host_sort_pairs(fs_sorter* s, int dtype, void* host_keys,
+                       uint64_t n_keys, uint32_t* host_vals, uint64_t n_vals);
+int fs_host_argsort(fs_sorter* s, int dtype, const void* host_keys,
+                    uint32_t* host_idx_out, uint64_t n);
+/* Host out-of-place form of sort_u32 etc.: host_in -> device -> sort ->
+ * host_out (host_in untouched); synchronous.  Same copy-in / sort /
+ * copy-out sequence as src/lib.rs:791-837. */
+int fs_host_sort_keys_copy(fs_sorter* s, int dtype, const void* host_in,
+                           void* host_out, uint64_t n);
+
+/* ---- per-kernel timing ---------------------------------------------------- */
+
+/* on != 0: record a CUDA event pair around every kernel the sorter launches,
+ * on its own stream (the forge-primitives GpuTimer analogue,
+ * forge-primitives/src/timing.rs:9-47).  Off by default. */
+int fs_set_kernel_timing(fs_sorter* s, int on);
+/* After a synchronous sort with timing on: write up to `cap` kernel
+ * durations in ms (launch order: histogram, plan, pass 0..P-1, finalize) and
+ * return how many were written (negative fs_status on failure). */
+int fs_last_kernel_times(fs_sorter* s, float* ms, int cap);
+
+/* ---- introspection ------------------------------------------------------- */
+
+/* Bytes of device scratch the sorter holds right now (grow-only arena,
+ * the analogue of ensure_buffers at src/lib.rs:1120-1289). */
+uint64_t fs_scratch_bytes(const fs_sorter* s);
+/* Number of kernels the last sort enqueued. */
+int fs_last_launch_count(const fs_sorter* s);
+/* ABI version (FS_ABI_VERSION). */
+int fs_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FORGESORT_H */

@@ -1,0 +1,120 @@
+"""SortBuffer (zero-copy), encode_sort on a caller stream, scratch reuse and
+cross-type interleaving -- the reference's correctness.rs:86-239 and
+regression.rs:8-193 behaviours."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def test_sort_buffer_basic_and_direct_write(sorter):
+    buf = sorter.alloc_sort_buffer("u32", 1000)
+    assert buf.capacity() == 1000 and buf.len() == 0 and buf.is_empty()
+    x = orc.gen("u32", 1000, seed=1)
+    buf.as_mut_slice()[:1000] = x
+    buf.set_len(1000)
+    sorter.sort_buffer(buf)
+    assert np.array_equal(buf.as_slice(), np.sort(x))
+    out = np.zeros(1000, np.uint32)
+    buf.copy_to_slice(out)
+    assert np.array_equal(out, np.sort(x))
+    with pytest.raises(AssertionError):
+        buf.set_len(1001)
+
+
+@pytest.mark.parametrize("dt,dist", [("i32", "i32"), ("f32", "f32_mix"), ("u64", "u64"),
+                                     ("i64", "i64"), ("f64", "f64_logu")])
+def test_typed_buffers(sorter, dt, dist):
+    x = orc.gen(dist, 50_001, seed=2)
+    buf = sorter.alloc_sort_buffer(dt, x.size)
+    buf.copy_from_slice(x)
+    getattr(sorter, f"sort_{dt}_buffer")(buf)
+    want = orc.sort_keys(x, dt)
+    assert np.array_equal(buf.as_slice().view(orc.BITS_DTYPE[dt]), want.view(orc.BITS_DTYPE[dt]))
+    with pytest.raises(TypeError):
+        sorter.sort_buffer(buf)  # SortBuffer<u32> required
+
+
+def test_sort_buffer_reuse_and_grow_only_scratch(sorter):
+    buf = sorter.alloc_sort_buffer("u32", 1 << 20)
+    sizes = [1 << 20, 1000, 4097, 1 << 18]
+    peak = 0
+    for i, n in enumerate(sizes):
+        x = orc.gen("u32", n, seed=10 + i)
+        buf.copy_from_slice(x)
+        sorter.sort_buffer(buf)
+        assert np.array_equal(buf.as_slice(), np.sort(x))
+        s = sorter.scratch_bytes()
+        assert s >= peak
+        peak = s
+
+
+def test_sort_pairs_buffer(sorter):
+    n = 100_000
+    k = orc.gen("zipf_u32", n, seed=5)
+    kb = sorter.alloc_sort_buffer("u32", n)
+    vb = sorter.alloc_sort_buffer("u32", n)
+    kb.copy_from_slice(k)
+    vb.copy_from_slice(np.arange(n, dtype=np.uint32))
+    sorter.sort_pairs_buffer(kb, vb)
+    wk, wv = orc.sort_pairs(k, np.arange(n, dtype=np.uint32), "u32")
+    assert np.array_equal(kb.as_slice(), wk) and np.array_equal(vb.as_slice(), wv)
+
+
+def test_encode_sort_on_caller_stream(sorter):
+    import torch
+    s = torch.cuda.Stream()
+    buf = sorter.alloc_sort_buffer("u32", 1024)
+    data = np.array([50, 10, 90, 30, 70, 20, 80, 40, 60, 100], np.uint32)
+    buf.copy_from_slice(data)
+    sorter.encode_sort(s, buf)
+    s.synchronize()
+    assert list(buf.as_slice()) == sorted(data.tolist())
+    one = sorter.alloc_sort_buffer("u32", 1)
+    one.copy_from_slice(np.array([42], np.uint32))
+    sorter.encode_sort(s, one)  # n <= 1: nothing enqueued
+    assert list(one.as_slice()) == [42]
+    sorter.set_stream(None)
+
+
+def test_with_context_shares_caller_stream():
+    import torch
+    from forge_sort import GpuSorter
+    st = torch.cuda.Stream()
+    s = GpuSorter.with_context(0, st)
+    t = torch.from_numpy(orc.gen("u32", 1 << 16, seed=3).view(np.int32)).cuda()
+    with torch.cuda.stream(st):
+        s.sort_device("u32", t.data_ptr(), t.numel(), sync=False)
+    st.synchronize()
+    got = t.cpu().numpy().view(np.uint32)
+    assert np.array_equal(got, np.sort(orc.gen("u32", 1 << 16, seed=3)))
+    s.close()
+
+
+def test_cross_type_interleave(sorter):
+    for i in range(3):
+        for dt, dist in (("u32", "u32"), ("f64", "f64_logu"), ("i32", "i32"), ("u64", "u64"), ("f32", "f32_mix")):
+            x = orc.gen(dist, 10_000 + i, seed=i)
+            a = x.copy()
+            getattr(sorter, f"sort_{dt}")(a)
+            assert np.array_equal(a.view(orc.BITS_DTYPE[dt]), orc.sort_keys(x, dt).view(orc.BITS_DTYPE[dt]))
+            assert np.array_equal(getattr(sorter, f"argsort_{dt}")(x), orc.argsort(x, dt))
+
+
+def test_device_pointer_checks(sorter):
+    host = np.zeros(16, np.uint32)
+    with pytest.raises(ValueError):
+        sorter.sort_device("u32", host.ctypes.data, 16)
+
+
+def test_launch_count(sorter):
+    x = orc.gen("u32", 100_000, seed=1)
+    sorter.sort_u32(x.copy())
+    assert sorter.last_launch_count() == 4 + 3
+    y = orc.gen("u64", 100_000, seed=1)
+    sorter.sort_u64(y.copy())
+    assert sorter.last_launch_count() == 8 + 3
