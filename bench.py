@@ -263,16 +263,20 @@ def run_ours(args):
     assert (tail[1:] >= tail[:-1]).all(), "bench output not sorted"
 
     # roofline of the dominant kernel: one onesweep pass
+    # kernel timing order: histogram, plan, (count+scan, scatter) x P, finalize
     sorter.set_kernel_timing(True)
     P = kb
-    pass_ms = []
+    pass_ms, count_ms, hist_l = [], [], []
     with torch.cuda.stream(stream):
         for _ in range(args.profile_steps):
             step()
             t = sorter.last_kernel_times()
-            pass_ms.extend(t[2:2 + P])
-            hist_ms = t[0]
+            hist_l.append(t[0])
+            count_ms.extend(t[2 + 2 * p] for p in range(1, P))
+            pass_ms.extend(t[3 + 2 * p] for p in range(P))
     sorter.set_kernel_timing(False)
+    hist_ms = sum(hist_l) / len(hist_l)
+    count_avg = sum(count_ms) / max(len(count_ms), 1)
     pass_avg = sum(pass_ms) / len(pass_ms)
     peak, peak_kind = measured_peak_hbm()
     alg_bytes_pass = m * 2 * kb
@@ -282,9 +286,11 @@ def run_ours(args):
         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
         "traffic": round(tr_per_key * m) if tr_per_key else None,
-        "kernel": "k_onesweep (one 8-bit LSD pass)",
+        "kernel": "k_scatter (one 8-bit LSD pass: rank, stage, scatter)",
         "alg_bytes_per_launch": alg_bytes_pass,
-        "pass_ms": round(pass_avg, 4), "hist_ms": round(hist_ms, 4),
+        "pass_ms": round(pass_avg, 4), "hist_ms": round(hist_ms, 4), "count_ms": round(count_avg, 4),
+        "count_frac": round(m * kb / (count_avg * 1e-3) / 1e9 / peak, 4) if count_avg else None,
+        "hist_frac": round(m * kb / (hist_ms * 1e-3) / 1e9 / peak, 4),
         "sort_alg_bytes_per_key": kb * (1 + 2 * P),
         "sort_frac": round(m * kb * (1 + 2 * P) / (ms * 1e-3) / 1e9 / peak, 4),
     }

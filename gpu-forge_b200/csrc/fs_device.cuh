@@ -63,45 +63,6 @@ __device__ __forceinline__ uint32_t digit_of(K x, int shift) {
   return (uint32_t)(x >> shift) & (RADIX - 1);
 }
 
-// ---- lookback status word -------------------------------------------------
-// One 64-bit word per (tile, digit):  [63:42] epoch  [41:40] flag  [39:0] count.
-// The epoch tags every word with the pass that wrote it, so the status array
-// never needs clearing between passes or sorts; a word from another pass reads
-// as "not ready".  40-bit counts cover any n <= 2^40.
-constexpr uint32_t ST_NOT_READY = 0;
-constexpr uint32_t ST_AGGREGATE = 1;  // this tile's own count
-constexpr uint32_t ST_INCLUSIVE = 2;  // count of all tiles <= this one
-constexpr int ST_EPOCH_BITS = 22;
-constexpr uint32_t ST_EPOCH_MASK = (1u << ST_EPOCH_BITS) - 1;
-constexpr uint64_t ST_VALUE_MASK = (1ull << 40) - 1;
-
-__device__ __forceinline__ uint64_t st_pack(uint32_t epoch, uint32_t flag,
-                                            uint64_t v) {
-  return ((uint64_t)(epoch & ST_EPOCH_MASK) << 42) | ((uint64_t)flag << 40) |
-         (v & ST_VALUE_MASK);
-}
-__device__ __forceinline__ uint32_t st_epoch(uint64_t w) {
-  return (uint32_t)(w >> 42);
-}
-__device__ __forceinline__ uint32_t st_flag(uint64_t w) {
-  return (uint32_t)(w >> 40) & 3u;
-}
-__device__ __forceinline__ uint64_t st_value(uint64_t w) {
-  return w & ST_VALUE_MASK;
-}
-
-__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v)
-               : "memory");
-}
-__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];"
-               : "=l"(v)
-               : "l"(p)
-               : "memory");
-  return v;
-}
 __device__ __forceinline__ int ld_relaxed_s32(const int* p) {
   int v;
   asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];"
@@ -126,6 +87,8 @@ enum PassFlags : uint32_t {
   PD_XF_OUT = 1u << 2,      // last executed pass: apply the inverse transform
   PD_SYNTH_IDX = 1u << 3,   // payload = input position (argsort), not loaded
   PD_WRITE_KEYS = 1u << 4,  // write keys (argsort's last pass does not)
+  PD_FIRST = 1u << 5,       // first executed pass: slice counts come from the
+                            // upfront histogram (input order is unchanged)
 };
 
 struct PassDesc {
@@ -153,7 +116,7 @@ struct FinalDesc {
 };
 
 // Device error codes (ctl->err).
-constexpr int DEV_ERR_TIMEOUT = 1;
+constexpr int DEV_ERR_TIMEOUT = 1;  // a bounded wait (bulk-copy barrier) ran out
 constexpr int DEV_ERR_BOUNDS = 2;  // a scatter position fell outside [0, n)
 
 struct SortCtl {
@@ -161,9 +124,15 @@ struct SortCtl {
   unsigned long long base[MAX_PASSES][RADIX];  // exclusive bucket starts
   PassDesc pass[MAX_PASSES];
   FinalDesc fin;
-  uint32_t tile_counter[MAX_PASSES];  // dynamic tile ids, one per pass
-  int err;                            // first device-side failure
-  uint32_t err_tile;                  // where it happened (diagnostics)
+  int err;  // first device-side failure (DEV_ERR_*)
+};
+
+// Slice geometry shared by the histogram, count, scan and scatter kernels:
+// slice c holds keys [c*keys_per_slice, min((c+1)*keys_per_slice, n)), a whole
+// number of scatter tiles, and is owned by CTA c of each of those kernels.
+struct Slices {
+  uint64_t keys_per_slice;
+  uint32_t count;
 };
 
 // Per-sort arguments of the plan kernel: where the keys and payload come from
@@ -180,6 +149,8 @@ struct PlanArgs {
   int has_vals;      // carry a payload
   int write_keys;    // keys are an output (false for argsort)
   int key_bytes;
+  unsigned long long* counts_out;  // optional copy of pass-0 digit counts
+  int ncounts;                     // entries of counts_out
 };
 
 }  // namespace fs

@@ -1,92 +1,245 @@
-// fs_kernels.cuh -- the sm_100a kernels of one sort:
+// fs_kernels.cuh -- the sm_100a kernels of one sort.
 //
-//   k_upfront_hist   one read of the keys -> histograms of ALL digit passes
-//   k_plan           exclusive bucket starts per pass, trivial-pass detection,
-//                    device-side pass/buffer plan (1 CTA)
-//   k_onesweep       one stable 8-bit LSD pass: warp-multisplit rank,
-//                    decoupled lookback across tiles, shared-memory staging by
-//                    digit, coalesced scatter; payload carried alongside
+// Per sort (P = key bytes, one 8-bit digit per pass, LSD):
+//   k_upfront_hist   one read of the keys -> global histograms of ALL digits,
+//                    and per-slice histograms of all digits
+//   k_plan           bucket starts per pass, trivial-pass detection,
+//                    device-side buffer routing (1 CTA)
+// per executed pass:
+//   k_count          per-slice counts of this pass's digit (skipped for the
+//                    first executed pass: the upfront slice histograms hold
+//                    them, the input order being unchanged)
+//   k_slice_scan     per-(slice, digit) global output offsets
+//   k_scatter        CTA c walks slice c tile by tile: warp multisplit rank,
+//                    shared-memory staging by digit, coalesced scatter;
+//                    payload carried alongside; next tile bulk-prefetched
+// then:
 //   k_finalize       copy-back / iota when the plan needs it; error hand-off
 //
-// They replace the reference pipeline sort_msd_histogram -> sort_msd_prep ->
+// The array is cut into as many contiguous slices as the scatter kernel keeps
+// CTAs resident, so no CTA ever waits on another: the offsets a slice needs
+// come from the counts, not from a chained scan across concurrently running
+// tiles.  That costs one extra read of the keys per pass after the first and
+// removes the latency-bound inter-CTA dependency chain.
+//
+// Replaces the reference pipeline sort_msd_histogram -> sort_msd_prep ->
 // sort_msd_atomic_scatter -> sort_inner_fused (+ sort_transform_*,
-// sort_init_indices, sort_gather_values) in forge-sort shaders/sort.metal.
+// sort_init_indices, sort_gather_values) of forge-sort shaders/sort.metal.
 #pragma once
 
 #include "fs_device.cuh"
 
-#ifndef FS_ONESWEEP_MIN_BLOCKS
-#define FS_ONESWEEP_MIN_BLOCKS 3
+#ifndef FS_RANK_BALLOT
+#define FS_RANK_BALLOT 1
 #endif
 
 namespace fs {
 
-// --------------------------------------------------------------------------
-// Upfront histogram: every digit of every pass from one read of the keys.
-// Replaces sort_msd_histogram (shaders/sort.metal:64-142), which counted only
-// the most significant byte, and the per-bucket histograms that
-// sort_inner_fused recomputed (sort.metal:378-769).
-//
-// Per key: P shared-memory increments.  When a whole warp shares the digit of
-// a pass (skewed keys: small integers, Zipf, all-equal), lane 0 adds the warp
-// count once instead of 32 conflicting atomics; the test costs one shuffle
-// and one warp OR-reduction per key.
-// --------------------------------------------------------------------------
-template <typename K, int XF, int BLOCK>
-__global__ void __launch_bounds__(BLOCK)
-    k_upfront_hist(const K* __restrict__ keys, uint64_t n, SortCtl* __restrict__ ctl) {
-  constexpr int P = (int)sizeof(K);
-  __shared__ uint32_t h[P][RADIX];
-  for (int i = threadIdx.x; i < P * RADIX; i += BLOCK) (&h[0][0])[i] = 0;
-  __syncthreads();
+// ---- bulk-copy (TMA, non-tensor, no multicast) + mbarrier helpers ----------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// global -> shared bulk copy; both addresses 16-byte aligned, bytes % 16 == 0
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+// Bounded wait on an mbarrier phase; false (and *err set) on timeout.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t timeout_ns, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0 && global_timer_ns() - t0 > timeout_ns) {
+      atomicCAS(err, 0, DEV_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
 
+// ---- digit functors ------------------------------------------------------------
+// A radix pass takes byte `shift/8` of the ordered key; the sample sort's
+// partition pass takes the index of the splitter bucket that the element's
+// (ordered key, global position) falls in.  The position breaks ties, so
+// equal keys still spread over ranks in input order.
+struct RadixDigit {
+  int shift;
+  static constexpr bool STAGE = false;  // recomputed from the staged key
+  template <typename K>
+  __device__ __forceinline__ uint32_t operator()(K k, uint64_t) const {
+    return digit_of(k, shift);
+  }
+};
+
+template <typename K, int XF>
+struct SplitterDigit {
+  const K* keys;         // nsplit raw splitter keys, ascending by (key, gpos)
+  const uint64_t* gpos;  // their global positions
+  int nsplit;
+  static constexpr bool STAGE = true;  // digits staged in shared memory
+  // number of splitters <= (k, g) in (ordered key, position) order
+  __device__ __forceinline__ uint32_t operator()(K k, uint64_t g) const {
+    int lo = 0, hi = nsplit;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      const K sk = to_ordered<K, XF>(__ldg(keys + mid));
+      const bool le = sk < k || (sk == k && __ldg(gpos + mid) <= g);
+      lo = le ? mid + 1 : lo;
+      hi = le ? hi : mid;
+    }
+    return (uint32_t)lo;
+  }
+};
+
+// Add one key per lane of a warp to per-digit counters h[pass][digit] for the
+// P lowest digits.  All lanes call this together.  When the whole warp
+// shares a pass's digit (small integers, Zipf, all-equal keys), one lane adds
+// the warp count instead of 32 same-address atomics.
+template <typename K, int P>
+__device__ __forceinline__ void warp_count_digits(uint32_t (*h)[RADIX], K x, bool valid) {
   const uint32_t lane = threadIdx.x & 31;
-  auto count = [&](K x, bool valid) {
-    x = to_ordered<K, XF>(x);
-    const uint32_t active = __ballot_sync(0xffffffffu, valid);
-    if (!valid) return;
-    // bits in which some active lane differs from the first active lane
-    const int src = __ffs(active) - 1;
-    const K x0 = __shfl_sync(active, x, src);
-    const K diff = x ^ x0;
-    uint32_t dlo = __reduce_or_sync(active, (uint32_t)diff);
-    uint32_t dhi = 0;
-    if constexpr (sizeof(K) == 8) dhi = __reduce_or_sync(active, (uint32_t)((uint64_t)diff >> 32));
+  const uint32_t active = __ballot_sync(0xffffffffu, valid);
+  if (!valid) return;
+  const int src = __ffs(active) - 1;
+  const K diff = x ^ __shfl_sync(active, x, src);
+  uint32_t dlo = __reduce_or_sync(active, (uint32_t)diff);
+  uint32_t dhi = 0xffffffffu;
+  if constexpr (sizeof(K) == 8) dhi = __reduce_or_sync(active, (uint32_t)((uint64_t)diff >> 32));
+  if constexpr (P < 4) dlo |= 0xffffffffu << (8 * P);  // bytes beyond P do not count
+  // a byte of dlo/dhi is zero <=> the whole warp shares that digit
+  const bool any_uniform =
+      (((dlo - 0x01010101u) & ~dlo & 0x80808080u) | ((dhi - 0x01010101u) & ~dhi & 0x80808080u)) != 0u;
+  if (!any_uniform) {
+#pragma unroll
+    for (int p = 0; p < P; ++p) atomicAdd(&h[p][digit_of(x, RADIX_BITS * p)], 1u);
+  } else {
 #pragma unroll
     for (int p = 0; p < P; ++p) {
       const uint32_t dbyte = (p < 4 ? (dlo >> (8 * p)) : (dhi >> (8 * (p - 4)))) & 0xffu;
       const uint32_t d = digit_of(x, RADIX_BITS * p);
-      if (dbyte) {
+      if (dbyte)
         atomicAdd(&h[p][d], 1u);
-      } else if (lane == (uint32_t)src) {
+      else if (lane == (uint32_t)src)
         atomicAdd(&h[p][d], (uint32_t)__popc(active));
+    }
+  }
+}
+
+// Visit the keys of [lo, hi) with the CTA's threads in coalesced order, 16-byte
+// vector loads when `keys` is 16-byte aligned (VEC), four loads (64 bytes) in
+// flight per thread to cover HBM latency; f(key, valid) is called by whole
+// warps (valid = in range).
+template <typename K, int BLOCK, bool VEC, typename F>
+__device__ __forceinline__ void for_each_key(const K* __restrict__ keys, uint64_t lo, uint64_t hi, F&& f) {
+  const uint32_t lane = threadIdx.x & 31, wbase = threadIdx.x & ~31u;
+  uint64_t tail = lo;
+  if constexpr (VEC) {
+    constexpr int KV = 16 / (int)sizeof(K);
+    constexpr int U = 4;
+    // lo is a multiple of KV for every slice (slices are whole tiles)
+    const uint64_t v0 = lo / KV, v1 = hi / KV;
+    const uint4* kv = reinterpret_cast<const uint4*>(keys);
+    uint64_t w = v0 + wbase;
+    for (; w + (U - 1) * BLOCK + 32 <= v1; w += U * BLOCK) {
+      uint4 a[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) a[u] = __ldcs(kv + w + u * BLOCK + lane);  // streamed: read once
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const K* ka = reinterpret_cast<const K*>(&a[u]);
+#pragma unroll
+        for (int q = 0; q < KV; ++q) f(ka[q], true);
       }
     }
-  };
+    for (; w < v1; w += BLOCK) {
+      const bool valid = w + lane < v1;
+      const uint4 a = valid ? kv[w + lane] : make_uint4(0, 0, 0, 0);
+      const K* ka = reinterpret_cast<const K*>(&a);
+#pragma unroll
+      for (int q = 0; q < KV; ++q) f(ka[q], valid);
+    }
+    tail = v1 * KV;
+  }
+  for (uint64_t w = tail + wbase; w < hi; w += BLOCK) {
+    const bool valid = w + lane < hi;
+    f(valid ? keys[w + lane] : K(0), valid);
+  }
+}
 
-  // Loop bounds are tested on the warp's first index (the stride is a
-  // multiple of 32), so whole warps iterate together and the warp-wide
-  // shuffles and reductions above stay converged.
-  const uint64_t stride = (uint64_t)gridDim.x * BLOCK;
-  uint64_t wb = (uint64_t)blockIdx.x * BLOCK + (threadIdx.x & ~31u);
-  // 4 independent loads in flight per thread
-  for (; wb + 3 * stride + 32 <= n; wb += 4 * stride) {
-    const uint64_t j = wb + lane;
-    const K x0 = keys[j], x1 = keys[j + stride], x2 = keys[j + 2 * stride], x3 = keys[j + 3 * stride];
-    count(x0, true);
-    count(x1, true);
-    count(x2, true);
-    count(x3, true);
-  }
-  for (; wb < n; wb += stride) {
-    const uint64_t j = wb + lane;
-    const bool valid = j < n;
-    count(valid ? keys[j] : K(0), valid);
-  }
+// --------------------------------------------------------------------------
+// Upfront histogram: every digit of every pass from one read of the keys.
+// CTA c reads slice c; it writes its slice histograms (the first executed
+// pass's slice counts) and adds them into the global histograms.
+// Replaces sort_msd_histogram (shaders/sort.metal:64-142), which counted only
+// the most significant byte, and the per-bucket histograms that
+// sort_inner_fused recomputed (sort.metal:378-769).
+// --------------------------------------------------------------------------
+template <typename K, int XF, int BLOCK, bool VEC>
+__global__ void __launch_bounds__(BLOCK)
+    k_upfront_hist(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
+                   uint32_t* __restrict__ slice_hist /* [count][P][RADIX] */) {
+  constexpr int P = (int)sizeof(K);
+  __shared__ uint32_t h[P][RADIX];
+  for (int i = threadIdx.x; i < P * RADIX; i += BLOCK) (&h[0][0])[i] = 0;
   __syncthreads();
+  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
+  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+  for_each_key<K, BLOCK, VEC>(keys, lo, hi,
+                              [&](K x, bool valid) { warp_count_digits<K, P>(h, to_ordered<K, XF>(x), valid); });
+  __syncthreads();
+  uint32_t* out = slice_hist + (size_t)blockIdx.x * P * RADIX;
   for (int b = threadIdx.x; b < P * RADIX; b += BLOCK) {
     const uint32_t c = (&h[0][0])[b];
+    out[b] = c;
     if (c) atomicAdd(&(&ctl->hist[0][0])[b], (unsigned long long)c);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Bucket histogram of the sample sort's partition pass (one pass, digit =
+// splitter bucket): global counts into ctl->hist[0], slice counts into
+// slice_hist[c][0][*].
+// --------------------------------------------------------------------------
+template <typename K, int XF, int BLOCK>
+__global__ void __launch_bounds__(BLOCK)
+    k_bucket_hist(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
+                  uint32_t* __restrict__ slice_hist, const SplitterDigit<K, XF> dfn, const uint64_t gpos_base) {
+  __shared__ uint32_t h[RADIX];
+  for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[i] = 0;
+  __syncthreads();
+  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
+  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+  for (uint64_t i = lo + threadIdx.x; i < hi; i += BLOCK)
+    atomicAdd(&h[dfn(to_ordered<K, XF>(keys[i]), gpos_base + i)], 1u);
+  __syncthreads();
+  uint32_t* out = slice_hist + (size_t)blockIdx.x * RADIX;
+  for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
+    out[b] = h[b];
+    if (h[b]) atomicAdd(&ctl->hist[0][b], (unsigned long long)h[b]);
   }
 }
 
@@ -96,16 +249,16 @@ __global__ void __launch_bounds__(BLOCK)
 // is skipped.  Then thread 0 routes the executed passes through the key and
 // payload buffers so that the result lands where the caller wants it.
 // Replaces sort_msd_prep (shaders/sort.metal:153-181).  Also zeroes the
-// histogram and the tile counters for the next sort.
+// histogram for the next sort.
 // --------------------------------------------------------------------------
-__global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanArgs a,
-                                                uint32_t first_tile) {
+__global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanArgs a) {
   const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
   __shared__ unsigned long long s_wsum[RADIX / 32];
   __shared__ int s_exec[MAX_PASSES];
   for (int p = 0; p < a.passes; ++p) {
     const unsigned long long c = ctl->hist[p][d];
     ctl->hist[p][d] = 0ull;
+    if (p == 0 && a.counts_out != nullptr && d < a.ncounts) a.counts_out[d] = c;
     unsigned long long x = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -120,7 +273,6 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
     if (d == 0) s_exec[p] = !trivial;
     __syncthreads();
   }
-  if (d < MAX_PASSES) ctl->tile_counter[d] = first_tile;
   if (d != 0) return;
 
   int m = 0;
@@ -142,7 +294,7 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
       void* kdst = slot_final ? a.kfinal : a.kother;
       uint32_t* vdst = slot_final ? a.vfinal : a.vother;
       uint32_t f = PD_EXEC;
-      if (i == 1) f |= PD_XF_IN;
+      if (i == 1) f |= PD_XF_IN | PD_FIRST;
       if (i == 1 && a.has_vals && a.vin == nullptr) f |= PD_SYNTH_IDX;
       if (i == m) f |= PD_XF_OUT;
       if (a.write_keys || i < m) f |= PD_WRITE_KEYS;
@@ -193,58 +345,157 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
 }
 
 // --------------------------------------------------------------------------
-// One stable LSD pass over digit `pass` (bits 8*pass .. 8*pass+7).
-//
-// Tile = BLOCK*IPT keys; warp w owns the contiguous segment
-// [w*32*IPT, (w+1)*32*IPT) and holds item k of lane l at k*32 + l, so ranking
-// items in (k, lane) order IS input order -> the pass is stable, which argsort
-// and pairs need (the reference's atomic MSD scatter was not:
-// shaders/sort.metal:267-283).
-//
-//   1. tile id from an atomic counter (so every tile we wait on is running)
-//   2. coalesced load (+ forward transform on the first executed pass;
-//      + index synthesis for argsort)
-//   3. warp multisplit rank: __match_any_sync groups equal digits; the
-//      highest lane of each group bumps the warp's shared counter
-//   4. per digit: warp prefix, tile count, publish AGGREGATE, exclusive scan
-//   5. decoupled lookback over earlier tiles' status words (bounded wait)
-//   6. stage keys (and payload) in shared memory in digit order
-//   7. coalesced scatter: consecutive staged keys of one digit go to
-//      consecutive global positions (+ inverse transform on the last pass)
+// Count: per-slice histogram of this pass's digit over the pass input (which
+// holds ordered keys: only the first executed pass transforms, and its counts
+// come from k_upfront_hist).
 // --------------------------------------------------------------------------
-template <typename K, bool VALS, int BLOCK, int IPT>
-struct OnesweepCfg {
+template <typename K, int BLOCK>
+__global__ void __launch_bounds__(BLOCK)
+    k_count(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
+            uint32_t* __restrict__ counts /* [count][RADIX] */) {
+  const uint32_t flags = ctl->pass[pass].flags;
+  if (!(flags & PD_EXEC) || (flags & PD_FIRST)) return;
+  const K* keys = static_cast<const K*>(ctl->pass[pass].kin);
+  __shared__ uint32_t h[1][RADIX];
+  for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[0][i] = 0;
+  __syncthreads();
+  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
+  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+  const int shift = pass * RADIX_BITS;
+  // count the pass digit only: it becomes the lowest byte of a 32-bit word
+  auto f = [&](K x, bool valid) { warp_count_digits<uint32_t, 1>(h, (uint32_t)(x >> shift) & 0xffu, valid); };
+  if ((reinterpret_cast<uintptr_t>(keys) & 15) == 0)
+    for_each_key<K, BLOCK, true>(keys, lo, hi, f);
+  else
+    for_each_key<K, BLOCK, false>(keys, lo, hi, f);
+  __syncthreads();
+  for (int b = threadIdx.x; b < RADIX; b += BLOCK) counts[(size_t)blockIdx.x * RADIX + b] = h[0][b];
+}
+
+// --------------------------------------------------------------------------
+// Slice scan: offsets[c][d] = base[pass][d] + sum of counts[c'][d], c' < c
+// (mod 2^32: positions are < 2^32).  One thread per digit.
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(RADIX)
+    k_slice_scan(SortCtl* __restrict__ ctl, const int pass, const int passes, const Slices sl,
+                 const uint32_t* __restrict__ slice_hist, const uint32_t* __restrict__ counts,
+                 uint32_t* __restrict__ offsets) {
+  const uint32_t flags = ctl->pass[pass].flags;
+  if (!(flags & PD_EXEC)) return;
+  const int d = threadIdx.x;
+  const bool first = (flags & PD_FIRST) != 0;
+  const uint32_t* src = first ? slice_hist + (size_t)pass * RADIX : counts;
+  const size_t stride = first ? (size_t)passes * RADIX : RADIX;
+  uint32_t run = (uint32_t)ctl->base[pass][d];
+  uint32_t c = 0;
+  for (; c + 8 <= sl.count; c += 8) {
+    uint32_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = src[(size_t)(c + u) * stride + d];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      offsets[(size_t)(c + u) * RADIX + d] = run;
+      run += v[u];
+    }
+  }
+  for (; c < sl.count; ++c) {
+    const uint32_t v = src[(size_t)c * stride + d];
+    offsets[(size_t)c * RADIX + d] = run;
+    run += v;
+  }
+}
+
+// --------------------------------------------------------------------------
+// Scatter: CTA c sorts slice c's keys into their pass-output positions, one
+// tile of BLOCK*IPT keys at a time, keeping a running output offset per digit.
+//
+// Tile layout: warp w owns the contiguous segment [w*32*IPT, (w+1)*32*IPT)
+// and holds item k of lane l at k*32 + l, so ranking items in (k, lane) order
+// IS input order -> the pass is stable, which argsort and pairs need (the
+// reference's atomic MSD scatter was not: shaders/sort.metal:267-283).
+//
+//   A. keys -> registers from the bulk-copied shared-memory slot (plain loads
+//      for the partial last tile and unaligned inputs); forward transform on
+//      the first executed pass
+//   B. warp multisplit rank: the lanes sharing a digit (eight ballots) read
+//      the warp's running count for it, the group's highest lane advances
+//      it; rank = count + lanes below in the group
+//   C. per digit: warp bases, tile-local start, output offset = running
+//      offset - start; running offset += tile count
+//   D. stage: key (and payload) written to its slot in the digit-sorted tile
+//   E. coalesced scatter: consecutive staged keys of one digit go to
+//      consecutive output positions (+ inverse transform on the last pass)
+// --------------------------------------------------------------------------
+
+// Lanes of the warp holding the same 8-bit digit as this lane (invalid lanes
+// of a partial tile match nobody but themselves).  Eight ballots over the
+// digit's bits measured 2x faster on B200 than the hardware match
+// instruction at 16 keys per thread (FS_RANK_BALLOT=0 selects
+// __match_any_sync).
+template <bool FULL>
+__device__ __forceinline__ uint32_t warp_peers(uint32_t d, bool valid) {
+#if FS_RANK_BALLOT
+  uint32_t peers = FULL ? 0xffffffffu : __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+  for (int b = 0; b < RADIX_BITS; ++b) {
+    const bool bit = (d >> b) & 1u;
+    const uint32_t bal = __ballot_sync(0xffffffffu, bit);
+    peers &= bit ? bal : ~bal;
+  }
+  return valid ? peers : (1u << (threadIdx.x & 31));
+#else
+  return __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
+#endif
+}
+
+template <typename K, bool VALS, int BLOCK, int IPT, bool STAGE_DIG>
+struct ScatterLayout {
   static constexpr int WARPS = BLOCK / 32;
   static constexpr int TILE = BLOCK * IPT;
   static constexpr int SEG = 32 * IPT;
-  static constexpr size_t STAGE_BYTES = (size_t)TILE * sizeof(K) + (VALS ? (size_t)TILE * 4 : 0);
-  static constexpr size_t HIST_BYTES = (size_t)WARPS * RADIX * 4;
-  static constexpr size_t DYN_SMEM = STAGE_BYTES > HIST_BYTES ? STAGE_BYTES : HIST_BYTES;
+  static constexpr size_t KEYS = (size_t)TILE * sizeof(K);
+  static constexpr size_t VALB = VALS ? (size_t)TILE * 4 : 0;
+  static constexpr size_t SLOT = KEYS + VALB;  // one bulk-copy slot (keys | vals)
+  // dynamic shared memory:
+  //   [slot 0 | slot 1 | stage keys | stage vals | warp digit counters | staged digits]
+  static constexpr size_t STAGE_OFF = 2 * SLOT;
+  static constexpr size_t CNT_OFF = STAGE_OFF + KEYS + VALB;
+  static constexpr size_t DIG_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;
+  static constexpr size_t BYTES = DIG_OFF + (STAGE_DIG ? (size_t)TILE : 0);
   static_assert(BLOCK >= RADIX && BLOCK % 32 == 0, "one thread per digit needed");
+  static_assert(KEYS % 16 == 0, "bulk copies move multiples of 16 bytes");
 };
 
-template <typename K, bool VALS, int XF, int BLOCK, int IPT, bool FULL>
-__device__ __forceinline__ bool onesweep_tile(
-    const uint32_t tile, const uint32_t tile_n, const uint64_t n, const int pass, const uint32_t flags,
-    const K* __restrict__ kin, K* __restrict__ kout, const uint32_t* __restrict__ vin,
-    uint32_t* __restrict__ vout, SortCtl* __restrict__ ctl, uint64_t* __restrict__ status,
-    const uint32_t epoch, const uint64_t timeout_ns, uint32_t* whist, K* skeys, uint32_t* svals,
-    uint32_t* s_start, uint32_t* s_off, uint32_t* s_wsum, int* s_abort) {
-  using C = OnesweepCfg<K, VALS, BLOCK, IPT>;
+template <typename K, bool VALS, int XF, int BLOCK, int IPT, bool FULL, bool FROM_SLOT, typename D>
+__device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_t tile_n, const uint64_t n,
+                                             const uint32_t flags, const K* __restrict__ kin,
+                                             K* __restrict__ kout, const uint32_t* __restrict__ vin,
+                                             uint32_t* __restrict__ vout, const unsigned char* slot,
+                                             unsigned char* dsm, uint32_t* s_run, uint32_t* s_off,
+                                             uint32_t* s_wsum, SortCtl* __restrict__ ctl, const D& dfn,
+                                             const uint64_t gpos_base) {
+  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE>;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t lt_mask = (1u << lane) - 1u;
-  const int shift = pass * RADIX_BITS;
-  const uint64_t tbase = (uint64_t)tile * C::TILE;
-  const uint32_t wofs = warp * C::SEG + lane;
+  const uint64_t gbase = gpos_base + tbase;
+  const uint32_t wofs = warp * Ly::SEG + lane;
+  const K* slot_keys = reinterpret_cast<const K*>(slot);
+  const uint32_t* slot_vals = reinterpret_cast<const uint32_t*>(slot + Ly::KEYS);
+  K* skeys = reinterpret_cast<K*>(dsm + Ly::STAGE_OFF);
+  uint32_t* svals = reinterpret_cast<uint32_t*>(dsm + Ly::STAGE_OFF + Ly::KEYS);
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF);
+  uint8_t* sdig = dsm + Ly::DIG_OFF;
+  uint32_t* wcnt = cnt + warp * RADIX;
 
-  // ---- 2. load -------------------------------------------------------------
+  // ---- A. keys -> registers ----------------------------------------------------
   K key[IPT];
-  uint32_t val[VALS ? IPT : 1];
-  uint32_t rk[IPT];
 #pragma unroll
   for (int k = 0; k < IPT; ++k) {
     const uint32_t li = wofs + k * 32;
-    key[k] = (FULL || li < tile_n) ? kin[tbase + li] : K(0);
+    if constexpr (FROM_SLOT)
+      key[k] = slot_keys[li];
+    else
+      key[k] = (FULL || li < tile_n) ? kin[tbase + li] : K(0);
   }
   if constexpr (XF != XF_NONE) {
     if (flags & PD_XF_IN) {
@@ -252,48 +503,37 @@ __device__ __forceinline__ bool onesweep_tile(
       for (int k = 0; k < IPT; ++k) key[k] = to_ordered<K, XF>(key[k]);
     }
   }
-  if constexpr (VALS) {
-    if (flags & PD_SYNTH_IDX) {
-#pragma unroll
-      for (int k = 0; k < IPT; ++k) val[k] = (uint32_t)(tbase + wofs + k * 32);
-    } else {
-#pragma unroll
-      for (int k = 0; k < IPT; ++k) {
-        const uint32_t li = wofs + k * 32;
-        val[k] = (FULL || li < tile_n) ? vin[tbase + li] : 0u;
-      }
-    }
-  }
 
-  // ---- 3. warp multisplit rank --------------------------------------------
-  uint32_t* wh = whist + warp * RADIX;
+  // ---- B. warp-local ranks -------------------------------------------------------
+  // Per key: the lanes sharing its digit; all read the warp's running count
+  // for that digit, the group's highest lane advances it.  After the loop
+  // the counters hold the warp's per-digit totals.
+  uint32_t rank[IPT];
 #pragma unroll
   for (int k = 0; k < IPT; ++k) {
     const bool valid = FULL || (wofs + k * 32) < tile_n;
-    const uint32_t d = digit_of(key[k], shift);
-    const uint32_t peers = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
+    const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
+    const uint32_t peers = warp_peers<FULL>(d, valid);
     uint32_t old = 0;
-    if (valid) old = wh[d];
+    if (valid) old = wcnt[d];
     __syncwarp();
-    if (valid && lane == 31u - __clz(peers)) wh[d] = old + __popc(peers);
+    if (valid && lane == 31u - __clz(peers)) wcnt[d] = old + __popc(peers);
     __syncwarp();
-    rk[k] = old + __popc(peers & lt_mask);
+    rank[k] = old + __popc(peers & lt_mask);
   }
   __syncthreads();
 
-  // ---- 4. per-digit totals, warp prefixes, publish aggregate, scan ----------
-  uint32_t cnt = 0;
+  // ---- C. per-digit bases and output offsets ------------------------------------
+  uint32_t tot = 0;
   if (tid < RADIX) {
 #pragma unroll
-    for (int w = 0; w < C::WARPS; ++w) {
-      const uint32_t c = whist[w * RADIX + tid];
-      whist[w * RADIX + tid] = cnt;
-      cnt += c;
+    for (int w = 0; w < Ly::WARPS; ++w) {
+      const uint32_t c = cnt[w * RADIX + tid];
+      cnt[w * RADIX + tid] = tot;
+      tot += c;
     }
-    st_relaxed_u64(status + (uint64_t)tile * RADIX + tid,
-                   st_pack(epoch, tile ? ST_AGGREGATE : ST_INCLUSIVE, cnt));
   }
-  uint32_t x = cnt;
+  uint32_t x = tot;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
@@ -301,78 +541,60 @@ __device__ __forceinline__ bool onesweep_tile(
   }
   if (lane == 31 && tid < RADIX) s_wsum[warp] = x;
   __syncthreads();
-
-  // ---- 5. decoupled lookback (one thread per digit) ------------------------
   if (tid < RADIX) {
-    uint32_t pre = 0;
-    for (uint32_t w = 0; w < warp; ++w) pre += s_wsum[w];
-    const uint32_t start = pre + x - cnt;
-    s_start[tid] = start;
-    uint64_t excl = 0;
-    bool ok = true;
-    if (tile > 0) {
-      const uint64_t* sp = status + (uint64_t)(tile - 1) * RADIX + tid;
-      const uint32_t ep = epoch & ST_EPOCH_MASK;
-      uint64_t t0 = 0;
-      for (;;) {
-        const uint64_t w = ld_relaxed_u64(sp);
-        const uint32_t f = st_flag(w);
-        if (f != ST_NOT_READY && st_epoch(w) == ep) {
-          excl += st_value(w);
-          if (f == ST_INCLUSIVE) break;
-          sp -= RADIX;  // tile 0 always publishes INCLUSIVE, so this stops
-        } else {
-          const uint64_t now = global_timer_ns();
-          if (t0 == 0) {
-            t0 = now;
-          } else if (now - t0 > timeout_ns || ld_relaxed_s32(&ctl->err) != 0) {
-            if (atomicCAS(&ctl->err, 0, DEV_ERR_TIMEOUT) == 0) ctl->err_tile = tile;
-            ok = false;
-            break;
-          }
-        }
+    uint32_t start = x - tot;
+    for (uint32_t w = 0; w < warp; ++w) start += s_wsum[w];
+#pragma unroll
+    for (int w = 0; w < Ly::WARPS; ++w) cnt[w * RADIX + tid] += start;
+    s_off[tid] = s_run[tid] - start;
+    s_run[tid] += tot;
+  }
+  __syncthreads();
+
+  // ---- D. stage in digit order -----------------------------------------------------
+  // cnt[w][d] now holds tile-local start of digit d + warp w's prefix
+  const bool synth = VALS && (flags & PD_SYNTH_IDX);
+#pragma unroll
+  for (int k = 0; k < IPT; ++k) {
+    const uint32_t li = wofs + k * 32;
+    if (FULL || li < tile_n) {
+      const uint32_t d = dfn(key[k], gbase + li);
+      const uint32_t pos = wcnt[d] + rank[k];
+      skeys[pos] = key[k];
+      if constexpr (VALS) {
+        uint32_t v;
+        if (synth)
+          v = (uint32_t)(tbase + li);
+        else if constexpr (FROM_SLOT)
+          v = slot_vals[li];
+        else
+          v = vin[tbase + li];
+        svals[pos] = v;
       }
-      if (ok)
-        st_relaxed_u64(status + (uint64_t)tile * RADIX + tid,
-                       st_pack(epoch, ST_INCLUSIVE, excl + cnt));
-    }
-    if (!ok) *s_abort = 1;
-    s_off[tid] = (uint32_t)(ctl->base[pass][tid] + excl) - start;
-  }
-  __syncthreads();
-  if (*s_abort) return false;
-
-  // ---- 6. stage in digit order ---------------------------------------------
-#pragma unroll
-  for (int k = 0; k < IPT; ++k) {
-    if (FULL || (wofs + k * 32) < tile_n) {
-      const uint32_t d = digit_of(key[k], shift);
-      rk[k] += s_start[d] + wh[d];
-    }
-  }
-  __syncthreads();  // whist and the staging area share memory
-#pragma unroll
-  for (int k = 0; k < IPT; ++k) {
-    if (FULL || (wofs + k * 32) < tile_n) {
-      skeys[rk[k]] = key[k];
-      if constexpr (VALS) svals[rk[k]] = val[k];
+      if constexpr (D::STAGE) sdig[pos] = (uint8_t)d;
     }
   }
   __syncthreads();
 
-  // ---- 7. coalesced scatter ------------------------------------------------
-  // Positions are checked against n: a wrong bucket offset records
-  // DEV_ERR_BOUNDS and drops the write instead of touching foreign memory.
+  // ---- E. coalesced scatter ---------------------------------------------------------
+  // Positions are checked against n: a wrong offset records DEV_ERR_BOUNDS
+  // and drops the write instead of touching foreign memory.
   const bool wkeys = (flags & PD_WRITE_KEYS) != 0;
   const bool xout = XF != XF_NONE && (flags & PD_XF_OUT);
+  const uint32_t last = (uint32_t)(n - 1);  // n <= 2^32: positions fit 32 bits
   bool oob = false;
 #pragma unroll
   for (int j = 0; j < IPT; ++j) {
     const uint32_t i = j * BLOCK + tid;
     if (FULL || i < tile_n) {
       const K kk = skeys[i];
-      const uint32_t pos = s_off[digit_of(kk, shift)] + i;
-      if ((uint64_t)pos < n) {
+      uint32_t d;
+      if constexpr (D::STAGE)
+        d = sdig[i];
+      else
+        d = dfn(kk, 0);
+      const uint32_t pos = s_off[d] + i;
+      if (pos <= last) {
         if (wkeys) kout[pos] = xout ? from_ordered<K, XF>(kk) : kk;
         if constexpr (VALS) vout[pos] = svals[i];
       } else {
@@ -381,52 +603,96 @@ __device__ __forceinline__ bool onesweep_tile(
     }
   }
   if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
-  __syncthreads();  // staging reads done before the next tile reuses smem
-  return true;
+  for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
+  __syncthreads();  // staging reads done, counters zeroed: next tile may start
 }
 
-template <typename K, bool VALS, int XF, int BLOCK, int IPT>
-__global__ void __launch_bounds__(BLOCK, FS_ONESWEEP_MIN_BLOCKS)
-    k_onesweep(SortCtl* __restrict__ ctl, const int pass, const uint64_t n,
-               const uint32_t num_tiles, uint64_t* __restrict__ status, const uint32_t epoch,
-               const uint64_t timeout_ns) {
-  using C = OnesweepCfg<K, VALS, BLOCK, IPT>;
-  extern __shared__ __align__(16) unsigned char dsm[];
-  uint32_t* whist = reinterpret_cast<uint32_t*>(dsm);
-  K* skeys = reinterpret_cast<K*>(dsm);
-  uint32_t* svals = reinterpret_cast<uint32_t*>(dsm + (size_t)C::TILE * sizeof(K));
-  __shared__ uint32_t s_start[RADIX];
+// One CTA per slice.  Tiles of the slice are processed in order; the next
+// tile's keys (and payload) are bulk-copied (cp.async.bulk global->shared, no
+// multicast) into the other of two slots while the current one is processed.
+// Every mbarrier wait is bounded; no CTA exits with a copy still in flight.
+template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, typename D>
+__global__ void __launch_bounds__(BLOCK, MINB)
+    k_scatter(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
+              const uint32_t* __restrict__ offsets, const uint64_t timeout_ns, const D dfn,
+              const uint64_t gpos_base) {
+  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE>;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  __shared__ uint32_t s_run[RADIX];
   __shared__ uint32_t s_off[RADIX];
-  __shared__ uint32_t s_wsum[C::WARPS];
-  __shared__ uint32_t s_tile;
+  __shared__ uint32_t s_wsum[Ly::WARPS];
+  __shared__ __align__(8) uint64_t s_bar[2];
   __shared__ int s_abort;
 
   const PassDesc pd = ctl->pass[pass];
   if (!(pd.flags & PD_EXEC)) return;
   const K* kin = static_cast<const K*>(pd.kin);
   K* kout = static_cast<K*>(pd.kout);
+  const bool copy_vals = VALS && !(pd.flags & PD_SYNTH_IDX);
+  const bool bulk_ok = (reinterpret_cast<uintptr_t>(kin) & 15) == 0 &&
+                       (!copy_vals || (reinterpret_cast<uintptr_t>(pd.vin) & 15) == 0);
+  const uint32_t tid = threadIdx.x;
+  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
+  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+  if (lo >= hi) return;
 
-  for (;;) {
-    if (threadIdx.x == 0) {
-      s_tile = atomicAdd(&ctl->tile_counter[pass], 1u);
-      s_abort = ld_relaxed_s32(&ctl->err);
+  // thread 0: start the copy of the tile at key `t0` into slot s (full tiles)
+  uint32_t armed = 0;  // thread 0: bit s = copy into slot s in flight
+  auto issue = [&](uint64_t t0, int s) {
+    if (bulk_ok && t0 + Ly::TILE <= hi) {
+      unsigned char* dst = dsm + (size_t)s * Ly::SLOT;
+      fence_proxy_async_smem();  // earlier generic reads of the slot precede the async write
+      mbar_arrive_expect_tx(&s_bar[s], (uint32_t)(Ly::KEYS + (copy_vals ? Ly::VALB : 0)));
+      bulk_g2s(dst, kin + t0, (uint32_t)Ly::KEYS, &s_bar[s]);
+      if (copy_vals) bulk_g2s(dst + Ly::KEYS, pd.vin + t0, (uint32_t)Ly::VALB, &s_bar[s]);
+      armed |= 1u << s;
     }
-    for (int i = threadIdx.x; i < C::WARPS * RADIX; i += BLOCK) whist[i] = 0;
-    __syncthreads();
-    const uint32_t tile = s_tile;
-    if (tile >= num_tiles || s_abort) return;
-    const uint64_t rem = n - (uint64_t)tile * C::TILE;
-    const uint32_t tile_n = rem < (uint64_t)C::TILE ? (uint32_t)rem : (uint32_t)C::TILE;
-    bool ok;
-    if (tile_n == (uint32_t)C::TILE)
-      ok = onesweep_tile<K, VALS, XF, BLOCK, IPT, true>(
-          tile, tile_n, n, pass, pd.flags, kin, kout, pd.vin, pd.vout, ctl, status, epoch,
-          timeout_ns, whist, skeys, svals, s_start, s_off, s_wsum, &s_abort);
+  };
+
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF);
+  for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
+  if (tid < RADIX) s_run[tid] = offsets[(size_t)blockIdx.x * RADIX + tid];
+  if (tid == 0) {
+    mbar_init(&s_bar[0], 1);
+    mbar_init(&s_bar[1], 1);
+    fence_mbar_init();
+    s_abort = 0;
+    issue(lo, 0);
+  }
+  __syncthreads();
+
+  uint32_t parity = 0;  // bit s: phase of slot s's barrier to wait for next
+  int s = 0;
+  for (uint64_t t0 = lo; t0 < hi; t0 += Ly::TILE, s ^= 1) {
+    const uint32_t tile_n = hi - t0 < (uint64_t)Ly::TILE ? (uint32_t)(hi - t0) : (uint32_t)Ly::TILE;
+    const bool full = tile_n == (uint32_t)Ly::TILE;
+    const bool from_slot = full && bulk_ok;
+    if (from_slot) {
+      if (!mbar_wait_bounded(&s_bar[s], (parity >> s) & 1u, timeout_ns, &ctl->err)) s_abort = 1;
+      parity ^= 1u << s;
+      if (tid == 0) armed &= ~(1u << s);
+    }
+    if (tid == 0) {
+      issue(t0 + Ly::TILE, s ^ 1);  // the other slot was consumed by the previous tile
+      if (ld_relaxed_s32(&ctl->err) != 0) s_abort = 1;
+    }
+    __syncthreads();  // one abort decision for the CTA
+    if (s_abort) break;
+    const unsigned char* slot = dsm + (size_t)s * Ly::SLOT;
+    if (from_slot)
+      scatter_tile<K, VALS, XF, BLOCK, IPT, true, true>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot,
+                                                       dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+    else if (full)
+      scatter_tile<K, VALS, XF, BLOCK, IPT, true, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+                                                        slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
     else
-      ok = onesweep_tile<K, VALS, XF, BLOCK, IPT, false>(
-          tile, tile_n, n, pass, pd.flags, kin, kout, pd.vin, pd.vout, ctl, status, epoch,
-          timeout_ns, whist, skeys, svals, s_start, s_off, s_wsum, &s_abort);
-    if (!ok) return;
+      scatter_tile<K, VALS, XF, BLOCK, IPT, false, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+                                                         slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+  }
+  // never leave a bulk copy into this CTA's shared memory in flight
+  if (tid == 0) {
+    for (int q = 0; q < 2; ++q)
+      if (armed & (1u << q)) mbar_wait_bounded(&s_bar[q], (parity >> q) & 1u, timeout_ns, &ctl->err);
   }
 }
 

@@ -23,8 +23,12 @@ struct fs_sorter {
   SortCtl* ctl = nullptr;
   int* host_err = nullptr;      // mapped pinned word written by k_finalize
   int* host_err_dev = nullptr;  // its device alias
-  uint64_t* status = nullptr;   // lookback status words, (tile, digit)
-  size_t status_bytes = 0;
+  void* slice_hist = nullptr;  // [slices][P][256] u32 from the upfront histogram
+  size_t slice_hist_bytes = 0;
+  void* counts = nullptr;      // [slices][256] u32 per-pass slice counts
+  size_t counts_bytes = 0;
+  void* offsets = nullptr;     // [slices][256] u32 per-pass output offsets
+  size_t offsets_bytes = 0;
   void* kother = nullptr;  // n keys of scratch (the OTHER slot)
   size_t kother_bytes = 0;
   void* kfinal2 = nullptr;  // argsort: keys are not an output, so FINAL is scratch too
@@ -35,10 +39,8 @@ struct fs_sorter {
   size_t dkeys_bytes = 0;
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
-  uint32_t epoch = 1;
   int sm_count = 0;
   uint64_t timeout_ns = 2000000000ull;
-  uint32_t first_tile = 0;
   int last_launches = 0;
   bool timing = false;  // fs_set_kernel_timing
   static constexpr int MAX_TIMED = 16;
@@ -81,19 +83,25 @@ int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
     if (e_ != cudaSuccess) return cuda_fail((s), e_, #call);   \
   } while (0)
 
-// Tile shapes.  32-bit keys: 256 threads x 16 keys; 64-bit keys likewise
-// (32 KiB of staged keys + 16 KiB of payload per tile).
-template <typename K> struct TileCfg;
-template <> struct TileCfg<uint32_t> {
-  static constexpr int BLOCK = 256;
-  static constexpr int IPT = 16;
+// Scatter tile shapes (threads x keys per thread) and resident CTAs per SM.
+// Shared memory per CTA = 2 bulk-copy slots + staging + 8 KiB of warp digit
+// counters: u32 keys 40+8 KiB (3 CTAs/SM), u32 pairs / u64 keys 96+8 KiB and
+// u64 pairs 72+8 KiB (2 CTAs/SM).
+template <typename K, bool VALS> struct TileCfg;
+template <> struct TileCfg<uint32_t, false> {
+  static constexpr int BLOCK = 256, IPT = 16, MINB = 3;
 };
-template <> struct TileCfg<uint64_t> {
-  static constexpr int BLOCK = 256;
-  static constexpr int IPT = 16;
+template <> struct TileCfg<uint32_t, true> {
+  static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
+};
+template <> struct TileCfg<uint64_t, false> {
+  static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
+};
+template <> struct TileCfg<uint64_t, true> {
+  static constexpr int BLOCK = 256, IPT = 8, MINB = 2;
 };
 
-constexpr int HIST_BLOCK = 256;
+constexpr int HIST_BLOCK = 512;  // histogram / count kernels: more loads in flight per SM
 
 int key_bytes_of(int dtype) { return dtype >= FS_U64 ? 8 : 4; }
 
@@ -152,59 +160,92 @@ int blocks_per_sm(fs_sorter* s, Kern k, int block, size_t smem) {
   return b > 0 ? b : 1;
 }
 
-template <typename K, bool VALS, int XF>
-int launch_pass(fs_sorter* s, int pass, uint64_t n, uint32_t tiles, uint32_t epoch) {
-  constexpr int B = TileCfg<K>::BLOCK, I = TileCfg<K>::IPT;
-  using C = OnesweepCfg<K, VALS, B, I>;
-  auto kern = k_onesweep<K, VALS, XF, B, I>;
-  static int configured_mask = 0;  // bit per device (attribute is per context)
+// Resident CTAs per SM of a scatter instantiation (cached per process; every
+// device here is the same architecture).
+template <typename K, bool VALS, int XF, typename D>
+int scatter_occupancy(fs_sorter* s) {
+  using T = TileCfg<K, VALS>;
+  using Ly = ScatterLayout<K, VALS, T::BLOCK, T::IPT, D::STAGE>;
+  auto kern = k_scatter<K, VALS, XF, T::BLOCK, T::IPT, T::MINB, D>;
+  static int configured_mask = 0;  // bit per device (the attribute is per context)
   static int bps = 0;
   if (!(configured_mask & (1 << (s->device & 31)))) {
-    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::DYN_SMEM));
-    bps = blocks_per_sm(s, kern, B, C::DYN_SMEM);
+    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES));
+    bps = blocks_per_sm(s, kern, T::BLOCK, Ly::BYTES);
     configured_mask |= 1 << (s->device & 31);
   }
+  return bps;
+}
+
+// Cut n keys into at most (resident scatter CTAs) contiguous slices of whole
+// tiles.
+template <typename K, bool VALS, int XF, typename D>
+int make_slices(fs_sorter* s, uint64_t n, Slices* sl) {
+  using T = TileCfg<K, VALS>;
+  constexpr uint64_t TILE = (uint64_t)T::BLOCK * T::IPT;
+  const int bps = scatter_occupancy<K, VALS, XF, D>(s);
+  if (bps < 0) return FS_E_GPU_EXECUTION;
+  const uint64_t tiles = (n + TILE - 1) / TILE;
   const uint64_t cap = (uint64_t)bps * s->sm_count;
-  const unsigned grid = (unsigned)(tiles < cap ? tiles : cap);
-  kern<<<grid, B, C::DYN_SMEM, s->stream>>>(s->ctl, pass, n, tiles, s->status, epoch, s->timeout_ns);
+  const uint64_t tps = (tiles + cap - 1) / cap;
+  sl->keys_per_slice = tps * TILE;
+  sl->count = (uint32_t)((tiles + tps - 1) / tps);
   return FS_OK;
+}
+
+template <typename K, bool VALS, int XF, typename D>
+void launch_scatter(fs_sorter* s, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
+  using T = TileCfg<K, VALS>;
+  using Ly = ScatterLayout<K, VALS, T::BLOCK, T::IPT, D::STAGE>;
+  k_scatter<K, VALS, XF, T::BLOCK, T::IPT, T::MINB, D><<<sl.count, T::BLOCK, Ly::BYTES, s->stream>>>(
+      s->ctl, pass, n, sl, static_cast<const uint32_t*>(s->offsets), s->timeout_ns, dfn, gpos_base);
+}
+
+int ensure_slice_buffers(fs_sorter* s, const Slices& sl, int passes) {
+  int rc = grow(s, &s->slice_hist, &s->slice_hist_bytes, (size_t)sl.count * passes * RADIX * 4, false);
+  if (!rc) rc = grow(s, &s->counts, &s->counts_bytes, (size_t)sl.count * RADIX * 4, false);
+  if (!rc) rc = grow(s, &s->offsets, &s->offsets_bytes, (size_t)sl.count * RADIX * 4, false);
+  return rc;
 }
 
 template <typename K, int XF>
 int enqueue_sort(fs_sorter* s, const PlanArgs& a) {
   constexpr int P = (int)sizeof(K);
-  constexpr int TILE = TileCfg<K>::BLOCK * TileCfg<K>::IPT;
   const uint64_t n = a.n;
-  const uint32_t tiles = (uint32_t)((n + TILE - 1) / TILE);
-  int rc = grow(s, (void**)&s->status, &s->status_bytes, (size_t)tiles * RADIX * sizeof(uint64_t), true);
+  Slices sl{};
+  int rc = a.has_vals ? make_slices<K, true, XF, RadixDigit>(s, n, &sl)
+                      : make_slices<K, false, XF, RadixDigit>(s, n, &sl);
   if (rc) return rc;
-  if (s->epoch + MAX_PASSES >= ST_EPOCH_MASK) {  // epoch wrap: forget all old words
-    FS_CUDA(s, cudaMemsetAsync(s->status, 0, s->status_bytes, s->stream));
-    s->epoch = 1;
-  }
-  const uint32_t epoch0 = s->epoch;
-  s->epoch += P;
-
-  // 1. histogram of every digit; enough CTAs for ~16 keys per thread, at most
-  //    8 per SM (each CTA flushes up to P*256 global atomics).
-  uint64_t hb = (n + (uint64_t)HIST_BLOCK * 16 - 1) / ((uint64_t)HIST_BLOCK * 16);
-  const uint64_t hcap = (uint64_t)s->sm_count * 8;
+  if ((rc = ensure_slice_buffers(s, sl, P))) return rc;
   s->ev_used = 0;
+  // 1. histograms of every digit (global + per slice)
   t_begin(s);
-  k_upfront_hist<K, XF, HIST_BLOCK><<<(unsigned)(hb < hcap ? hb : hcap), HIST_BLOCK, 0, s->stream>>>(
-      static_cast<const K*>(a.kin), n, s->ctl);
+  if ((reinterpret_cast<uintptr_t>(a.kin) & 15) == 0)
+    k_upfront_hist<K, XF, HIST_BLOCK, true><<<sl.count, HIST_BLOCK, 0, s->stream>>>(
+        static_cast<const K*>(a.kin), n, s->ctl, sl, static_cast<uint32_t*>(s->slice_hist));
+  else
+    k_upfront_hist<K, XF, HIST_BLOCK, false><<<sl.count, HIST_BLOCK, 0, s->stream>>>(
+        static_cast<const K*>(a.kin), n, s->ctl, sl, static_cast<uint32_t*>(s->slice_hist));
   t_end(s);
   // 2. plan
   t_begin(s);
-  k_plan<<<1, RADIX, 0, s->stream>>>(s->ctl, a, s->first_tile);
+  k_plan<<<1, RADIX, 0, s->stream>>>(s->ctl, a);
   t_end(s);
-  // 3. passes
+  // 3. passes: count (not for the first executed pass), slice scan, scatter
   for (int p = 0; p < P; ++p) {
     t_begin(s);
-    rc = a.has_vals ? launch_pass<K, true, XF>(s, p, n, tiles, epoch0 + p)
-                    : launch_pass<K, false, XF>(s, p, n, tiles, epoch0 + p);
+    k_count<K, HIST_BLOCK><<<sl.count, HIST_BLOCK, 0, s->stream>>>(s->ctl, p, n, sl,
+                                                                  static_cast<uint32_t*>(s->counts));
+    k_slice_scan<<<1, RADIX, 0, s->stream>>>(s->ctl, p, P, sl, static_cast<const uint32_t*>(s->slice_hist),
+                                            static_cast<const uint32_t*>(s->counts),
+                                            static_cast<uint32_t*>(s->offsets));
     t_end(s);
-    if (rc) return rc;
+    t_begin(s);
+    if (a.has_vals)
+      launch_scatter<K, true, XF>(s, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
+    else
+      launch_scatter<K, false, XF>(s, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
+    t_end(s);
   }
   // 4. finalize
   uint64_t fb = (n + 255) / 256;
@@ -212,7 +253,7 @@ int enqueue_sort(fs_sorter* s, const PlanArgs& a) {
   t_begin(s);
   k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, s->stream>>>(s->ctl, n, s->host_err_dev);
   t_end(s);
-  s->last_launches = P + 3;
+  s->last_launches = 3 + 3 * P;
   FS_CUDA(s, cudaGetLastError());
   return FS_OK;
 }
@@ -238,7 +279,7 @@ int finish(fs_sorter* s, int sync) {
     *(volatile int*)s->host_err = 0;
     if (he == DEV_ERR_BOUNDS)
       return fail(s, FS_E_GPU_EXECUTION, "scatter position out of range (histogram/offset inconsistency)");
-    return fail(s, FS_E_TIMEOUT, "lookback timeout: a tile waited longer than %llu ms for its predecessor",
+    return fail(s, FS_E_TIMEOUT, "device wait timeout: a bulk copy did not complete within %llu ms",
                 (unsigned long long)(s->timeout_ns / 1000000ull));
   }
   return FS_OK;
@@ -317,7 +358,7 @@ int fs_destroy(fs_sorter* s) {
   cudaSetDevice(s->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
   for (auto& kv : s->allocs) cudaFree(kv.first);
-  void* bufs[] = {s->status, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->ctl};
+  void* bufs[] = {s->slice_hist, s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->ctl};
   for (void* b : bufs)
     if (b) cudaFree(b);
   if (s->host_err) cudaFreeHost(s->host_err);
@@ -592,7 +633,7 @@ int fs_last_kernel_times(fs_sorter* s, float* ms, int cap) {
 
 uint64_t fs_scratch_bytes(const fs_sorter* s) {
   if (!s) return 0;
-  return s->status_bytes + s->kother_bytes + s->kfinal2_bytes + s->vother_bytes + s->dkeys_bytes +
+  return s->slice_hist_bytes + s->counts_bytes + s->offsets_bytes + s->kother_bytes + s->kfinal2_bytes + s->vother_bytes + s->dkeys_bytes +
          s->dvals_bytes + sizeof(SortCtl);
 }
 

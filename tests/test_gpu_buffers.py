@@ -114,7 +114,8 @@ def test_device_pointer_checks(sorter):
 def test_launch_count(sorter):
     x = orc.gen("u32", 100_000, seed=1)
     sorter.sort_u32(x.copy())
-    assert sorter.last_launch_count() == 4 + 3
+    # histogram, plan, (count, scan, scatter) per pass, finalize
+    assert sorter.last_launch_count() == 3 + 3 * 4
     y = orc.gen("u64", 100_000, seed=1)
     sorter.sort_u64(y.copy())
-    assert sorter.last_launch_count() == 8 + 3
+    assert sorter.last_launch_count() == 3 + 3 * 8
