@@ -43,7 +43,7 @@ struct fs_sorter {
   uint64_t timeout_ns = 2000000000ull;
   int last_launches = 0;
   bool timing = false;  // fs_set_kernel_timing
-  static constexpr int MAX_TIMED = 16;
+  static constexpr int MAX_TIMED = 24;
   cudaEvent_t ev[2 * MAX_TIMED] = {};
   int ev_used = 0;
   std::unordered_map<void*, size_t> allocs;  // fs_alloc'd pointers -> bytes
@@ -105,14 +105,6 @@ constexpr int HIST_BLOCK = 512;  // histogram / count kernels: more loads in fli
 
 int key_bytes_of(int dtype) { return dtype >= FS_U64 ? 8 : 4; }
 
-// Event pair around each launch when kernel timing is on.
-void t_begin(fs_sorter* s) {
-  if (s->timing && s->ev_used < fs_sorter::MAX_TIMED) cudaEventRecord(s->ev[2 * s->ev_used], s->stream);
-}
-void t_end(fs_sorter* s) {
-  if (s->timing && s->ev_used < fs_sorter::MAX_TIMED) cudaEventRecord(s->ev[2 * s->ev_used++ + 1], s->stream);
-}
-
 int grow(fs_sorter* s, void** p, size_t* cap, size_t need, bool zero) {
   if (*cap >= need) return FS_OK;
   if (*p) {
@@ -153,26 +145,59 @@ int prepare_ptr(fs_sorter* s, const void* p, size_t bytes, const char* what) {
   return FS_OK;
 }
 
+// Everything one enqueued sort needs: device and stream, the control block,
+// scratch buffers that are already large enough, and where k_finalize
+// reports device errors.  `s` (may be null) receives error text and owns the
+// kernel-timing events.
+struct Exec {
+  int device;
+  cudaStream_t stream;
+  int sm_count;
+  uint64_t timeout_ns;
+  SortCtl* ctl;
+  int* err_out;
+  uint32_t* slice_hist;  // >= slices * P * 256 words
+  uint32_t* counts;      // >= slices * 256 words
+  uint32_t* offsets;     // >= slices * 256 words
+  fs_sorter* s;
+};
+
+// Event pair around each launch when kernel timing is on.
+void t_begin(const Exec& e) {
+  fs_sorter* s = e.s;
+  if (s && s->timing && s->ev_used < fs_sorter::MAX_TIMED) cudaEventRecord(s->ev[2 * s->ev_used], e.stream);
+}
+void t_end(const Exec& e) {
+  fs_sorter* s = e.s;
+  if (s && s->timing && s->ev_used < fs_sorter::MAX_TIMED) cudaEventRecord(s->ev[2 * s->ev_used++ + 1], e.stream);
+}
+
+// Resident CTAs per SM, or -(fs_status) on failure.
 template <typename Kern>
 int blocks_per_sm(fs_sorter* s, Kern k, int block, size_t smem) {
   int b = 0;
-  FS_CUDA(s, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, block, smem));
+  const cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, block, smem);
+  if (err != cudaSuccess) return -cuda_fail(s, err, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
   return b > 0 ? b : 1;
 }
 
 // Resident CTAs per SM of a scatter instantiation (cached per process; every
-// device here is the same architecture).
+// device here is the same architecture).  Sets the kernel's shared-memory
+// limit on the current device the first time; allocates nothing.
 template <typename K, bool VALS, int XF, typename D>
-int scatter_occupancy(fs_sorter* s) {
+int scatter_occupancy(const Exec& e) {
   using T = TileCfg<K, VALS>;
   using Ly = ScatterLayout<K, VALS, T::BLOCK, T::IPT, D::STAGE>;
   auto kern = k_scatter<K, VALS, XF, T::BLOCK, T::IPT, T::MINB, D>;
   static int configured_mask = 0;  // bit per device (the attribute is per context)
   static int bps = 0;
-  if (!(configured_mask & (1 << (s->device & 31)))) {
-    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES));
-    bps = blocks_per_sm(s, kern, T::BLOCK, Ly::BYTES);
-    configured_mask |= 1 << (s->device & 31);
+  if (!(configured_mask & (1 << (e.device & 31)))) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES);
+    if (err != cudaSuccess) return -cuda_fail(e.s, err, "cudaFuncSetAttribute");
+    const int b = blocks_per_sm(e.s, kern, T::BLOCK, Ly::BYTES);
+    if (b < 0) return b;
+    bps = b;
+    configured_mask |= 1 << (e.device & 31);
   }
   return bps;
 }
@@ -180,13 +205,13 @@ int scatter_occupancy(fs_sorter* s) {
 // Cut n keys into at most (resident scatter CTAs) contiguous slices of whole
 // tiles.
 template <typename K, bool VALS, int XF, typename D>
-int make_slices(fs_sorter* s, uint64_t n, Slices* sl) {
+int make_slices(const Exec& e, uint64_t n, Slices* sl) {
   using T = TileCfg<K, VALS>;
   constexpr uint64_t TILE = (uint64_t)T::BLOCK * T::IPT;
-  const int bps = scatter_occupancy<K, VALS, XF, D>(s);
-  if (bps < 0) return FS_E_GPU_EXECUTION;
+  const int bps = scatter_occupancy<K, VALS, XF, D>(e);
+  if (bps < 0) return -bps;
   const uint64_t tiles = (n + TILE - 1) / TILE;
-  const uint64_t cap = (uint64_t)bps * s->sm_count;
+  const uint64_t cap = (uint64_t)bps * e.sm_count;
   const uint64_t tps = (tiles + cap - 1) / cap;
   sl->keys_per_slice = tps * TILE;
   sl->count = (uint32_t)((tiles + tps - 1) / tps);
@@ -194,11 +219,83 @@ int make_slices(fs_sorter* s, uint64_t n, Slices* sl) {
 }
 
 template <typename K, bool VALS, int XF, typename D>
-void launch_scatter(fs_sorter* s, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
+void launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
   using T = TileCfg<K, VALS>;
   using Ly = ScatterLayout<K, VALS, T::BLOCK, T::IPT, D::STAGE>;
-  k_scatter<K, VALS, XF, T::BLOCK, T::IPT, T::MINB, D><<<sl.count, T::BLOCK, Ly::BYTES, s->stream>>>(
-      s->ctl, pass, n, sl, static_cast<const uint32_t*>(s->offsets), s->timeout_ns, dfn, gpos_base);
+  k_scatter<K, VALS, XF, T::BLOCK, T::IPT, T::MINB, D><<<sl.count, T::BLOCK, Ly::BYTES, e.stream>>>(
+      e.ctl, pass, n, sl, e.offsets, e.timeout_ns, dfn, gpos_base);
+}
+
+template <typename K, int XF>
+int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launches) {
+  constexpr int P = (int)sizeof(K);
+  const uint64_t n = a.n;
+  if (e.s) e.s->ev_used = 0;
+  // 1. histograms of every digit (global + per slice)
+  t_begin(e);
+  if ((reinterpret_cast<uintptr_t>(a.kin) & 15) == 0)
+    k_upfront_hist<K, XF, HIST_BLOCK, true>
+        <<<sl.count, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
+  else
+    k_upfront_hist<K, XF, HIST_BLOCK, false>
+        <<<sl.count, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
+  t_end(e);
+  // 2. plan
+  t_begin(e);
+  k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
+  t_end(e);
+  // 3. passes: count (not for the first executed pass), slice scan, scatter
+  for (int p = 0; p < P; ++p) {
+    t_begin(e);
+    k_count<K, HIST_BLOCK><<<sl.count, HIST_BLOCK, 0, e.stream>>>(e.ctl, p, n, sl, e.counts);
+    k_slice_scan<<<1, RADIX, 0, e.stream>>>(e.ctl, p, P, sl, e.slice_hist, e.counts, e.offsets);
+    t_end(e);
+    t_begin(e);
+    if (a.has_vals)
+      launch_scatter<K, true, XF>(e, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
+    else
+      launch_scatter<K, false, XF>(e, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
+    t_end(e);
+  }
+  // 4. finalize
+  uint64_t fb = (n + 255) / 256;
+  const uint64_t fcap = (uint64_t)e.sm_count * 4;
+  t_begin(e);
+  k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, e.stream>>>(e.ctl, n, e.err_out);
+  t_end(e);
+  if (launches) *launches = 3 + 3 * P;
+  FS_CUDA(e.s, cudaGetLastError());
+  return FS_OK;
+}
+
+// Slice geometry for (dtype, n, payload).
+int dispatch_slices(const Exec& e, int dtype, uint64_t n, bool vals, Slices* sl) {
+  const bool w = dtype >= FS_U64;
+  const int xf = dtype % 3;
+  if (!w && !vals) return xf == 0 ? make_slices<uint32_t, false, XF_NONE, RadixDigit>(e, n, sl)
+                                  : xf == 1 ? make_slices<uint32_t, false, XF_SIGN, RadixDigit>(e, n, sl)
+                                            : make_slices<uint32_t, false, XF_FLOAT, RadixDigit>(e, n, sl);
+  if (!w && vals) return xf == 0 ? make_slices<uint32_t, true, XF_NONE, RadixDigit>(e, n, sl)
+                                 : xf == 1 ? make_slices<uint32_t, true, XF_SIGN, RadixDigit>(e, n, sl)
+                                           : make_slices<uint32_t, true, XF_FLOAT, RadixDigit>(e, n, sl);
+  if (w && !vals) return xf == 0 ? make_slices<uint64_t, false, XF_NONE, RadixDigit>(e, n, sl)
+                                 : xf == 1 ? make_slices<uint64_t, false, XF_SIGN, RadixDigit>(e, n, sl)
+                                           : make_slices<uint64_t, false, XF_FLOAT, RadixDigit>(e, n, sl);
+  return xf == 0 ? make_slices<uint64_t, true, XF_NONE, RadixDigit>(e, n, sl)
+                 : xf == 1 ? make_slices<uint64_t, true, XF_SIGN, RadixDigit>(e, n, sl)
+                           : make_slices<uint64_t, true, XF_FLOAT, RadixDigit>(e, n, sl);
+}
+
+int dispatch_enqueue(const Exec& e, int dtype, const PlanArgs& a, const Slices& sl, int* launches) {
+  switch (dtype) {
+    case FS_U32: return enqueue_sort<uint32_t, XF_NONE>(e, a, sl, launches);
+    case FS_I32: return enqueue_sort<uint32_t, XF_SIGN>(e, a, sl, launches);
+    case FS_F32: return enqueue_sort<uint32_t, XF_FLOAT>(e, a, sl, launches);
+    case FS_U64: return enqueue_sort<uint64_t, XF_NONE>(e, a, sl, launches);
+    case FS_I64: return enqueue_sort<uint64_t, XF_SIGN>(e, a, sl, launches);
+    case FS_F64: return enqueue_sort<uint64_t, XF_FLOAT>(e, a, sl, launches);
+    default: return fail(e.s, FS_E_INVALID, "unknown dtype %d", dtype);
+  }
 }
 
 int ensure_slice_buffers(fs_sorter* s, const Slices& sl, int passes) {
@@ -208,66 +305,29 @@ int ensure_slice_buffers(fs_sorter* s, const Slices& sl, int passes) {
   return rc;
 }
 
-template <typename K, int XF>
-int enqueue_sort(fs_sorter* s, const PlanArgs& a) {
-  constexpr int P = (int)sizeof(K);
-  const uint64_t n = a.n;
-  Slices sl{};
-  int rc = a.has_vals ? make_slices<K, true, XF, RadixDigit>(s, n, &sl)
-                      : make_slices<K, false, XF, RadixDigit>(s, n, &sl);
-  if (rc) return rc;
-  if ((rc = ensure_slice_buffers(s, sl, P))) return rc;
-  s->ev_used = 0;
-  // 1. histograms of every digit (global + per slice)
-  t_begin(s);
-  if ((reinterpret_cast<uintptr_t>(a.kin) & 15) == 0)
-    k_upfront_hist<K, XF, HIST_BLOCK, true><<<sl.count, HIST_BLOCK, 0, s->stream>>>(
-        static_cast<const K*>(a.kin), n, s->ctl, sl, static_cast<uint32_t*>(s->slice_hist));
-  else
-    k_upfront_hist<K, XF, HIST_BLOCK, false><<<sl.count, HIST_BLOCK, 0, s->stream>>>(
-        static_cast<const K*>(a.kin), n, s->ctl, sl, static_cast<uint32_t*>(s->slice_hist));
-  t_end(s);
-  // 2. plan
-  t_begin(s);
-  k_plan<<<1, RADIX, 0, s->stream>>>(s->ctl, a);
-  t_end(s);
-  // 3. passes: count (not for the first executed pass), slice scan, scatter
-  for (int p = 0; p < P; ++p) {
-    t_begin(s);
-    k_count<K, HIST_BLOCK><<<sl.count, HIST_BLOCK, 0, s->stream>>>(s->ctl, p, n, sl,
-                                                                  static_cast<uint32_t*>(s->counts));
-    k_slice_scan<<<1, RADIX, 0, s->stream>>>(s->ctl, p, P, sl, static_cast<const uint32_t*>(s->slice_hist),
-                                            static_cast<const uint32_t*>(s->counts),
-                                            static_cast<uint32_t*>(s->offsets));
-    t_end(s);
-    t_begin(s);
-    if (a.has_vals)
-      launch_scatter<K, true, XF>(s, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
-    else
-      launch_scatter<K, false, XF>(s, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
-    t_end(s);
-  }
-  // 4. finalize
-  uint64_t fb = (n + 255) / 256;
-  const uint64_t fcap = (uint64_t)s->sm_count * 4;
-  t_begin(s);
-  k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, s->stream>>>(s->ctl, n, s->host_err_dev);
-  t_end(s);
-  s->last_launches = 3 + 3 * P;
-  FS_CUDA(s, cudaGetLastError());
-  return FS_OK;
+Exec exec_of(fs_sorter* s) {
+  Exec e{};
+  e.device = s->device;
+  e.stream = s->stream;
+  e.sm_count = s->sm_count;
+  e.timeout_ns = s->timeout_ns;
+  e.ctl = s->ctl;
+  e.err_out = s->host_err_dev;
+  e.s = s;
+  return e;
 }
 
+// The sorter's path: size the slices, grow its scratch, enqueue.
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
-  switch (dtype) {
-    case FS_U32: return enqueue_sort<uint32_t, XF_NONE>(s, a);
-    case FS_I32: return enqueue_sort<uint32_t, XF_SIGN>(s, a);
-    case FS_F32: return enqueue_sort<uint32_t, XF_FLOAT>(s, a);
-    case FS_U64: return enqueue_sort<uint64_t, XF_NONE>(s, a);
-    case FS_I64: return enqueue_sort<uint64_t, XF_SIGN>(s, a);
-    case FS_F64: return enqueue_sort<uint64_t, XF_FLOAT>(s, a);
-    default: return fail(s, FS_E_INVALID, "unknown dtype %d", dtype);
-  }
+  Exec e = exec_of(s);
+  Slices sl{};
+  int rc = dispatch_slices(e, dtype, a.n, a.has_vals != 0, &sl);
+  if (rc) return rc;
+  if ((rc = ensure_slice_buffers(s, sl, a.passes))) return rc;
+  e.slice_hist = static_cast<uint32_t*>(s->slice_hist);
+  e.counts = static_cast<uint32_t*>(s->counts);
+  e.offsets = static_cast<uint32_t*>(s->offsets);
+  return dispatch_enqueue(e, dtype, a, sl, &s->last_launches);
 }
 
 int finish(fs_sorter* s, int sync) {

@@ -70,13 +70,15 @@ int fs_create(int device, void* stream, fs_sorter** out);
 int fs_destroy(fs_sorter* s);
 
 /* Text of the last failure on `s` (never NULL; "" when none).  With s == NULL,
- * the text of the last fs_create failure on this thread. */
+ * the text of the last failure on this thread of a call that has no sorter
+ * (fs_create). */
 const char* fs_last_error(const fs_sorter* s);
 
 /* Replace the stream the sorter enqueues on (NULL = its private stream). */
 int fs_set_stream(fs_sorter* s, void* stream);
 /* Wait for all work enqueued by `s`, then report any device-side failure
- * (lookback timeout) that an asynchronous call left behind. */
+ * (a bounded wait that ran out, an out-of-range scatter) that an
+ * asynchronous call left behind. */
 int fs_synchronize(fs_sorter* s);
 
 /* ---- memory (SortBuffer backing) --------------------------------------- */
@@ -144,9 +146,10 @@ int fs_host_sort_keys_copy(fs_sorter* s, int dtype, const void* host_in,
  * on its own stream (the forge-primitives GpuTimer analogue,
  * forge-primitives/src/timing.rs:9-47).  Off by default. */
 int fs_set_kernel_timing(fs_sorter* s, int on);
-/* After a synchronous sort with timing on: write up to `cap` kernel
- * durations in ms (launch order: histogram, plan, pass 0..P-1, finalize) and
- * return how many were written (negative fs_status on failure). */
+/* After a synchronous sort with timing on: write up to `cap` durations in ms
+ * and return how many were written (negative fs_status on failure).  Order:
+ * histogram, plan, then per digit pass (count + slice scan, scatter), then
+ * finalize -- 3 + 2*P entries for P = key bytes. */
 int fs_last_kernel_times(fs_sorter* s, float* ms, int cap);
 
 /* ---- introspection ------------------------------------------------------- */
