@@ -357,6 +357,42 @@ int set_device(fs_sorter* s) {
   return FS_OK;
 }
 
+// ---- allocation-free sorting ------------------------------------------------
+// Scratch for fs_sort_keys_noalloc lives in one file-scope device array sized
+// for NA_MAX_KEY_BYTES of keys.  Every device that loads this library holds it
+// until the process exits.  Carved as:
+//   [other-key buffer | slice histograms | slice counts | slice offsets |
+//    control block | error word]
+constexpr uint64_t NA_MAX_KEY_BYTES = 4ull << 20;  // 2^20 u32/i32/f32 or 2^19 u64/i64/f64 keys
+constexpr uint32_t NA_MAX_SLICES = 256;            // >= tiles of the largest allowed sort
+constexpr size_t NA_OFF_KEYS = 0;
+constexpr size_t NA_OFF_HIST = NA_OFF_KEYS + NA_MAX_KEY_BYTES;
+constexpr size_t NA_OFF_COUNTS = NA_OFF_HIST + (size_t)NA_MAX_SLICES * MAX_PASSES * RADIX * 4;
+constexpr size_t NA_OFF_OFFSETS = NA_OFF_COUNTS + (size_t)NA_MAX_SLICES * RADIX * 4;
+constexpr size_t NA_OFF_CTL = NA_OFF_OFFSETS + (size_t)NA_MAX_SLICES * RADIX * 4;
+constexpr size_t NA_OFF_ERR = NA_OFF_CTL + ((sizeof(SortCtl) + 255) / 256) * 256;
+constexpr size_t NA_BYTES = NA_OFF_ERR + 256;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
+
+// Device address of g_noalloc_scratch per device.  In host code the array's
+// name is only a host-side stand-in: kernels must be given this address.
+unsigned char* g_na_base[64] = {};
+std::mutex g_na_mu;
+
+int noalloc_base(int device, unsigned char** out) {
+  if (device < 0 || device >= 64) return fail(nullptr, FS_E_INVALID, "device %d out of range", device);
+  std::lock_guard<std::mutex> lk(g_na_mu);
+  if (!g_na_base[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // with `device` current
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_na_base[device] = static_cast<unsigned char*>(p);
+  }
+  *out = g_na_base[device];
+  return FS_OK;
+}
+
 }  // namespace
 
 // ============================================================================
@@ -689,6 +725,67 @@ int fs_last_kernel_times(fs_sorter* s, float* ms, int cap) {
       return -cuda_fail(s, cudaGetLastError(), "cudaEventElapsedTime");
   }
   return k;
+}
+
+int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream) {
+  if (dtype < FS_U32 || dtype > FS_F64) return fail(nullptr, FS_E_INVALID, "unknown dtype %d", dtype);
+  const int kb = key_bytes_of(dtype);
+  if (n * (uint64_t)kb > NA_MAX_KEY_BYTES)
+    return fail(nullptr, FS_E_INVALID,
+                "n = %llu keys exceeds the allocation-free limit of %llu bytes of keys (%llu keys of %d bytes)",
+                (unsigned long long)n, (unsigned long long)NA_MAX_KEY_BYTES,
+                (unsigned long long)(NA_MAX_KEY_BYTES / kb), kb);
+  if (n <= 1) return FS_OK;
+  if (!keys) return fail(nullptr, FS_E_INVALID, "keys is NULL");
+  int device = 0;
+  cudaError_t ce = cudaGetDevice(&device);
+  if (ce != cudaSuccess) return cuda_fail(nullptr, ce, "cudaGetDevice");
+  cudaPointerAttributes at{};
+  ce = cudaPointerGetAttributes(&at, keys);
+  if (ce != cudaSuccess || at.type != cudaMemoryTypeDevice || at.device != device) {
+    cudaGetLastError();
+    return fail(nullptr, FS_E_INVALID, "keys must be device memory of the current device %d", device);
+  }
+  unsigned char* base = nullptr;
+  int rc = noalloc_base(device, &base);
+  if (rc) return rc;
+  Exec e{};
+  e.device = device;
+  e.stream = static_cast<cudaStream_t>(stream);
+  ce = cudaDeviceGetAttribute(&e.sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (ce != cudaSuccess) return cuda_fail(nullptr, ce, "cudaDeviceGetAttribute");
+  e.timeout_ns = 2000000000ull;
+  e.ctl = reinterpret_cast<SortCtl*>(base + NA_OFF_CTL);
+  e.err_out = reinterpret_cast<int*>(base + NA_OFF_ERR);
+  e.slice_hist = reinterpret_cast<uint32_t*>(base + NA_OFF_HIST);
+  e.counts = reinterpret_cast<uint32_t*>(base + NA_OFF_COUNTS);
+  e.offsets = reinterpret_cast<uint32_t*>(base + NA_OFF_OFFSETS);
+  e.s = nullptr;
+  Slices sl{};
+  if ((rc = dispatch_slices(e, dtype, n, false, &sl))) return rc;
+  if (sl.count > NA_MAX_SLICES) return fail(nullptr, FS_E_INVALID, "internal: %u slices exceed the fixed scratch", sl.count);
+  // The arena keeps the previous call's contents: the histogram accumulates
+  // from zero and the error words must start clear.
+  ce = cudaMemsetAsync(e.ctl, 0, sizeof(SortCtl), e.stream);
+  if (ce == cudaSuccess) ce = cudaMemsetAsync(e.err_out, 0, sizeof(int), e.stream);
+  if (ce != cudaSuccess) return cuda_fail(nullptr, ce, "cudaMemsetAsync(noalloc scratch)");
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys;
+  a.kfinal = keys;
+  a.kother = base + NA_OFF_KEYS;
+  a.passes = kb;
+  a.has_vals = 0;
+  a.write_keys = 1;
+  a.key_bytes = kb;
+  if ((rc = dispatch_enqueue(e, dtype, a, sl, nullptr))) return rc;
+  int dev_err = 0;
+  ce = cudaMemcpyAsync(&dev_err, e.err_out, sizeof(int), cudaMemcpyDeviceToHost, e.stream);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(e.stream);
+  if (ce != cudaSuccess) return cuda_fail(nullptr, ce, "fs_sort_keys_noalloc");
+  if (dev_err == DEV_ERR_BOUNDS) return fail(nullptr, FS_E_GPU_EXECUTION, "scatter position out of range");
+  if (dev_err != 0) return fail(nullptr, FS_E_TIMEOUT, "device wait timeout in fs_sort_keys_noalloc");
+  return FS_OK;
 }
 
 uint64_t fs_scratch_bytes(const fs_sorter* s) {

@@ -71,7 +71,7 @@ int fs_destroy(fs_sorter* s);
 
 /* Text of the last failure on `s` (never NULL; "" when none).  With s == NULL,
  * the text of the last failure on this thread of a call that has no sorter
- * (fs_create). */
+ * (fs_create, fs_sort_keys_noalloc). */
 const char* fs_last_error(const fs_sorter* s);
 
 /* Replace the stream the sorter enqueues on (NULL = its private stream). */
@@ -151,6 +151,31 @@ int fs_set_kernel_timing(fs_sorter* s, int on);
  * histogram, plan, then per digit pass (count + slice scan, scatter), then
  * finalize -- 3 + 2*P entries for P = key bytes. */
 int fs_last_kernel_times(fs_sorter* s, float* ms, int cap);
+
+/* ---- allocation-free form ------------------------------------------------ */
+
+/* Sort n keys in place at `keys` (device memory of the current device),
+ * enqueued on `stream` (a cudaStream_t; NULL = legacy default stream), then
+ * wait for that stream and report device-side failures.  Same order as
+ * fs_sort_keys.
+ *
+ * No counterpart in the reference.  This entry point allocates nothing -- no
+ * cudaMalloc, cudaFree, pinned host memory or allocating library routine, and
+ * no sorter object -- for callers that must not allocate: code running under
+ * a fixed device-memory budget or a caching allocator that owns all device
+ * memory, host threads that must not block in the driver's allocator, and
+ * plugins embedded in runtimes that forbid device allocations at call time.
+ * Its scratch is one fixed device array inside this library, sized for 4 MiB
+ * of keys (2^20 u32/i32/f32 or 2^19 u64/i64/f64 keys); larger n returns
+ * FS_E_INVALID with the limit in fs_last_error(NULL).  Every GPU that loads
+ * the library holds that array (about 6.6 MB) until the process exits.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All
+ * calls share the one array: calls that overlap on the GPU (other streams or
+ * host threads, same device) race and corrupt each other's results, so
+ * serialise them.  Errors: text in fs_last_error(NULL). */
+int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream);
 
 /* ---- introspection ------------------------------------------------------- */
 
