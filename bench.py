@@ -218,7 +218,7 @@ def run_ours(args):
 
     rank, world, local = dist_env()
     if world > 1:
-        raise SystemExit("multi-GPU sample sort not wired into bench.py yet")
+        return run_multi(args)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     stream = torch.cuda.Stream(device=dev)
@@ -338,6 +338,145 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     sorter.close()
+
+
+def run_multi(args):
+    """N > 1: the sample sort, one process per GPU (torchrun), NCCL all-to-all."""
+    import datetime
+
+    import torch
+    import torch.distributed as tdist
+
+    import forge_sort
+    from forge_sort import _lib
+    from forge_sort.samplesort import CudaOps, SampleSorter
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    stream = torch.cuda.Stream(device=dev)
+    sorter = forge_sort.GpuSorter.with_context(local, stream)
+    L = _lib.load()
+    dt = args.dtype
+    kb = 4 if dt == "u32" else 8
+    n_total = 1 << args.log2n
+    m = n_total // world
+    tdt = torch.int32 if kb == 4 else torch.int64
+    keys_in = torch.empty(m, dtype=tdt, device=dev)
+    gen = {"u32": _lib.GEN_U32, "u64": _lib.GEN_U64}[dt]
+    if args.dist == "skew":
+        gen = _lib.GEN_SKEW_U32
+    assert L.fs_generate(gen, 42, rank * m, m, keys_in.data_ptr(), stream.cuda_stream) == 0
+    stream.synchronize()
+    ss = SampleSorter(CudaOps(sorter, torch), dtype=dt)
+
+    def step():
+        return ss.sort(keys_in, gpos_base=rank * m)
+
+    def timed(fn, steps):
+        tdist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        out = None
+        for _ in range(steps):
+            out = fn()
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)  # the job is as slow as its slowest rank
+        tdist.barrier()
+        return float(t.item()), out
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            out = step()
+        del out
+        with Clocks(local) as clk:
+            ms, out = timed(step, args.steps)
+    clocks = clk.summary()
+
+    # correctness of the timed output: sorted pieces, ordered across ranks,
+    # all keys accounted for
+    o = out.cpu().numpy().view("u4" if kb == 4 else "u8")
+    assert (o[1:] >= o[:-1]).all(), "rank output not sorted"
+    edge = torch.tensor([int(o[0]) if o.size else -1, int(o[-1]) if o.size else -1, o.size],
+                        dtype=torch.float64, device=dev)
+    edges = [torch.empty_like(edge) for _ in range(world)]
+    tdist.all_gather(edges, edge)
+    ev = [e.cpu().tolist() for e in edges]
+    assert sum(int(e[2]) for e in ev) == n_total, "keys lost in the exchange"
+    nonempty = [e for e in ev if e[2] > 0]
+    assert all(a[1] <= b[0] for a, b in zip(nonempty, nonempty[1:])), "ranks out of order"
+    recv = ss.last.recv_counts
+    max_piece = max(int(e[2]) for e in ev)
+
+    # dominant kernel: k_scatter of the local sort (the last call of a step)
+    sorter.set_kernel_timing(True)
+    with torch.cuda.stream(stream):
+        step()
+    t = sorter.last_kernel_times()
+    sorter.set_kernel_timing(False)
+    P = kb
+    pass_ms = [t[3 + 2 * p] for p in range(P)]
+    pass_avg = sum(pass_ms) / len(pass_ms)
+    peak, peak_kind = measured_peak_hbm()
+    piece = out.numel()
+    achieved = piece * 2 * kb / (pass_avg * 1e-3) / 1e9
+    # phase-summed roofline of the whole job (slowest rank holds max_piece):
+    # partition hist+pass (3K), local sort (K(1+2P) + K(P-1) counts),
+    # send read + receive write (2K) over HBM, and (G-1)/G of the keys over
+    # NVLink at the measured 770 GB/s per direction
+    nvlink = 770.0
+    hbm_b = m * 3 * kb + max_piece * (kb * (1 + 2 * P) + kb * (P - 1)) + 2 * m * kb
+    t_roof = hbm_b / (peak * 1e9) + m * kb * (world - 1) / world / (nvlink * 1e9)
+    roofline = {
+        "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+        "kernel": "k_scatter (local sort pass)", "alg_bytes_per_launch": piece * 2 * kb,
+        "pass_ms": round(pass_avg, 4),
+        "job_roofline_ms": round(t_roof * 1e3, 3), "job_frac": round(t_roof * 1e3 / ms, 4),
+        "job_model": "HBM: partition 3K + local sort K(1+2P)+K(P-1) + exchange 2K per key; NVLink (G-1)/G*K at 770 GB/s",
+    }
+    value = n_total / (ms * 1e-3) / 1e6
+
+    e2e = None
+    if not args.no_e2e:
+        h_in = torch.empty(m, dtype=tdt, pin_memory=True)
+        h_in.copy_(keys_in.cpu())
+        h_out = torch.empty(max_piece + (1 << 20), dtype=tdt, pin_memory=True)
+
+        def e2e_step():
+            d_in = torch.empty(m, dtype=tdt, device=dev)
+            d_in.copy_(h_in, non_blocking=True)
+            r = ss.sort(d_in, gpos_base=rank * m)
+            h_out[: r.numel()].copy_(r, non_blocking=True)
+            return r.numel()
+
+        with torch.cuda.stream(stream):
+            for _ in range(min(args.warmup, 3)):
+                e2e_step()
+            ems, got = timed(e2e_step, args.steps)
+        e2e = {"value": round(n_total / (ems * 1e-3) / 1e6, 2), "unit": UNIT,
+               "h2d_bytes_per_step": m * kb, "d2h_bytes_per_step": int(got) * kb,
+               "ms_per_step": round(ems, 3), "api": "SampleSorter.sort on pinned host shards (H2D, sort, D2H per rank)"}
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": dt, "data": "synthetic", "config": config(args, world),
+        "roofline": roofline, "cpu_baseline": None, "e2e": e2e, "clocks": clocks,
+        "gpu_launches": (5 + 3 + 3 * P) * args.steps,
+        "balance": {"max_piece": max_piece, "mean_piece": n_total // world, "recv_counts_rank0": recv if rank == 0 else None},
+        "impl": "ours",
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    sorter.close()
+    tdist.barrier()
+    tdist.destroy_process_group()
 
 
 def main():

@@ -330,6 +330,47 @@ int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   return dispatch_enqueue(e, dtype, a, sl, &s->last_launches);
 }
 
+// ---- sample-sort partition --------------------------------------------------
+// One stable pass that moves every key to the splitter bucket its (ordered
+// key, global position) falls in: the same slice / count / scatter machinery
+// as a radix pass, with the bucket index as the digit.
+template <typename K, int XF>
+int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_t n, uint64_t gpos_base,
+                      const void* spl_keys, const uint64_t* spl_gpos, int nsplit, unsigned long long* counts_out) {
+  using D = SplitterDigit<K, XF>;
+  const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
+  Exec e = exec_of(s);
+  Slices sl{};
+  int rc = make_slices<K, false, XF, D>(e, n, &sl);
+  if (rc) return rc;
+  if ((rc = ensure_slice_buffers(s, sl, 1))) return rc;
+  e.slice_hist = static_cast<uint32_t*>(s->slice_hist);
+  e.counts = static_cast<uint32_t*>(s->counts);
+  e.offsets = static_cast<uint32_t*>(s->offsets);
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys_in;
+  a.kfinal = keys_out;
+  a.kother = s->kother;
+  a.passes = 1;
+  a.has_vals = 0;
+  a.write_keys = 1;
+  a.key_bytes = (int)sizeof(K);
+  a.counts_out = counts_out;
+  a.ncounts = nsplit + 1;
+  k_bucket_hist<K, XF, HIST_BLOCK><<<sl.count, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(keys_in), n, e.ctl,
+                                                                         sl, e.slice_hist, dfn, gpos_base);
+  k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
+  k_slice_scan<<<1, RADIX, 0, e.stream>>>(e.ctl, 0, 1, sl, e.slice_hist, e.counts, e.offsets);
+  launch_scatter<K, false, XF>(e, 0, n, sl, dfn, gpos_base);
+  uint64_t fb = (n + 255) / 256;
+  const uint64_t fcap = (uint64_t)e.sm_count * 4;
+  k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, e.stream>>>(e.ctl, n, e.err_out);
+  s->last_launches = 5;
+  FS_CUDA(s, cudaGetLastError());
+  return FS_OK;
+}
+
 int finish(fs_sorter* s, int sync) {
   FS_CUDA(s, cudaGetLastError());
   if (!sync) return FS_OK;
@@ -786,6 +827,41 @@ int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream) {
   if (dev_err == DEV_ERR_BOUNDS) return fail(nullptr, FS_E_GPU_EXECUTION, "scatter position out of range");
   if (dev_err != 0) return fail(nullptr, FS_E_TIMEOUT, "device wait timeout in fs_sort_keys_noalloc");
   return FS_OK;
+}
+
+int fs_partition(fs_sorter* s, int dtype, const void* keys_in, uint64_t n, uint64_t gpos_base,
+                 const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit, void* keys_out,
+                 uint64_t* bucket_counts, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (nsplit < 0 || nsplit > RADIX - 1) return fail(s, FS_E_INVALID, "nsplit = %d outside [0, 255]", nsplit);
+  if (!bucket_counts) return fail(s, FS_E_INVALID, "bucket_counts is NULL");
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  if ((rc = prepare_ptr(s, bucket_counts, (size_t)(nsplit + 1) * 8, "bucket_counts"))) return rc;
+  if (n == 0) {
+    FS_CUDA(s, cudaMemsetAsync(bucket_counts, 0, (size_t)(nsplit + 1) * 8, s->stream));
+    return finish(s, sync);
+  }
+  if (keys_in == keys_out) return fail(s, FS_E_INVALID, "keys_in and keys_out must differ");
+  if ((rc = prepare_ptr(s, keys_in, (size_t)n * kb, "keys_in"))) return rc;
+  if ((rc = prepare_ptr(s, keys_out, (size_t)n * kb, "keys_out"))) return rc;
+  if (nsplit > 0) {
+    if ((rc = prepare_ptr(s, splitter_keys, (size_t)nsplit * kb, "splitter_keys"))) return rc;
+    if ((rc = prepare_ptr(s, splitter_gpos, (size_t)nsplit * 8, "splitter_gpos"))) return rc;
+  }
+  if ((rc = grow(s, &s->kother, &s->kother_bytes, (size_t)n * kb, false))) return rc;
+  auto* counts = reinterpret_cast<unsigned long long*>(bucket_counts);
+  switch (dtype) {
+    case FS_U32: rc = enqueue_partition<uint32_t, XF_NONE>(s, keys_in, keys_out, n, gpos_base, splitter_keys, splitter_gpos, nsplit, counts); break;
+    case FS_I32: rc = enqueue_partition<uint32_t, XF_SIGN>(s, keys_in, keys_out, n, gpos_base, splitter_keys, splitter_gpos, nsplit, counts); break;
+    case FS_F32: rc = enqueue_partition<uint32_t, XF_FLOAT>(s, keys_in, keys_out, n, gpos_base, splitter_keys, splitter_gpos, nsplit, counts); break;
+    case FS_U64: rc = enqueue_partition<uint64_t, XF_NONE>(s, keys_in, keys_out, n, gpos_base, splitter_keys, splitter_gpos, nsplit, counts); break;
+    case FS_I64: rc = enqueue_partition<uint64_t, XF_SIGN>(s, keys_in, keys_out, n, gpos_base, splitter_keys, splitter_gpos, nsplit, counts); break;
+    default: rc = enqueue_partition<uint64_t, XF_FLOAT>(s, keys_in, keys_out, n, gpos_base, splitter_keys, splitter_gpos, nsplit, counts); break;
+  }
+  if (rc) return rc;
+  return finish(s, sync);
 }
 
 uint64_t fs_scratch_bytes(const fs_sorter* s) {

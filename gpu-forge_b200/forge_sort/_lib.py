@@ -48,6 +48,7 @@ SIGNATURES = {
     "fs_host_sort_keys_copy": (_i32, [_vp, _i32, _vp, _vp, _u64]),
     "fs_set_kernel_timing": (_i32, [_vp, _i32]),
     "fs_last_kernel_times": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), _i32]),
+    "fs_partition": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _i32]),
     "fs_sort_keys_noalloc": (_i32, [_i32, _vp, _u64, _vp]),
     "fs_scratch_bytes": (_u64, [_vp]),
     "fs_last_launch_count": (_i32, [_vp]),

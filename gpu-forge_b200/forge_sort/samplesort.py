@@ -1,0 +1,182 @@
+"""Multi-GPU sample sort over torch.distributed (one process per GPU).
+
+No counterpart in the reference (forge-sort is single-device); this is the
+1-8 x B200 path the benchmark configs ask for.  Every rank holds one shard of
+the input; afterwards rank r holds the r-th contiguous piece of the globally
+sorted sequence (concatenating the ranks' outputs in rank order gives the
+sorted input, bit for bit).
+
+Per call, on every rank:
+  1. samples: S keys at regular positions of the (unsorted) shard, tagged
+     with their global positions; all-gathered, so every rank sorts the same
+     G*S tuples on the host and picks the same G-1 splitters (every S-th);
+     the (key, global position) order breaks ties, so duplicate-heavy input
+     still splits evenly;
+  2. partition: one stable GPU pass sends every key to its splitter bucket
+     (fs_partition: the radix scatter machinery with the bucket as digit);
+  3. exchange: bucket sizes, then one all-to-all of the buckets (NCCL over
+     NVLink on GPUs);
+  4. local sort of the received keys (the single-GPU radix sort).
+
+The local steps go through a LocalOps object so the host logic can run on
+CPU ranks (gloo) in tests with a CPU stand-in; CudaOps is the product path.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Tuple
+
+import numpy as np
+
+from .sorter import GpuSorter, dtype_name
+
+_BITS = {"u32": np.uint32, "i32": np.uint32, "f32": np.uint32,
+         "u64": np.uint64, "i64": np.uint64, "f64": np.uint64}
+_WIDTH = {"u32": 32, "i32": 32, "f32": 32, "u64": 64, "i64": 64, "f64": 64}
+
+
+def ordered_bits(raw: np.ndarray, dt: str) -> np.ndarray:
+    """Order-preserving image of raw key bits as uint64 (unsigned order ==
+    the sort order): sign flip for signed ints, FloatFlip for floats."""
+    w = _WIDTH[dt]
+    x = np.ascontiguousarray(raw).view(_BITS[dt]).astype(np.uint64)
+    sign = np.uint64(1) << np.uint64(w - 1)
+    if dt in ("i32", "i64"):
+        return x ^ sign
+    if dt in ("f32", "f64"):
+        full = np.uint64((1 << w) - 1)
+        neg = (x & sign) != 0
+        return np.where(neg, x ^ full, x ^ sign)
+    return x
+
+
+def choose_splitters(samples_ordered: np.ndarray, samples_gpos: np.ndarray, ranks: int,
+                     per_rank: int) -> np.ndarray:
+    """Indices (into the gathered sample arrays) of the G-1 splitters: every
+    per_rank-th tuple in (ordered key, global position) order."""
+    order = np.lexsort((samples_gpos, samples_ordered))
+    picks = [order[j * per_rank] for j in range(1, ranks)]
+    return np.asarray(picks, dtype=np.int64)
+
+
+def sample_positions(m: int, per_rank: int) -> np.ndarray:
+    """Regular positions within a shard of m keys (empty if m == 0)."""
+    if m == 0:
+        return np.zeros(0, np.int64)
+    return ((np.arange(per_rank, dtype=np.float64) + 0.5) * (m / per_rank)).astype(np.int64).clip(0, m - 1)
+
+
+class CudaOps:
+    """Product path: the partition and the local sort run in libforgesort."""
+
+    def __init__(self, sorter: GpuSorter, torch):
+        self.s = sorter
+        self.torch = torch
+
+    def partition(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray) -> Tuple[object, List[int]]:
+        torch = self.torch
+        dev = keys.device
+        nspl = len(spl_gpos)
+        out = torch.empty_like(keys)
+        counts = torch.zeros(nspl + 1, dtype=torch.int64, device=dev)
+        if nspl:
+            sk = torch.from_numpy(np.ascontiguousarray(spl_raw).view(
+                np.int32 if _WIDTH[dt] == 32 else np.int64)).to(dev)
+            sg = torch.from_numpy(spl_gpos.astype(np.int64)).to(dev)
+            skp, sgp = sk.data_ptr(), sg.data_ptr()
+        else:
+            sk = sg = None
+            skp = sgp = 0
+        self.s.partition_device(dt, keys.data_ptr(), keys.numel(), gpos_base, skp, sgp, nspl, out.data_ptr(),
+                                counts.data_ptr(), sync=True)
+        del sk, sg
+        return out, [int(c) for c in counts.cpu().tolist()]
+
+    def sort(self, dt, keys):
+        out = self.torch.empty_like(keys)
+        if keys.numel():
+            self.s.sort_device_copy(dt, keys.data_ptr(), out.data_ptr(), keys.numel(), sync=True)
+        return out
+
+
+@dataclass
+class SampleSortStats:
+    send_counts: List[int]
+    recv_counts: List[int]
+
+
+class SampleSorter:
+    """Sample sort across the ranks of a torch.distributed process group.
+
+    sort(keys) takes this rank's shard (a 1-D torch tensor holding the raw
+    key bits as int32/int64) and returns this rank's piece of the globally
+    sorted sequence.  gpos_base is the global position of keys[0] (default:
+    the sum of the shard sizes of lower ranks, gathered once per call)."""
+
+    def __init__(self, ops, dtype="u32", group=None, samples_per_rank: int = 8192):
+        import torch
+        import torch.distributed as dist
+        self.torch = torch
+        self.dist = dist
+        self.ops = ops
+        self.dt = dtype_name(dtype)
+        self.group = group
+        self.per_rank = samples_per_rank
+        self.last: Optional[SampleSortStats] = None
+
+    def _world(self):
+        return self.dist.get_world_size(self.group), self.dist.get_rank(self.group)
+
+    def sort(self, keys, gpos_base: Optional[int] = None):
+        torch, dist, dt = self.torch, self.dist, self.dt
+        G, r = self._world()
+        m = keys.numel()
+        dev = keys.device
+        if gpos_base is None:
+            sizes = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(G)]
+            dist.all_gather(sizes, torch.tensor([m], dtype=torch.int64, device=dev), group=self.group)
+            gpos_base = int(sum(int(t.item()) for t in sizes[:r]))
+        if G == 1:
+            self.last = SampleSortStats([m], [m])
+            return self.ops.sort(dt, keys)
+
+        # 1. regular samples with their global positions -> splitters
+        S = self.per_rank
+        pos = sample_positions(m, S)
+        raw = keys[torch.from_numpy(pos).to(dev)].cpu().numpy() if m else np.zeros(0, keys.cpu().numpy().dtype)
+        ords = ordered_bits(raw, dt) if m else np.zeros(0, np.uint64)
+        gpos = (pos + gpos_base).astype(np.uint64)
+        # fixed-size exchange: pad empty shards with maximal tuples (never picked
+        # below index (G-1)*S unless most shards are empty; still a valid split)
+        if m == 0:
+            ords = np.full(S, np.iinfo(np.uint64).max, np.uint64)
+            gpos = np.full(S, np.iinfo(np.uint64).max, np.uint64)
+            raw = np.zeros(S, dtype=np.int32 if _WIDTH[dt] == 32 else np.int64)
+        mine = np.stack([ords.view(np.int64), gpos.view(np.int64),
+                         np.ascontiguousarray(raw).view(_BITS[dt]).astype(np.uint64).view(np.int64)], axis=1)
+        t_mine = torch.from_numpy(np.ascontiguousarray(mine)).to(dev)
+        gathered = [torch.empty_like(t_mine) for _ in range(G)]
+        dist.all_gather(gathered, t_mine, group=self.group)
+        allv = torch.cat(gathered).cpu().numpy()
+        a_ord = allv[:, 0].view(np.uint64)
+        a_gpos = allv[:, 1].view(np.uint64)
+        a_raw = allv[:, 2].view(np.uint64)
+        picks = choose_splitters(a_ord, a_gpos, G, S)
+        spl_raw = a_raw[picks].astype(_BITS[dt])
+        spl_gpos = a_gpos[picks]
+
+        # 2. stable partition into G buckets
+        part, send = self.ops.partition(dt, keys, gpos_base, spl_raw, spl_gpos)
+
+        # 3. exchange sizes, then the buckets
+        sc = torch.tensor(send, dtype=torch.int64, device=dev)
+        rc = torch.empty(G, dtype=torch.int64, device=dev)
+        dist.all_to_all_single(rc, sc, group=self.group)
+        recv = [int(x) for x in rc.cpu().tolist()]
+        inbox = torch.empty(sum(recv), dtype=keys.dtype, device=dev)
+        dist.all_to_all_single(inbox, part, output_split_sizes=recv, input_split_sizes=send, group=self.group)
+        del part
+
+        # 4. local sort of this rank's bucket
+        self.last = SampleSortStats(send, recv)
+        return self.ops.sort(dt, inbox)

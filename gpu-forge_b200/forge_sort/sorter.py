@@ -431,6 +431,15 @@ class GpuSorter:
             self._call(-k)
         return [float(buf[i]) for i in range(k)]
 
+    def partition_device(self, dt, in_ptr: int, n: int, gpos_base: int, spl_keys_ptr: int, spl_gpos_ptr: int,
+                         nsplit: int, out_ptr: int, counts_ptr: int, sync: bool = True) -> None:
+        """Stable splitter partition (multi-GPU sample sort step), device pointers."""
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_partition(self._h, _DT[name][0], ctypes.c_void_p(in_ptr), n, gpos_base,
+                                            ctypes.c_void_p(spl_keys_ptr), ctypes.c_void_p(spl_gpos_ptr), nsplit,
+                                            ctypes.c_void_p(out_ptr), ctypes.c_void_p(counts_ptr), int(sync)))
+        self._pending = self._pending or not sync
+
     def host_sort_ptr(self, dt, host_ptr: int, n: int) -> None:
         """sort_<dt> on raw (e.g. pinned) host memory; H2D + sort + D2H."""
         name = dtype_name(dt)

@@ -152,6 +152,22 @@ int fs_set_kernel_timing(fs_sorter* s, int on);
  * finalize -- 3 + 2*P entries for P = key bytes. */
 int fs_last_kernel_times(fs_sorter* s, float* ms, int cap);
 
+/* ---- multi-GPU sample sort building block -------------------------------- */
+
+/* Stable partition of n keys (device pointers keys_in -> keys_out, which must
+ * differ) into nsplit+1 contiguous buckets.  Bucket b holds the keys whose
+ * (key, global position) pair is >= splitter b-1 and < splitter b, in the
+ * same order as fs_sort_keys; a key's global position is gpos_base + its index.
+ * splitter_keys (nsplit keys of `dtype`, raw bits) and splitter_gpos
+ * (nsplit u64) are device pointers, ascending by (key, position).  Writes the
+ * bucket sizes to bucket_counts (device, nsplit+1 u64).  0 <= nsplit <= 255.
+ * No counterpart in the reference (it has no multi-GPU path); this is the
+ * partition step of the 1-8 GPU sample sort. */
+int fs_partition(fs_sorter* s, int dtype, const void* keys_in, uint64_t n,
+                 uint64_t gpos_base, const void* splitter_keys,
+                 const uint64_t* splitter_gpos, int nsplit, void* keys_out,
+                 uint64_t* bucket_counts, int sync);
+
 /* ---- allocation-free form ------------------------------------------------ */
 
 /* Sort n keys in place at `keys` (device memory of the current device),

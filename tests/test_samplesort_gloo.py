@@ -1,0 +1,116 @@
+"""Multi-GPU sample-sort host logic on CPU ranks (gloo, world sizes 2 and 3).
+
+The orchestration in forge_sort.samplesort (sampling, splitter choice with
+the (key, global position) tie-break, size exchange, all-to-all) runs for
+real; the two GPU steps (partition, local sort) are replaced by a numpy
+stand-in and the result is checked against the oracle's sort of the whole
+input.  No GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+N_PER_RANK = 20_000
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+class CpuOps:
+    """Host stand-in for CudaOps (test only)."""
+
+    def __init__(self, torch):
+        self.torch = torch
+
+    def partition(self, dt, keys, gpos_base, spl_raw, spl_gpos):
+        from forge_sort.samplesort import ordered_bits
+        x = keys.numpy()
+        o = ordered_bits(x, dt)
+        g = np.arange(x.size, dtype=np.uint64) + np.uint64(gpos_base)
+        so = ordered_bits(spl_raw, dt)
+        bucket = np.zeros(x.size, np.int64)
+        for j in range(len(spl_gpos)):
+            bucket += ((o > so[j]) | ((o == so[j]) & (g >= spl_gpos[j]))).astype(np.int64)
+        idx = np.argsort(bucket, kind="stable")
+        counts = np.bincount(bucket, minlength=len(spl_gpos) + 1)
+        return self.torch.from_numpy(x[idx].copy()), [int(c) for c in counts]
+
+    def sort(self, dt, keys):
+        from oracle import oracle as orc
+        x = keys.numpy()
+        bits = np.uint32 if x.dtype.itemsize == 4 else np.uint64
+        npdt = orc.NP_DTYPE[dt]
+        s = orc.sort_keys(x.view(bits).view(npdt), dt)
+        return self.torch.from_numpy(s.view(x.dtype).copy())
+
+
+def _worker(rank, world, port, dist_name, dt, result_path, per_rank_sizes):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "gpu-forge_b200"), root]
+    import torch
+    import torch.distributed as tdist
+    from forge_sort.samplesort import SampleSorter
+    from oracle import oracle as orc
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    tdist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        start = sum(per_rank_sizes[:rank])
+        m = per_rank_sizes[rank]
+        x = orc.gen(dist_name, sum(per_rank_sizes), seed=5)[start:start + m]
+        bits = np.uint32 if x.dtype.itemsize == 4 else np.uint64
+        t = torch.from_numpy(np.ascontiguousarray(x).view(bits).view(np.int32 if bits is np.uint32 else np.int64))
+        ss = SampleSorter(CpuOps(torch), dtype=dt, samples_per_rank=512)
+        out = ss.sort(t)
+        np.save(f"{result_path}.{rank}.npy", out.numpy())
+    finally:
+        tdist.destroy_process_group()
+
+
+def _run(world, dist_name, dt, tmp_path, per_rank_sizes=None):
+    import torch.multiprocessing as mp
+    sizes = per_rank_sizes or [N_PER_RANK] * world
+    path = str(tmp_path / "out")
+    mp.start_processes(_worker, args=(world, _free_port(), dist_name, dt, path, sizes), nprocs=world,
+                       start_method="spawn")
+    from oracle import oracle as orc
+    x = orc.gen(dist_name, sum(sizes), seed=5)
+    want = orc.sort_keys(x, dt)
+    bits = np.uint32 if want.dtype.itemsize == 4 else np.uint64
+    pieces = [np.load(f"{path}.{r}.npy").view(bits) for r in range(world)]
+    got = np.concatenate(pieces)
+    assert np.array_equal(got, want.view(bits))
+    return [p.size for p in pieces]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_uniform_u32(world, tmp_path):
+    sizes = _run(world, "u32", "u32", tmp_path)
+    assert max(sizes) < 1.25 * N_PER_RANK  # regular sampling keeps buckets near n/G
+
+
+def test_skewed_u32_70pct_in_one_range(tmp_path):
+    sizes = _run(2, "skew_u32", "u32", tmp_path)
+    assert max(sizes) < 1.25 * N_PER_RANK
+
+
+def test_all_duplicates_still_split_by_position(tmp_path):
+    # zipf keys: most mass on a few values; the (key, position) tie-break
+    # still divides equal keys between ranks
+    sizes = _run(2, "zipf_u32", "u32", tmp_path)
+    assert max(sizes) < 1.25 * N_PER_RANK
+
+
+@pytest.mark.parametrize("dt,dist_name", [("f64", "f64_logu"), ("i64", "i64"), ("f32", "f32_mix")])
+def test_other_key_types(dt, dist_name, tmp_path):
+    _run(2, dist_name, dt, tmp_path)
+
+
+def test_uneven_and_empty_shards(tmp_path):
+    _run(3, "u32", "u32", tmp_path, per_rank_sizes=[25_000, 0, 7_000])
