@@ -89,6 +89,7 @@ enum PassFlags : uint32_t {
   PD_WRITE_KEYS = 1u << 4,  // write keys (argsort's last pass does not)
   PD_FIRST = 1u << 5,       // first executed pass: slice counts come from the
                             // upfront histogram (input order is unchanged)
+  PD_UNSTABLE = 1u << 6,    // keys-only first pass: order among equal digits is free
 };
 
 struct PassDesc {
@@ -151,6 +152,7 @@ struct PlanArgs {
   int key_bytes;
   unsigned long long* counts_out;  // optional copy of pass-0 digit counts
   int ncounts;                     // entries of counts_out
+  int unstable_first;              // keys-only LSD sort: first pass may reorder ties
 };
 
 }  // namespace fs

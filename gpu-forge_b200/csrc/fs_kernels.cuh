@@ -30,7 +30,7 @@
 #include "fs_device.cuh"
 
 #ifndef FS_RANK_BALLOT
-#define FS_RANK_BALLOT 1
+#define FS_RANK_BALLOT 2
 #endif
 
 namespace fs {
@@ -91,7 +91,13 @@ struct RadixDigit {
   static constexpr bool STAGE = false;  // recomputed from the staged key
   template <typename K>
   __device__ __forceinline__ uint32_t operator()(K k, uint64_t) const {
-    return digit_of(k, shift);
+    // one byte-permute instruction instead of shift + mask
+    if constexpr (sizeof(K) == 4) {
+      return __byte_perm((uint32_t)k, 0u, 0x4440u | (uint32_t)(shift >> 3));
+    } else {
+      const uint32_t half = shift >= 32 ? (uint32_t)((uint64_t)k >> 32) : (uint32_t)k;
+      return __byte_perm(half, 0u, 0x4440u | (uint32_t)((shift >> 3) & 3));
+    }
   }
 };
 
@@ -206,16 +212,20 @@ __global__ void __launch_bounds__(BLOCK)
   __shared__ uint32_t h[P][RADIX];
   for (int i = threadIdx.x; i < P * RADIX; i += BLOCK) (&h[0][0])[i] = 0;
   __syncthreads();
-  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
-  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
-  for_each_key<K, BLOCK, VEC>(keys, lo, hi,
-                              [&](K x, bool valid) { warp_count_digits<K, P>(h, to_ordered<K, XF>(x), valid); });
-  __syncthreads();
-  uint32_t* out = slice_hist + (size_t)blockIdx.x * P * RADIX;
-  for (int b = threadIdx.x; b < P * RADIX; b += BLOCK) {
-    const uint32_t c = (&h[0][0])[b];
-    out[b] = c;
-    if (c) atomicAdd(&(&ctl->hist[0][0])[b], (unsigned long long)c);
+  for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
+    const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
+    const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+    for_each_key<K, BLOCK, VEC>(keys, lo, hi,
+                                [&](K x, bool valid) { warp_count_digits<K, P>(h, to_ordered<K, XF>(x), valid); });
+    __syncthreads();
+    uint32_t* out = slice_hist + (size_t)c * P * RADIX;
+    for (int b = threadIdx.x; b < P * RADIX; b += BLOCK) {
+      const uint32_t v = (&h[0][0])[b];
+      out[b] = v;
+      (&h[0][0])[b] = 0;
+      if (v) atomicAdd(&(&ctl->hist[0][0])[b], (unsigned long long)v);
+    }
+    __syncthreads();
   }
 }
 
@@ -231,15 +241,20 @@ __global__ void __launch_bounds__(BLOCK)
   __shared__ uint32_t h[RADIX];
   for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[i] = 0;
   __syncthreads();
-  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
-  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
-  for (uint64_t i = lo + threadIdx.x; i < hi; i += BLOCK)
-    atomicAdd(&h[dfn(to_ordered<K, XF>(keys[i]), gpos_base + i)], 1u);
-  __syncthreads();
-  uint32_t* out = slice_hist + (size_t)blockIdx.x * RADIX;
-  for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
-    out[b] = h[b];
-    if (h[b]) atomicAdd(&ctl->hist[0][b], (unsigned long long)h[b]);
+  for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
+    const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
+    const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+    for (uint64_t i = lo + threadIdx.x; i < hi; i += BLOCK)
+      atomicAdd(&h[dfn(to_ordered<K, XF>(keys[i]), gpos_base + i)], 1u);
+    __syncthreads();
+    uint32_t* out = slice_hist + (size_t)c * RADIX;
+    for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
+      const uint32_t v = h[b];
+      out[b] = v;
+      h[b] = 0;
+      if (v) atomicAdd(&ctl->hist[0][b], (unsigned long long)v);
+    }
+    __syncthreads();
   }
 }
 
@@ -295,6 +310,7 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
       uint32_t* vdst = slot_final ? a.vfinal : a.vother;
       uint32_t f = PD_EXEC;
       if (i == 1) f |= PD_XF_IN | PD_FIRST;
+      if (i == 1 && !a.has_vals && a.unstable_first) f |= PD_UNSTABLE;
       if (i == 1 && a.has_vals && a.vin == nullptr) f |= PD_SYNTH_IDX;
       if (i == m) f |= PD_XF_OUT;
       if (a.write_keys || i < m) f |= PD_WRITE_KEYS;
@@ -359,46 +375,53 @@ __global__ void __launch_bounds__(BLOCK)
   __shared__ uint32_t h[1][RADIX];
   for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[0][i] = 0;
   __syncthreads();
-  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
-  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
   const int shift = pass * RADIX_BITS;
   // count the pass digit only: it becomes the lowest byte of a 32-bit word
   auto f = [&](K x, bool valid) { warp_count_digits<uint32_t, 1>(h, (uint32_t)(x >> shift) & 0xffu, valid); };
-  if ((reinterpret_cast<uintptr_t>(keys) & 15) == 0)
-    for_each_key<K, BLOCK, true>(keys, lo, hi, f);
-  else
-    for_each_key<K, BLOCK, false>(keys, lo, hi, f);
-  __syncthreads();
-  for (int b = threadIdx.x; b < RADIX; b += BLOCK) counts[(size_t)blockIdx.x * RADIX + b] = h[0][b];
+  const bool vec = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
+  for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
+    const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
+    const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+    if (vec)
+      for_each_key<K, BLOCK, true>(keys, lo, hi, f);
+    else
+      for_each_key<K, BLOCK, false>(keys, lo, hi, f);
+    __syncthreads();
+    for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
+      counts[(size_t)c * RADIX + b] = h[0][b];
+      h[0][b] = 0;
+    }
+    __syncthreads();
+  }
 }
 
 // --------------------------------------------------------------------------
 // Slice scan: offsets[c][d] = base[pass][d] + sum of counts[c'][d], c' < c
 // (mod 2^32: positions are < 2^32).  One thread per digit.
 // --------------------------------------------------------------------------
-__global__ void __launch_bounds__(RADIX)
+constexpr int SCAN_LANES = 4;  // threads per digit in k_slice_scan
+__global__ void __launch_bounds__(RADIX * SCAN_LANES)
     k_slice_scan(SortCtl* __restrict__ ctl, const int pass, const int passes, const Slices sl,
                  const uint32_t* __restrict__ slice_hist, const uint32_t* __restrict__ counts,
                  uint32_t* __restrict__ offsets) {
   const uint32_t flags = ctl->pass[pass].flags;
   if (!(flags & PD_EXEC)) return;
-  const int d = threadIdx.x;
+  const int d = threadIdx.x % RADIX, q = threadIdx.x / RADIX;
   const bool first = (flags & PD_FIRST) != 0;
   const uint32_t* src = first ? slice_hist + (size_t)pass * RADIX : counts;
   const size_t stride = first ? (size_t)passes * RADIX : RADIX;
+  // thread q of digit d owns slices [c0, c1): sum them, exchange the four
+  // sums, then write the running offsets
+  const uint32_t per = (sl.count + SCAN_LANES - 1) / SCAN_LANES;
+  const uint32_t c0 = q * per, c1 = c0 + per < sl.count ? c0 + per : sl.count;
+  uint32_t sum = 0;
+  for (uint32_t c = c0; c < c1; ++c) sum += src[(size_t)c * stride + d];
+  __shared__ uint32_t s_part[SCAN_LANES][RADIX];
+  s_part[q][d] = sum;
+  __syncthreads();
   uint32_t run = (uint32_t)ctl->base[pass][d];
-  uint32_t c = 0;
-  for (; c + 8 <= sl.count; c += 8) {
-    uint32_t v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = src[(size_t)(c + u) * stride + d];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      offsets[(size_t)(c + u) * RADIX + d] = run;
-      run += v[u];
-    }
-  }
-  for (; c < sl.count; ++c) {
+  for (int j = 0; j < q; ++j) run += s_part[j][d];
+  for (uint32_t c = c0; c < c1; ++c) {
     const uint32_t v = src[(size_t)c * stride + d];
     offsets[(size_t)c * RADIX + d] = run;
     run += v;
@@ -434,7 +457,16 @@ __global__ void __launch_bounds__(RADIX)
 // __match_any_sync).
 template <bool FULL>
 __device__ __forceinline__ uint32_t warp_peers(uint32_t d, bool valid) {
-#if FS_RANK_BALLOT
+#if FS_RANK_BALLOT == 2
+  // lanes whose digit differs from mine in some bit, then complement
+  uint32_t diff = FULL ? 0u : ~__ballot_sync(0xffffffffu, valid);
+#pragma unroll
+  for (int b = 0; b < RADIX_BITS; ++b) {
+    const uint32_t bit = (d >> b) & 1u;
+    diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
+  }
+  return valid ? ~diff : (1u << (threadIdx.x & 31));
+#elif FS_RANK_BALLOT
   uint32_t peers = FULL ? 0xffffffffu : __ballot_sync(0xffffffffu, valid);
 #pragma unroll
   for (int b = 0; b < RADIX_BITS; ++b) {
@@ -509,17 +541,28 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   // for that digit, the group's highest lane advances it.  After the loop
   // the counters hold the warp's per-digit totals.
   uint32_t rank[IPT];
+  if (flags & PD_UNSTABLE) {
+    // Keys-only first pass: no earlier order to keep, so any order among
+    // equal digits is correct -- one shared atomic per key ranks it.
 #pragma unroll
-  for (int k = 0; k < IPT; ++k) {
-    const bool valid = FULL || (wofs + k * 32) < tile_n;
-    const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
-    const uint32_t peers = warp_peers<FULL>(d, valid);
-    uint32_t old = 0;
-    if (valid) old = wcnt[d];
-    __syncwarp();
-    if (valid && lane == 31u - __clz(peers)) wcnt[d] = old + __popc(peers);
-    __syncwarp();
-    rank[k] = old + __popc(peers & lt_mask);
+    for (int k = 0; k < IPT; ++k) {
+      const bool valid = FULL || (wofs + k * 32) < tile_n;
+      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
+      rank[k] = valid ? atomicAdd(&wcnt[d], 1u) : 0u;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      const bool valid = FULL || (wofs + k * 32) < tile_n;
+      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
+      const uint32_t peers = warp_peers<FULL>(d, valid);
+      uint32_t old = 0;
+      if (valid) old = wcnt[d];
+      __syncwarp();
+      if (valid && lane == 31u - __clz(peers)) wcnt[d] = old + __popc(peers);
+      __syncwarp();
+      rank[k] = old + __popc(peers & lt_mask);
+    }
   }
   __syncthreads();
 
@@ -607,11 +650,17 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   __syncthreads();  // staging reads done, counters zeroed: next tile may start
 }
 
-// One CTA per slice.  Tiles of the slice are processed in order; the next
-// tile's keys (and payload) are bulk-copied (cp.async.bulk global->shared, no
+// Which passes a scatter instantiation takes (the plan decides on the
+// device whether a pass ranks stably, so both instantiations are launched and
+// the one that does not match exits at once).
+enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1, SCATTER_STABLE = 2 };
+
+// CTAs loop over slices (c = blockIdx.x, +gridDim.x, ...); tiles of a slice
+// are processed in order with per-digit running offsets.  The next tile's
+// keys (and payload) are bulk-copied (cp.async.bulk global->shared, no
 // multicast) into the other of two slots while the current one is processed.
 // Every mbarrier wait is bounded; no CTA exits with a copy still in flight.
-template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, typename D>
+template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, int MODE, typename D>
 __global__ void __launch_bounds__(BLOCK, MINB)
     k_scatter(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
               const uint32_t* __restrict__ offsets, const uint64_t timeout_ns, const D dfn,
@@ -626,19 +675,19 @@ __global__ void __launch_bounds__(BLOCK, MINB)
 
   const PassDesc pd = ctl->pass[pass];
   if (!(pd.flags & PD_EXEC)) return;
+  if (MODE == SCATTER_UNSTABLE && !(pd.flags & PD_UNSTABLE)) return;
+  if (MODE == SCATTER_STABLE && (pd.flags & PD_UNSTABLE)) return;
   const K* kin = static_cast<const K*>(pd.kin);
   K* kout = static_cast<K*>(pd.kout);
   const bool copy_vals = VALS && !(pd.flags & PD_SYNTH_IDX);
   const bool bulk_ok = (reinterpret_cast<uintptr_t>(kin) & 15) == 0 &&
                        (!copy_vals || (reinterpret_cast<uintptr_t>(pd.vin) & 15) == 0);
   const uint32_t tid = threadIdx.x;
-  const uint64_t lo = (uint64_t)blockIdx.x * sl.keys_per_slice;
-  const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
-  if (lo >= hi) return;
 
-  // thread 0: start the copy of the tile at key `t0` into slot s (full tiles)
+  // thread 0: start the copy of the tile at key `t0` of a slice ending at
+  // `hi` into slot s (full tiles only)
   uint32_t armed = 0;  // thread 0: bit s = copy into slot s in flight
-  auto issue = [&](uint64_t t0, int s) {
+  auto issue = [&](uint64_t t0, uint64_t hi, int s) {
     if (bulk_ok && t0 + Ly::TILE <= hi) {
       unsigned char* dst = dsm + (size_t)s * Ly::SLOT;
       fence_proxy_async_smem();  // earlier generic reads of the slot precede the async write
@@ -651,43 +700,52 @@ __global__ void __launch_bounds__(BLOCK, MINB)
 
   uint32_t* cnt = reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF);
   for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
-  if (tid < RADIX) s_run[tid] = offsets[(size_t)blockIdx.x * RADIX + tid];
   if (tid == 0) {
     mbar_init(&s_bar[0], 1);
     mbar_init(&s_bar[1], 1);
     fence_mbar_init();
     s_abort = 0;
-    issue(lo, 0);
   }
-  __syncthreads();
 
   uint32_t parity = 0;  // bit s: phase of slot s's barrier to wait for next
   int s = 0;
-  for (uint64_t t0 = lo; t0 < hi; t0 += Ly::TILE, s ^= 1) {
-    const uint32_t tile_n = hi - t0 < (uint64_t)Ly::TILE ? (uint32_t)(hi - t0) : (uint32_t)Ly::TILE;
-    const bool full = tile_n == (uint32_t)Ly::TILE;
-    const bool from_slot = full && bulk_ok;
-    if (from_slot) {
-      if (!mbar_wait_bounded(&s_bar[s], (parity >> s) & 1u, timeout_ns, &ctl->err)) s_abort = 1;
-      parity ^= 1u << s;
-      if (tid == 0) armed &= ~(1u << s);
-    }
-    if (tid == 0) {
-      issue(t0 + Ly::TILE, s ^ 1);  // the other slot was consumed by the previous tile
-      if (ld_relaxed_s32(&ctl->err) != 0) s_abort = 1;
-    }
-    __syncthreads();  // one abort decision for the CTA
-    if (s_abort) break;
-    const unsigned char* slot = dsm + (size_t)s * Ly::SLOT;
-    if (from_slot)
-      scatter_tile<K, VALS, XF, BLOCK, IPT, true, true>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot,
-                                                       dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
-    else if (full)
-      scatter_tile<K, VALS, XF, BLOCK, IPT, true, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                        slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
-    else
-      scatter_tile<K, VALS, XF, BLOCK, IPT, false, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+  bool aborted = false;
+  for (uint32_t c = blockIdx.x; c < sl.count && !aborted; c += gridDim.x) {
+    const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
+    const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
+    __syncthreads();  // the previous slice's last tile is done with s_run
+    if (tid < RADIX) s_run[tid] = offsets[(size_t)c * RADIX + tid];
+    if (tid == 0) issue(lo, hi, s);
+    __syncthreads();
+    for (uint64_t t0 = lo; t0 < hi; t0 += Ly::TILE, s ^= 1) {
+      const uint32_t tile_n = hi - t0 < (uint64_t)Ly::TILE ? (uint32_t)(hi - t0) : (uint32_t)Ly::TILE;
+      const bool full = tile_n == (uint32_t)Ly::TILE;
+      const bool from_slot = full && bulk_ok;
+      if (from_slot) {
+        if (!mbar_wait_bounded(&s_bar[s], (parity >> s) & 1u, timeout_ns, &ctl->err)) s_abort = 1;
+        parity ^= 1u << s;
+        if (tid == 0) armed &= ~(1u << s);
+      }
+      if (tid == 0) {
+        issue(t0 + Ly::TILE, hi, s ^ 1);  // the other slot was consumed by the previous tile
+        if (ld_relaxed_s32(&ctl->err) != 0) s_abort = 1;
+      }
+      __syncthreads();  // one abort decision for the CTA
+      if (s_abort) {
+        aborted = true;
+        break;
+      }
+      const unsigned char* slot = dsm + (size_t)s * Ly::SLOT;
+      if (from_slot)
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, true>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+      else if (full)
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+      else
+        scatter_tile<K, VALS, XF, BLOCK, IPT, false, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+                                                           slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+    }
   }
   // never leave a bulk copy into this CTA's shared memory in flight
   if (tid == 0) {

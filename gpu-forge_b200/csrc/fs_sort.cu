@@ -83,23 +83,39 @@ int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
     if (e_ != cudaSuccess) return cuda_fail((s), e_, #call);   \
   } while (0)
 
-// Scatter tile shapes (threads x keys per thread) and resident CTAs per SM.
-// Shared memory per CTA = 2 bulk-copy slots + staging + 8 KiB of warp digit
-// counters: u32 keys 40+8 KiB (3 CTAs/SM), u32 pairs / u64 keys 96+8 KiB and
-// u64 pairs 72+8 KiB (2 CTAs/SM).
-template <typename K, bool VALS> struct TileCfg;
-template <> struct TileCfg<uint32_t, false> {
+// Scatter tile shapes (threads x keys per thread, resident CTAs per SM).
+// StableCfg ranks with the ballot multisplit (every pass of argsort / pairs,
+// and the passes after the first of a keys-only sort); UnstableCfg ranks
+// with one shared atomic per key (the first executed pass of a keys-only
+// sort).  Measured on B200 with 2^30 u32 keys: stable 256x16 at 3 CTAs/SM
+// 4.85 ms/pass, unstable 256x24 at 2 CTAs/SM 2.72 ms/pass.
+template <typename K, bool VALS> struct StableCfg;
+template <> struct StableCfg<uint32_t, false> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 3;
 };
-template <> struct TileCfg<uint32_t, true> {
+template <> struct StableCfg<uint32_t, true> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
 };
-template <> struct TileCfg<uint64_t, false> {
+template <> struct StableCfg<uint64_t, false> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
 };
-template <> struct TileCfg<uint64_t, true> {
+template <> struct StableCfg<uint64_t, true> {
   static constexpr int BLOCK = 256, IPT = 8, MINB = 2;
 };
+template <typename K> struct UnstableCfg;
+template <> struct UnstableCfg<uint32_t> {
+  static constexpr int BLOCK = 256, IPT = 24, MINB = 2;
+};
+template <> struct UnstableCfg<uint64_t> {
+  static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
+};
+template <typename C> constexpr uint64_t tile_of() { return (uint64_t)C::BLOCK * C::IPT; }
+constexpr uint64_t gcd64(uint64_t a, uint64_t b) { return b ? gcd64(b, a % b) : a; }
+constexpr uint64_t lcm64(uint64_t a, uint64_t b) { return a / gcd64(a, b) * b; }
+
+// Slices per SM: a multiple of 2, 3 and 4 so the scatter (2 or 3 CTAs/SM) and
+// histogram/count (4 CTAs/SM) grids split the slices evenly.
+constexpr int SLICES_PER_SM = 12;
 
 constexpr int HIST_BLOCK = 512;  // histogram / count kernels: more loads in flight per SM
 
@@ -184,17 +200,16 @@ int blocks_per_sm(fs_sorter* s, Kern k, int block, size_t smem) {
 // Resident CTAs per SM of a scatter instantiation (cached per process; every
 // device here is the same architecture).  Sets the kernel's shared-memory
 // limit on the current device the first time; allocates nothing.
-template <typename K, bool VALS, int XF, typename D>
+template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int scatter_occupancy(const Exec& e) {
-  using T = TileCfg<K, VALS>;
-  using Ly = ScatterLayout<K, VALS, T::BLOCK, T::IPT, D::STAGE>;
-  auto kern = k_scatter<K, VALS, XF, T::BLOCK, T::IPT, T::MINB, D>;
+  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE>;
+  auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D>;
   static int configured_mask = 0;  // bit per device (the attribute is per context)
   static int bps = 0;
   if (!(configured_mask & (1 << (e.device & 31)))) {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES);
     if (err != cudaSuccess) return -cuda_fail(e.s, err, "cudaFuncSetAttribute");
-    const int b = blocks_per_sm(e.s, kern, T::BLOCK, Ly::BYTES);
+    const int b = blocks_per_sm(e.s, kern, C::BLOCK, Ly::BYTES);
     if (b < 0) return b;
     bps = b;
     configured_mask |= 1 << (e.device & 31);
@@ -202,60 +217,78 @@ int scatter_occupancy(const Exec& e) {
   return bps;
 }
 
-// Cut n keys into at most (resident scatter CTAs) contiguous slices of whole
-// tiles.
-template <typename K, bool VALS, int XF, typename D>
-int make_slices(const Exec& e, uint64_t n, Slices* sl) {
-  using T = TileCfg<K, VALS>;
-  constexpr uint64_t TILE = (uint64_t)T::BLOCK * T::IPT;
-  const int bps = scatter_occupancy<K, VALS, XF, D>(e);
+template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
+int launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
+  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE>;
+  const int bps = scatter_occupancy<K, VALS, XF, C, MODE, D>(e);
   if (bps < 0) return -bps;
-  const uint64_t tiles = (n + TILE - 1) / TILE;
   const uint64_t cap = (uint64_t)bps * e.sm_count;
-  const uint64_t tps = (tiles + cap - 1) / cap;
-  sl->keys_per_slice = tps * TILE;
-  sl->count = (uint32_t)((tiles + tps - 1) / tps);
+  const unsigned grid = (unsigned)(sl.count < cap ? sl.count : cap);
+  k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D><<<grid, C::BLOCK, Ly::BYTES, e.stream>>>(
+      e.ctl, pass, n, sl, e.offsets, e.timeout_ns, dfn, gpos_base);
   return FS_OK;
 }
 
-template <typename K, bool VALS, int XF, typename D>
-void launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
-  using T = TileCfg<K, VALS>;
-  using Ly = ScatterLayout<K, VALS, T::BLOCK, T::IPT, D::STAGE>;
-  k_scatter<K, VALS, XF, T::BLOCK, T::IPT, T::MINB, D><<<sl.count, T::BLOCK, Ly::BYTES, e.stream>>>(
-      e.ctl, pass, n, sl, e.offsets, e.timeout_ns, dfn, gpos_base);
+// Cut n keys into contiguous slices of whole `unit`-key blocks (a multiple of
+// every tile size used on them), about SLICES_PER_SM per SM.
+Slices make_slices(const Exec& e, uint64_t n, uint64_t unit) {
+  const uint64_t units = (n + unit - 1) / unit;
+  const uint64_t target = (uint64_t)SLICES_PER_SM * e.sm_count;
+  const uint64_t ups = (units + target - 1) / target;  // units per slice
+  Slices sl{};
+  sl.keys_per_slice = ups * unit;
+  sl.count = (uint32_t)((units + ups - 1) / ups);
+  return sl;
+}
+
+// Grid of the histogram / count kernels: 4 CTAs of HIST_BLOCK threads per SM.
+unsigned stream_grid(const Exec& e, const Slices& sl) {
+  const uint64_t cap = (uint64_t)4 * e.sm_count;
+  return (unsigned)(sl.count < cap ? sl.count : cap);
 }
 
 template <typename K, int XF>
 int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launches) {
   constexpr int P = (int)sizeof(K);
   const uint64_t n = a.n;
+  const unsigned sg = stream_grid(e, sl);
   if (e.s) e.s->ev_used = 0;
   // 1. histograms of every digit (global + per slice)
   t_begin(e);
   if ((reinterpret_cast<uintptr_t>(a.kin) & 15) == 0)
     k_upfront_hist<K, XF, HIST_BLOCK, true>
-        <<<sl.count, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
   else
     k_upfront_hist<K, XF, HIST_BLOCK, false>
-        <<<sl.count, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
   t_end(e);
   // 2. plan
   t_begin(e);
   k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
   t_end(e);
   // 3. passes: count (not for the first executed pass), slice scan, scatter
+  int nl = 2;
   for (int p = 0; p < P; ++p) {
     t_begin(e);
-    k_count<K, HIST_BLOCK><<<sl.count, HIST_BLOCK, 0, e.stream>>>(e.ctl, p, n, sl, e.counts);
-    k_slice_scan<<<1, RADIX, 0, e.stream>>>(e.ctl, p, P, sl, e.slice_hist, e.counts, e.offsets);
+    k_count<K, HIST_BLOCK><<<sg, HIST_BLOCK, 0, e.stream>>>(e.ctl, p, n, sl, e.counts);
+    k_slice_scan<<<1, RADIX * SCAN_LANES, 0, e.stream>>>(e.ctl, p, P, sl, e.slice_hist, e.counts, e.offsets);
     t_end(e);
     t_begin(e);
-    if (a.has_vals)
-      launch_scatter<K, true, XF>(e, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
-    else
-      launch_scatter<K, false, XF>(e, p, n, sl, RadixDigit{p * RADIX_BITS}, 0ull);
+    const RadixDigit dg{p * RADIX_BITS};
+    int rc;
+    if (a.has_vals) {
+      rc = launch_scatter<K, true, XF, StableCfg<K, true>, SCATTER_ANY>(e, p, n, sl, dg, 0ull);
+      nl += 3;
+    } else if (a.unstable_first) {
+      rc = launch_scatter<K, false, XF, UnstableCfg<K>, SCATTER_UNSTABLE>(e, p, n, sl, dg, 0ull);
+      if (!rc) rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_STABLE>(e, p, n, sl, dg, 0ull);
+      nl += 4;
+    } else {
+      rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_ANY>(e, p, n, sl, dg, 0ull);
+      nl += 3;
+    }
     t_end(e);
+    if (rc) return rc;
   }
   // 4. finalize
   uint64_t fb = (n + 255) / 256;
@@ -263,27 +296,24 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
   t_begin(e);
   k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, e.stream>>>(e.ctl, n, e.err_out);
   t_end(e);
-  if (launches) *launches = 3 + 3 * P;
+  if (launches) *launches = nl + 1;
   FS_CUDA(e.s, cudaGetLastError());
   return FS_OK;
 }
 
-// Slice geometry for (dtype, n, payload).
-int dispatch_slices(const Exec& e, int dtype, uint64_t n, bool vals, Slices* sl) {
+// Slice geometry for (dtype, n, payload, first-pass rank method).
+Slices dispatch_slices(const Exec& e, int dtype, uint64_t n, bool vals, bool unstable_first) {
   const bool w = dtype >= FS_U64;
-  const int xf = dtype % 3;
-  if (!w && !vals) return xf == 0 ? make_slices<uint32_t, false, XF_NONE, RadixDigit>(e, n, sl)
-                                  : xf == 1 ? make_slices<uint32_t, false, XF_SIGN, RadixDigit>(e, n, sl)
-                                            : make_slices<uint32_t, false, XF_FLOAT, RadixDigit>(e, n, sl);
-  if (!w && vals) return xf == 0 ? make_slices<uint32_t, true, XF_NONE, RadixDigit>(e, n, sl)
-                                 : xf == 1 ? make_slices<uint32_t, true, XF_SIGN, RadixDigit>(e, n, sl)
-                                           : make_slices<uint32_t, true, XF_FLOAT, RadixDigit>(e, n, sl);
-  if (w && !vals) return xf == 0 ? make_slices<uint64_t, false, XF_NONE, RadixDigit>(e, n, sl)
-                                 : xf == 1 ? make_slices<uint64_t, false, XF_SIGN, RadixDigit>(e, n, sl)
-                                           : make_slices<uint64_t, false, XF_FLOAT, RadixDigit>(e, n, sl);
-  return xf == 0 ? make_slices<uint64_t, true, XF_NONE, RadixDigit>(e, n, sl)
-                 : xf == 1 ? make_slices<uint64_t, true, XF_SIGN, RadixDigit>(e, n, sl)
-                           : make_slices<uint64_t, true, XF_FLOAT, RadixDigit>(e, n, sl);
+  uint64_t unit;
+  if (vals)
+    unit = w ? tile_of<StableCfg<uint64_t, true>>() : tile_of<StableCfg<uint32_t, true>>();
+  else if (w)
+    unit = unstable_first ? lcm64(tile_of<StableCfg<uint64_t, false>>(), tile_of<UnstableCfg<uint64_t>>())
+                          : tile_of<StableCfg<uint64_t, false>>();
+  else
+    unit = unstable_first ? lcm64(tile_of<StableCfg<uint32_t, false>>(), tile_of<UnstableCfg<uint32_t>>())
+                          : tile_of<StableCfg<uint32_t, false>>();
+  return make_slices(e, n, unit);
 }
 
 int dispatch_enqueue(const Exec& e, int dtype, const PlanArgs& a, const Slices& sl, int* launches) {
@@ -320,10 +350,9 @@ Exec exec_of(fs_sorter* s) {
 // The sorter's path: size the slices, grow its scratch, enqueue.
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   Exec e = exec_of(s);
-  Slices sl{};
-  int rc = dispatch_slices(e, dtype, a.n, a.has_vals != 0, &sl);
+  const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);
+  int rc = ensure_slice_buffers(s, sl, a.passes);
   if (rc) return rc;
-  if ((rc = ensure_slice_buffers(s, sl, a.passes))) return rc;
   e.slice_hist = static_cast<uint32_t*>(s->slice_hist);
   e.counts = static_cast<uint32_t*>(s->counts);
   e.offsets = static_cast<uint32_t*>(s->offsets);
@@ -340,10 +369,9 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
   using D = SplitterDigit<K, XF>;
   const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
   Exec e = exec_of(s);
-  Slices sl{};
-  int rc = make_slices<K, false, XF, D>(e, n, &sl);
+  const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
+  int rc = ensure_slice_buffers(s, sl, 1);
   if (rc) return rc;
-  if ((rc = ensure_slice_buffers(s, sl, 1))) return rc;
   e.slice_hist = static_cast<uint32_t*>(s->slice_hist);
   e.counts = static_cast<uint32_t*>(s->counts);
   e.offsets = static_cast<uint32_t*>(s->offsets);
@@ -358,11 +386,11 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
   a.key_bytes = (int)sizeof(K);
   a.counts_out = counts_out;
   a.ncounts = nsplit + 1;
-  k_bucket_hist<K, XF, HIST_BLOCK><<<sl.count, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(keys_in), n, e.ctl,
-                                                                         sl, e.slice_hist, dfn, gpos_base);
+  k_bucket_hist<K, XF, HIST_BLOCK><<<stream_grid(e, sl), HIST_BLOCK, 0, e.stream>>>(
+      static_cast<const K*>(keys_in), n, e.ctl, sl, e.slice_hist, dfn, gpos_base);
   k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
-  k_slice_scan<<<1, RADIX, 0, e.stream>>>(e.ctl, 0, 1, sl, e.slice_hist, e.counts, e.offsets);
-  launch_scatter<K, false, XF>(e, 0, n, sl, dfn, gpos_base);
+  k_slice_scan<<<1, RADIX * SCAN_LANES, 0, e.stream>>>(e.ctl, 0, 1, sl, e.slice_hist, e.counts, e.offsets);
+  if ((rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base))) return rc;
   uint64_t fb = (n + 255) / 256;
   const uint64_t fcap = (uint64_t)e.sm_count * 4;
   k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, e.stream>>>(e.ctl, n, e.err_out);
@@ -576,6 +604,7 @@ int fs_sort_keys(fs_sorter* s, int dtype, void* keys, uint64_t n, int sync) {
   a.has_vals = 0;
   a.write_keys = 1;
   a.key_bytes = kb;
+  a.unstable_first = 1;  // keys only: equal keys are identical bits
   if ((rc = dispatch(s, dtype, a))) return rc;
   return finish(s, sync);
 }
@@ -721,6 +750,7 @@ int fs_sort_keys_copy(fs_sorter* s, int dtype, const void* keys_in, void* keys_o
   a.has_vals = 0;
   a.write_keys = 1;
   a.key_bytes = kb;
+  a.unstable_first = 1;  // keys only: equal keys are identical bits
   if ((rc = dispatch(s, dtype, a))) return rc;
   return finish(s, sync);
 }
@@ -802,8 +832,7 @@ int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream) {
   e.counts = reinterpret_cast<uint32_t*>(base + NA_OFF_COUNTS);
   e.offsets = reinterpret_cast<uint32_t*>(base + NA_OFF_OFFSETS);
   e.s = nullptr;
-  Slices sl{};
-  if ((rc = dispatch_slices(e, dtype, n, false, &sl))) return rc;
+  const Slices sl = dispatch_slices(e, dtype, n, false, true);
   if (sl.count > NA_MAX_SLICES) return fail(nullptr, FS_E_INVALID, "internal: %u slices exceed the fixed scratch", sl.count);
   // The arena keeps the previous call's contents: the histogram accumulates
   // from zero and the error words must start clear.
@@ -819,6 +848,7 @@ int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream) {
   a.has_vals = 0;
   a.write_keys = 1;
   a.key_bytes = kb;
+  a.unstable_first = 1;  // keys only: equal keys are identical bits
   if ((rc = dispatch_enqueue(e, dtype, a, sl, nullptr))) return rc;
   int dev_err = 0;
   ce = cudaMemcpyAsync(&dev_err, e.err_out, sizeof(int), cudaMemcpyDeviceToHost, e.stream);
