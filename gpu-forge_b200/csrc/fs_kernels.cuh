@@ -30,7 +30,7 @@
 #include "fs_device.cuh"
 
 #ifndef FS_RANK_BALLOT
-#define FS_RANK_BALLOT 2
+#define FS_RANK_BALLOT 3
 #endif
 
 namespace fs {
@@ -121,40 +121,6 @@ struct SplitterDigit {
   }
 };
 
-// Add one key per lane of a warp to per-digit counters h[pass][digit] for the
-// P lowest digits.  All lanes call this together.  When the whole warp
-// shares a pass's digit (small integers, Zipf, all-equal keys), one lane adds
-// the warp count instead of 32 same-address atomics.
-template <typename K, int P>
-__device__ __forceinline__ void warp_count_digits(uint32_t (*h)[RADIX], K x, bool valid) {
-  const uint32_t lane = threadIdx.x & 31;
-  const uint32_t active = __ballot_sync(0xffffffffu, valid);
-  if (!valid) return;
-  const int src = __ffs(active) - 1;
-  const K diff = x ^ __shfl_sync(active, x, src);
-  uint32_t dlo = __reduce_or_sync(active, (uint32_t)diff);
-  uint32_t dhi = 0xffffffffu;
-  if constexpr (sizeof(K) == 8) dhi = __reduce_or_sync(active, (uint32_t)((uint64_t)diff >> 32));
-  if constexpr (P < 4) dlo |= 0xffffffffu << (8 * P);  // bytes beyond P do not count
-  // a byte of dlo/dhi is zero <=> the whole warp shares that digit
-  const bool any_uniform =
-      (((dlo - 0x01010101u) & ~dlo & 0x80808080u) | ((dhi - 0x01010101u) & ~dhi & 0x80808080u)) != 0u;
-  if (!any_uniform) {
-#pragma unroll
-    for (int p = 0; p < P; ++p) atomicAdd(&h[p][digit_of(x, RADIX_BITS * p)], 1u);
-  } else {
-#pragma unroll
-    for (int p = 0; p < P; ++p) {
-      const uint32_t dbyte = (p < 4 ? (dlo >> (8 * p)) : (dhi >> (8 * (p - 4)))) & 0xffu;
-      const uint32_t d = digit_of(x, RADIX_BITS * p);
-      if (dbyte)
-        atomicAdd(&h[p][d], 1u);
-      else if (lane == (uint32_t)src)
-        atomicAdd(&h[p][d], (uint32_t)__popc(active));
-    }
-  }
-}
-
 // Visit the keys of [lo, hi) with the CTA's threads in coalesced order, 16-byte
 // vector loads when `keys` is 16-byte aligned (VEC), four loads (64 bytes) in
 // flight per thread to cover HBM latency; f(key, valid) is called by whole
@@ -209,24 +175,40 @@ __global__ void __launch_bounds__(BLOCK)
     k_upfront_hist(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
                    uint32_t* __restrict__ slice_hist /* [count][P][RADIX] */) {
   constexpr int P = (int)sizeof(K);
-  __shared__ uint32_t h[P][RADIX];
-  for (int i = threadIdx.x; i < P * RADIX; i += BLOCK) (&h[0][0])[i] = 0;
+  // REP copies of the P histograms (one per group of warps) cut contention
+  constexpr int REP = sizeof(K) == 4 ? 4 : 2;
+  constexpr int WPR = (BLOCK / 32) / REP;  // warps per copy
+  __shared__ uint32_t hr[REP][P][RADIX];
+  uint32_t(*h)[RADIX] = hr[(threadIdx.x >> 5) / WPR];
+  for (int i = threadIdx.x; i < REP * P * RADIX; i += BLOCK) (&hr[0][0][0])[i] = 0;
   __syncthreads();
+  const RadixDigit dg{0};
   for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
     const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
     const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
-    for_each_key<K, BLOCK, VEC>(keys, lo, hi,
-                                [&](K x, bool valid) { warp_count_digits<K, P>(h, to_ordered<K, XF>(x), valid); });
+    // one shared atomic per digit per key
+    for_each_key<K, BLOCK, VEC>(keys, lo, hi, [&](K x, bool valid) {
+      if (valid) {
+        const K o = to_ordered<K, XF>(x);
+#pragma unroll
+        for (int p = 0; p < P; ++p) atomicAdd(&h[p][RadixDigit{p * RADIX_BITS}(o, 0)], 1u);
+      }
+    });
     __syncthreads();
     uint32_t* out = slice_hist + (size_t)c * P * RADIX;
     for (int b = threadIdx.x; b < P * RADIX; b += BLOCK) {
-      const uint32_t v = (&h[0][0])[b];
+      uint32_t v = 0;
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        v += (&hr[r][0][0])[b];
+        (&hr[r][0][0])[b] = 0;
+      }
       out[b] = v;
-      (&h[0][0])[b] = 0;
       if (v) atomicAdd(&(&ctl->hist[0][0])[b], (unsigned long long)v);
     }
     __syncthreads();
   }
+  (void)dg;
 }
 
 // --------------------------------------------------------------------------
@@ -372,12 +354,18 @@ __global__ void __launch_bounds__(BLOCK)
   const uint32_t flags = ctl->pass[pass].flags;
   if (!(flags & PD_EXEC) || (flags & PD_FIRST)) return;
   const K* keys = static_cast<const K*>(ctl->pass[pass].kin);
-  __shared__ uint32_t h[1][RADIX];
-  for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[0][i] = 0;
+  // one histogram per warp: no atomic contention between warps
+  constexpr int WARPS = BLOCK / 32;
+  __shared__ uint32_t hw[WARPS][RADIX];
+  uint32_t* h = hw[threadIdx.x >> 5];
+  for (int i = threadIdx.x; i < WARPS * RADIX; i += BLOCK) (&hw[0][0])[i] = 0;
   __syncthreads();
   const int shift = pass * RADIX_BITS;
-  // count the pass digit only: it becomes the lowest byte of a 32-bit word
-  auto f = [&](K x, bool valid) { warp_count_digits<uint32_t, 1>(h, (uint32_t)(x >> shift) & 0xffu, valid); };
+  // one shared atomic per key (skewed digits only slow the warp that meets them)
+  const RadixDigit dg{shift};
+  auto f = [&](K x, bool valid) {
+    if (valid) atomicAdd(&h[dg(x, 0)], 1u);
+  };
   const bool vec = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
   for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
     const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
@@ -388,8 +376,13 @@ __global__ void __launch_bounds__(BLOCK)
       for_each_key<K, BLOCK, false>(keys, lo, hi, f);
     __syncthreads();
     for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
-      counts[(size_t)c * RADIX + b] = h[0][b];
-      h[0][b] = 0;
+      uint32_t v = 0;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) {
+        v += hw[w][b];
+        hw[w][b] = 0;
+      }
+      counts[(size_t)c * RADIX + b] = v;
     }
     __syncthreads();
   }
@@ -450,14 +443,19 @@ __global__ void __launch_bounds__(RADIX * SCAN_LANES)
 //      consecutive output positions (+ inverse transform on the last pass)
 // --------------------------------------------------------------------------
 
-// Lanes of the warp holding the same 8-bit digit as this lane (invalid lanes
-// of a partial tile match nobody but themselves).  Eight ballots over the
-// digit's bits measured 2x faster on B200 than the hardware match
-// instruction at 16 keys per thread (FS_RANK_BALLOT=0 selects
-// __match_any_sync).
+// Stable warp ranking.  Three ways to find the lanes that share this lane's
+// digit were measured on B200 (2^30 u32 keys, 256x16 tiles, stable pass):
+//   FS_RANK_BALLOT=3 (default): owner election through a per-warp byte per
+//     digit, then five ballots over the owner's lane bits  3.96 ms/pass
+//   FS_RANK_BALLOT=2: eight ballots over the digit's bits  4.75 ms/pass
+//   FS_RANK_BALLOT=0: __match_any_sync                      ~2x slower again
+// warp_peers serves 2 and 0; owner election is written out in scatter_tile.
+// Invalid lanes of a partial tile match nobody but themselves.
 template <bool FULL>
 __device__ __forceinline__ uint32_t warp_peers(uint32_t d, bool valid) {
-#if FS_RANK_BALLOT == 2
+#if FS_RANK_BALLOT == 0
+  return __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
+#else
   // lanes whose digit differs from mine in some bit, then complement
   uint32_t diff = FULL ? 0u : ~__ballot_sync(0xffffffffu, valid);
 #pragma unroll
@@ -466,17 +464,6 @@ __device__ __forceinline__ uint32_t warp_peers(uint32_t d, bool valid) {
     diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
   }
   return valid ? ~diff : (1u << (threadIdx.x & 31));
-#elif FS_RANK_BALLOT
-  uint32_t peers = FULL ? 0xffffffffu : __ballot_sync(0xffffffffu, valid);
-#pragma unroll
-  for (int b = 0; b < RADIX_BITS; ++b) {
-    const bool bit = (d >> b) & 1u;
-    const uint32_t bal = __ballot_sync(0xffffffffu, bit);
-    peers &= bit ? bal : ~bal;
-  }
-  return valid ? peers : (1u << (threadIdx.x & 31));
-#else
-  return __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
 #endif
 }
 
@@ -489,16 +476,18 @@ struct ScatterLayout {
   static constexpr size_t VALB = VALS ? (size_t)TILE * 4 : 0;
   static constexpr size_t SLOT = KEYS + VALB;  // one bulk-copy slot (keys | vals)
   // dynamic shared memory:
-  //   [slot 0 | slot 1 | stage keys | stage vals | warp digit counters | staged digits]
+  //   [slot 0 | slot 1 | stage keys | stage vals | warp digit counters |
+  //    warp digit owners | staged digits]
   static constexpr size_t STAGE_OFF = 2 * SLOT;
   static constexpr size_t CNT_OFF = STAGE_OFF + KEYS + VALB;
-  static constexpr size_t DIG_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;
+  static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;  // per-warp digit owners
+  static constexpr size_t DIG_OFF = REP_OFF + (size_t)WARPS * RADIX;
   static constexpr size_t BYTES = DIG_OFF + (STAGE_DIG ? (size_t)TILE : 0);
   static_assert(BLOCK >= RADIX && BLOCK % 32 == 0, "one thread per digit needed");
   static_assert(KEYS % 16 == 0, "bulk copies move multiples of 16 bytes");
 };
 
-template <typename K, bool VALS, int XF, int BLOCK, int IPT, bool FULL, bool FROM_SLOT, typename D>
+template <typename K, bool VALS, int XF, int BLOCK, int IPT, bool FULL, bool FROM_SLOT, bool UNSTABLE, typename D>
 __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_t tile_n, const uint64_t n,
                                              const uint32_t flags, const K* __restrict__ kin,
                                              K* __restrict__ kout, const uint32_t* __restrict__ vin,
@@ -518,6 +507,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   uint32_t* cnt = reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF);
   uint8_t* sdig = dsm + Ly::DIG_OFF;
   uint32_t* wcnt = cnt + warp * RADIX;
+  uint8_t* wrep = dsm + Ly::REP_OFF + warp * RADIX;
 
   // ---- A. keys -> registers ----------------------------------------------------
   K key[IPT];
@@ -541,7 +531,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   // for that digit, the group's highest lane advances it.  After the loop
   // the counters hold the warp's per-digit totals.
   uint32_t rank[IPT];
-  if (flags & PD_UNSTABLE) {
+  if constexpr (UNSTABLE) {
     // Keys-only first pass: no earlier order to keep, so any order among
     // equal digits is correct -- one shared atomic per key ranks it.
 #pragma unroll
@@ -549,6 +539,33 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       const bool valid = FULL || (wofs + k * 32) < tile_n;
       const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
       rank[k] = valid ? atomicAdd(&wcnt[d], 1u) : 0u;
+    }
+  } else if constexpr (FS_RANK_BALLOT == 3) {
+    // Owner election: every lane writes its lane number into its digit's
+    // byte; after the warp syncs, all lanes of a digit read the same owner
+    // (whichever write landed).  Lanes sharing a digit are then exactly the
+    // lanes sharing an owner: five ballots over the owner's bits instead of
+    // eight over the digit's.  The owner advances the running count.
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      const bool valid = FULL || (wofs + k * 32) < tile_n;
+      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
+      if (valid) wrep[d] = (uint8_t)lane;
+      __syncwarp();
+      const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
+      uint32_t diff = 0;
+#pragma unroll
+      for (int b = 0; b < 5; ++b) {
+        const uint32_t bit = (own >> b) & 1u;
+        diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
+      }
+      const uint32_t peers = ~diff;
+      uint32_t old = 0;
+      if (valid) old = wcnt[d];
+      __syncwarp();
+      if (valid && lane == own) wcnt[d] = old + __popc(peers);
+      __syncwarp();
+      rank[k] = old + __popc(peers & lt_mask);
     }
   } else {
 #pragma unroll
@@ -652,7 +669,8 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
 
 // Which passes a scatter instantiation takes (the plan decides on the
 // device whether a pass ranks stably, so both instantiations are launched and
-// the one that does not match exits at once).
+// the one that does not match exits at once).  The rank method is compiled
+// in: SCATTER_UNSTABLE ranks with shared atomics, the others with ballots.
 enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1, SCATTER_STABLE = 2 };
 
 // CTAs loop over slices (c = blockIdx.x, +gridDim.x, ...); tiles of a slice
@@ -737,13 +755,13 @@ __global__ void __launch_bounds__(BLOCK, MINB)
       }
       const unsigned char* slot = dsm + (size_t)s * Ly::SLOT;
       if (from_slot)
-        scatter_tile<K, VALS, XF, BLOCK, IPT, true, true>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
       else if (full)
-        scatter_tile<K, VALS, XF, BLOCK, IPT, true, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
                                                           slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
       else
-        scatter_tile<K, VALS, XF, BLOCK, IPT, false, false>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
+        scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
                                                            slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
     }
   }

@@ -88,10 +88,23 @@ int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
 // and the passes after the first of a keys-only sort); UnstableCfg ranks
 // with one shared atomic per key (the first executed pass of a keys-only
 // sort).  Measured on B200 with 2^30 u32 keys: stable 256x16 at 3 CTAs/SM
-// 4.85 ms/pass, unstable 256x24 at 2 CTAs/SM 2.72 ms/pass.
+// 3.96 ms/pass (256x12 at 4: 4.67, 256x24 at 2: 4.29), unstable 256x32 at
+// 2 CTAs/SM 2.58 ms/pass (256x24 at 2: 2.79).
+#ifndef FS_U32_STABLE_IPT
+#define FS_U32_STABLE_IPT 16
+#endif
+#ifndef FS_U32_STABLE_MINB
+#define FS_U32_STABLE_MINB 3
+#endif
+#ifndef FS_U32_UNSTABLE_IPT
+#define FS_U32_UNSTABLE_IPT 32
+#endif
+#ifndef FS_U32_UNSTABLE_MINB
+#define FS_U32_UNSTABLE_MINB 2
+#endif
 template <typename K, bool VALS> struct StableCfg;
 template <> struct StableCfg<uint32_t, false> {
-  static constexpr int BLOCK = 256, IPT = 16, MINB = 3;
+  static constexpr int BLOCK = 256, IPT = FS_U32_STABLE_IPT, MINB = FS_U32_STABLE_MINB;
 };
 template <> struct StableCfg<uint32_t, true> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
@@ -104,7 +117,7 @@ template <> struct StableCfg<uint64_t, true> {
 };
 template <typename K> struct UnstableCfg;
 template <> struct UnstableCfg<uint32_t> {
-  static constexpr int BLOCK = 256, IPT = 24, MINB = 2;
+  static constexpr int BLOCK = 256, IPT = FS_U32_UNSTABLE_IPT, MINB = FS_U32_UNSTABLE_MINB;
 };
 template <> struct UnstableCfg<uint64_t> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
