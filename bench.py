@@ -296,7 +296,7 @@ def run_ours(args):
                        "ms": round(first_avg, 4), "frac": frac(alg_bytes_pass, first_avg)},
         "count": {"kernel": "k_count + k_slice_scan (per-slice digit counts, reads every key)",
                   "ms": round(count_avg, 4), "frac": frac(m * kb, count_avg)},
-        "hist": {"kernel": "k_upfront_hist (all digits, reads every key)",
+        "hist": {"kernel": "k_first_count (digit-0 slice counts + OR/AND of all keys, reads every key)",
                  "ms": round(hist_ms, 4), "frac": frac(m * kb, hist_ms)},
         "sort_alg_bytes_per_key": kb * (1 + 2 * P),
         "sort_frac": frac(m * kb * (1 + 2 * P), ms),

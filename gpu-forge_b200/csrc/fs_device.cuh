@@ -3,6 +3,8 @@
 // device-resident control block the host enqueues against.
 #pragma once
 
+#include <cstddef>
+
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -121,8 +123,10 @@ constexpr int DEV_ERR_TIMEOUT = 1;  // a bounded wait (bulk-copy barrier) ran ou
 constexpr int DEV_ERR_BOUNDS = 2;  // a scatter position fell outside [0, n)
 
 struct SortCtl {
-  unsigned long long hist[MAX_PASSES][RADIX];  // upfront histogram, all digits
-  unsigned long long base[MAX_PASSES][RADIX];  // exclusive bucket starts
+  // Accumulators, cleared before every sort (the first CTL_ACCUM_BYTES):
+  unsigned long long hist[MAX_PASSES][RADIX];  // global digit counts of each pass
+  unsigned long long kor;    // OR of all ordered keys
+  unsigned long long kandn;  // OR of all complemented ordered keys (= ~AND)
   PassDesc pass[MAX_PASSES];
   FinalDesc fin;
   int err;  // first device-side failure (DEV_ERR_*)
@@ -138,6 +142,10 @@ struct Slices {
 
 // Per-sort arguments of the plan kernel: where the keys and payload come from
 // and where they must end up.
+// Bytes of SortCtl that are zeroed before every sort: hist, kor, kandn.
+constexpr size_t CTL_ACCUM_BYTES = sizeof(unsigned long long) * (MAX_PASSES * RADIX + 2);
+static_assert(offsetof(SortCtl, pass) == CTL_ACCUM_BYTES, "accumulators lead SortCtl");
+
 struct PlanArgs {
   uint64_t n;
   const void* kin;   // pass-1 key source (may be const user input)
@@ -153,6 +161,9 @@ struct PlanArgs {
   unsigned long long* counts_out;  // optional copy of pass-0 digit counts
   int ncounts;                     // entries of counts_out
   int unstable_first;              // keys-only LSD sort: first pass may reorder ties
+  int trivial_from_bits;           // 1: a pass is trivial when kor/kandn show its
+                                   // digit never varies; 0: when hist[0] has one
+                                   // digit holding all n keys (single-pass plans)
 };
 
 }  // namespace fs

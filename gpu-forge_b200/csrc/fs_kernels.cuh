@@ -1,14 +1,12 @@
 // fs_kernels.cuh -- the sm_100a kernels of one sort.
 //
 // Per sort (P = key bytes, one 8-bit digit per pass, LSD):
-//   k_upfront_hist   one read of the keys -> global histograms of ALL digits,
-//                    and per-slice histograms of all digits
-//   k_plan           bucket starts per pass, trivial-pass detection,
-//                    device-side buffer routing (1 CTA)
+//   k_first_count    one read of the keys -> per-slice counts of digit 0 and
+//                    their totals, OR / AND of all keys (which digits vary)
+//   k_plan           trivial-pass detection, device-side buffer routing
 // per executed pass:
-//   k_count          per-slice counts of this pass's digit (skipped for the
-//                    first executed pass: the upfront slice histograms hold
-//                    them, the input order being unchanged)
+//   k_count          per-slice counts of this pass's digit and their totals
+//                    (pass 0: already counted by k_first_count)
 //   k_slice_scan     per-(slice, digit) global output offsets
 //   k_scatter        CTA c walks slice c tile by tile: warp multisplit rank,
 //                    shared-memory staging by digit, coalesced scatter;
@@ -163,63 +161,83 @@ __device__ __forceinline__ void for_each_key(const K* __restrict__ keys, uint64_
 }
 
 // --------------------------------------------------------------------------
-// Upfront histogram: every digit of every pass from one read of the keys.
-// CTA c reads slice c; it writes its slice histograms (the first executed
-// pass's slice counts) and adds them into the global histograms.
+// First count: one read of the keys gives
+//   - the slice counts of digit 0 of the ordered keys (counts[c][d]) and
+//     their global totals (ctl->hist[0]),
+//   - the OR of the ordered keys and the OR of their complements: a digit
+//     whose bits never vary marks a pass that would be the identity, which the
+//     plan skips before any scatter runs.
+// Later passes count their own digit (k_count) when their input exists, so
+// no pass needs a histogram taken up front; testing for trivial passes needs
+// only the two bitwise reductions.
 // Replaces sort_msd_histogram (shaders/sort.metal:64-142), which counted only
 // the most significant byte, and the per-bucket histograms that
 // sort_inner_fused recomputed (sort.metal:378-769).
 // --------------------------------------------------------------------------
 template <typename K, int XF, int BLOCK, bool VEC>
 __global__ void __launch_bounds__(BLOCK)
-    k_upfront_hist(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
-                   uint32_t* __restrict__ slice_hist /* [count][P][RADIX] */) {
-  constexpr int P = (int)sizeof(K);
-  // REP copies of the P histograms (one per group of warps) cut contention
-  constexpr int REP = sizeof(K) == 4 ? 4 : 2;
-  constexpr int WPR = (BLOCK / 32) / REP;  // warps per copy
-  __shared__ uint32_t hr[REP][P][RADIX];
-  uint32_t(*h)[RADIX] = hr[(threadIdx.x >> 5) / WPR];
-  for (int i = threadIdx.x; i < REP * P * RADIX; i += BLOCK) (&hr[0][0][0])[i] = 0;
+    k_first_count(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
+                  uint32_t* __restrict__ counts /* [count][RADIX] */) {
+  constexpr int WARPS = BLOCK / 32;
+  __shared__ uint32_t hw[WARPS][RADIX];
+  __shared__ uint32_t tot[RADIX];
+  uint32_t* h = hw[threadIdx.x >> 5];
+  for (int i = threadIdx.x; i < WARPS * RADIX; i += BLOCK) (&hw[0][0])[i] = 0;
+  for (int i = threadIdx.x; i < RADIX; i += BLOCK) tot[i] = 0;
   __syncthreads();
+  K kor = 0, kandn = 0;
   const RadixDigit dg{0};
   for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
     const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
     const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
-    // one shared atomic per digit per key
     for_each_key<K, BLOCK, VEC>(keys, lo, hi, [&](K x, bool valid) {
       if (valid) {
         const K o = to_ordered<K, XF>(x);
-#pragma unroll
-        for (int p = 0; p < P; ++p) atomicAdd(&h[p][RadixDigit{p * RADIX_BITS}(o, 0)], 1u);
+        kor |= o;
+        kandn |= ~o;
+        atomicAdd(&h[dg(o, 0)], 1u);
       }
     });
     __syncthreads();
-    uint32_t* out = slice_hist + (size_t)c * P * RADIX;
-    for (int b = threadIdx.x; b < P * RADIX; b += BLOCK) {
+    for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
       uint32_t v = 0;
 #pragma unroll
-      for (int r = 0; r < REP; ++r) {
-        v += (&hr[r][0][0])[b];
-        (&hr[r][0][0])[b] = 0;
+      for (int w = 0; w < WARPS; ++w) {
+        v += hw[w][b];
+        hw[w][b] = 0;
       }
-      out[b] = v;
-      if (v) atomicAdd(&(&ctl->hist[0][0])[b], (unsigned long long)v);
+      counts[(size_t)c * RADIX + b] = v;
+      tot[b] += v;
     }
     __syncthreads();
   }
-  (void)dg;
+  for (int b = threadIdx.x; b < RADIX; b += BLOCK)
+    if (tot[b]) atomicAdd(&ctl->hist[0][b], (unsigned long long)tot[b]);
+  // bitwise reductions: warp, then one atomic pair per warp
+  uint32_t lo_or = __reduce_or_sync(0xffffffffu, (uint32_t)kor);
+  uint32_t lo_an = __reduce_or_sync(0xffffffffu, (uint32_t)kandn);
+  uint32_t hi_or = 0, hi_an = 0;
+  if constexpr (sizeof(K) == 8) {
+    hi_or = __reduce_or_sync(0xffffffffu, (uint32_t)((uint64_t)kor >> 32));
+    hi_an = __reduce_or_sync(0xffffffffu, (uint32_t)((uint64_t)kandn >> 32));
+  } else {
+    hi_an = 0xffffffffu;  // bits above a 32-bit key never count as varying
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicOr(&ctl->kor, ((unsigned long long)hi_or << 32) | lo_or);
+    atomicOr(&ctl->kandn, ((unsigned long long)hi_an << 32) | lo_an);
+  }
 }
 
 // --------------------------------------------------------------------------
 // Bucket histogram of the sample sort's partition pass (one pass, digit =
 // splitter bucket): global counts into ctl->hist[0], slice counts into
-// slice_hist[c][0][*].
+// counts[c][*].
 // --------------------------------------------------------------------------
 template <typename K, int XF, int BLOCK>
 __global__ void __launch_bounds__(BLOCK)
     k_bucket_hist(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
-                  uint32_t* __restrict__ slice_hist, const SplitterDigit<K, XF> dfn, const uint64_t gpos_base) {
+                  uint32_t* __restrict__ counts, const SplitterDigit<K, XF> dfn, const uint64_t gpos_base) {
   __shared__ uint32_t h[RADIX];
   for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[i] = 0;
   __syncthreads();
@@ -229,7 +247,7 @@ __global__ void __launch_bounds__(BLOCK)
     for (uint64_t i = lo + threadIdx.x; i < hi; i += BLOCK)
       atomicAdd(&h[dfn(to_ordered<K, XF>(keys[i]), gpos_base + i)], 1u);
     __syncthreads();
-    uint32_t* out = slice_hist + (size_t)c * RADIX;
+    uint32_t* out = counts + (size_t)c * RADIX;
     for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
       const uint32_t v = h[b];
       out[b] = v;
@@ -241,35 +259,24 @@ __global__ void __launch_bounds__(BLOCK)
 }
 
 // --------------------------------------------------------------------------
-// Plan: per pass, exclusive scan of the digit counts -> global bucket starts;
-// a pass in which one digit holds all n keys is the identity permutation and
-// is skipped.  Then thread 0 routes the executed passes through the key and
-// payload buffers so that the result lands where the caller wants it.
-// Replaces sort_msd_prep (shaders/sort.metal:153-181).  Also zeroes the
-// histogram for the next sort.
+// Plan: which passes run (a pass whose digit is the same for all n keys is the
+// identity permutation and is skipped), then thread 0 routes the executed
+// passes through the key and payload buffers so that the result lands where
+// the caller wants it.  Replaces sort_msd_prep (shaders/sort.metal:153-181).
 // --------------------------------------------------------------------------
 __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanArgs a) {
-  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
-  __shared__ unsigned long long s_wsum[RADIX / 32];
+  const int d = threadIdx.x;
   __shared__ int s_exec[MAX_PASSES];
-  for (int p = 0; p < a.passes; ++p) {
-    const unsigned long long c = ctl->hist[p][d];
-    ctl->hist[p][d] = 0ull;
-    if (p == 0 && a.counts_out != nullptr && d < a.ncounts) a.counts_out[d] = c;
-    unsigned long long x = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) s_wsum[warp] = x;
-    const int trivial = __syncthreads_or(c == a.n);
-    unsigned long long pre = 0;
-    for (int w = 0; w < warp; ++w) pre += s_wsum[w];
-    ctl->base[p][d] = pre + x - c;
-    if (d == 0) s_exec[p] = !trivial;
-    __syncthreads();
+  const unsigned long long c0 = ctl->hist[0][d];
+  if (a.counts_out != nullptr && d < a.ncounts) a.counts_out[d] = c0;
+  if (a.trivial_from_bits) {
+    const unsigned long long varying = ctl->kor & ctl->kandn;
+    if (d < a.passes) s_exec[d] = ((varying >> (RADIX_BITS * d)) & (RADIX - 1)) != 0;
+  } else {
+    const int trivial = __syncthreads_or(c0 == a.n);
+    if (d == 0) s_exec[0] = !trivial;
   }
+  __syncthreads();
   if (d != 0) return;
 
   int m = 0;
@@ -343,28 +350,32 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
 }
 
 // --------------------------------------------------------------------------
-// Count: per-slice histogram of this pass's digit over the pass input (which
-// holds ordered keys: only the first executed pass transforms, and its counts
-// come from k_upfront_hist).
+// Count: per-slice histogram of this pass's digit over the pass input, and its
+// global totals (ctl->hist[pass]).  Pass 0 was counted by k_first_count.  The
+// input holds ordered keys except for the first executed pass, which reads
+// the caller's keys and transforms them as it counts.
 // --------------------------------------------------------------------------
-template <typename K, int BLOCK>
+template <typename K, int XF, int BLOCK>
 __global__ void __launch_bounds__(BLOCK)
     k_count(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
             uint32_t* __restrict__ counts /* [count][RADIX] */) {
   const uint32_t flags = ctl->pass[pass].flags;
-  if (!(flags & PD_EXEC) || (flags & PD_FIRST)) return;
+  if (!(flags & PD_EXEC) || pass == 0) return;
   const K* keys = static_cast<const K*>(ctl->pass[pass].kin);
+  const bool xf = XF != XF_NONE && (flags & PD_XF_IN);
   // one histogram per warp: no atomic contention between warps
   constexpr int WARPS = BLOCK / 32;
   __shared__ uint32_t hw[WARPS][RADIX];
+  __shared__ uint32_t tot[RADIX];
   uint32_t* h = hw[threadIdx.x >> 5];
   for (int i = threadIdx.x; i < WARPS * RADIX; i += BLOCK) (&hw[0][0])[i] = 0;
+  for (int i = threadIdx.x; i < RADIX; i += BLOCK) tot[i] = 0;
   __syncthreads();
   const int shift = pass * RADIX_BITS;
   // one shared atomic per key (skewed digits only slow the warp that meets them)
   const RadixDigit dg{shift};
   auto f = [&](K x, bool valid) {
-    if (valid) atomicAdd(&h[dg(x, 0)], 1u);
+    if (valid) atomicAdd(&h[dg(xf ? to_ordered<K, XF>(x) : x, 0)], 1u);
   };
   const bool vec = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
   for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
@@ -383,39 +394,62 @@ __global__ void __launch_bounds__(BLOCK)
         hw[w][b] = 0;
       }
       counts[(size_t)c * RADIX + b] = v;
+      tot[b] += v;
     }
     __syncthreads();
   }
+  for (int b = threadIdx.x; b < RADIX; b += BLOCK)
+    if (tot[b]) atomicAdd(&ctl->hist[pass][b], (unsigned long long)tot[b]);
 }
 
 // --------------------------------------------------------------------------
-// Slice scan: offsets[c][d] = base[pass][d] + sum of counts[c'][d], c' < c
-// (mod 2^32: positions are < 2^32).  One thread per digit.
+// Slice scan: offsets[c][d] = (keys of digit < d in the whole pass) + (keys
+// of digit d in slices c' < c), mod 2^32 (positions are < 2^32).
+// SCAN_GROUPS CTAs of 32 digits each; in a CTA, warp w owns a run of slices
+// and lane l digit 32*blockIdx.x + l, so every load is one 128-byte row.
 // --------------------------------------------------------------------------
-constexpr int SCAN_LANES = 4;  // threads per digit in k_slice_scan
-__global__ void __launch_bounds__(RADIX * SCAN_LANES)
-    k_slice_scan(SortCtl* __restrict__ ctl, const int pass, const int passes, const Slices sl,
-                 const uint32_t* __restrict__ slice_hist, const uint32_t* __restrict__ counts,
-                 uint32_t* __restrict__ offsets) {
+constexpr int SCAN_GROUPS = RADIX / 32;
+constexpr int SCAN_WARPS = 32;
+__global__ void __launch_bounds__(SCAN_WARPS * 32)
+    k_slice_scan(SortCtl* __restrict__ ctl, const int pass, const Slices sl,
+                 const uint32_t* __restrict__ counts, uint32_t* __restrict__ offsets) {
   const uint32_t flags = ctl->pass[pass].flags;
   if (!(flags & PD_EXEC)) return;
-  const int d = threadIdx.x % RADIX, q = threadIdx.x / RADIX;
-  const bool first = (flags & PD_FIRST) != 0;
-  const uint32_t* src = first ? slice_hist + (size_t)pass * RADIX : counts;
-  const size_t stride = first ? (size_t)passes * RADIX : RADIX;
-  // thread q of digit d owns slices [c0, c1): sum them, exchange the four
-  // sums, then write the running offsets
-  const uint32_t per = (sl.count + SCAN_LANES - 1) / SCAN_LANES;
-  const uint32_t c0 = q * per, c1 = c0 + per < sl.count ? c0 + per : sl.count;
-  uint32_t sum = 0;
-  for (uint32_t c = c0; c < c1; ++c) sum += src[(size_t)c * stride + d];
-  __shared__ uint32_t s_part[SCAN_LANES][RADIX];
-  s_part[q][d] = sum;
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ uint32_t s_part[SCAN_WARPS][32];
+  __shared__ uint32_t s_wtot[RADIX / 32];
+  __shared__ uint32_t s_base[RADIX];
+  // bucket starts: exclusive scan of the pass's global digit counts
+  uint32_t t = 0, x = 0;
+  if (tid < RADIX) {
+    t = (uint32_t)ctl->hist[pass][tid];
+    x = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if ((int)lane >= o) x += y;
+    }
+    if (lane == 31) s_wtot[warp] = x;
+  }
   __syncthreads();
-  uint32_t run = (uint32_t)ctl->base[pass][d];
-  for (int j = 0; j < q; ++j) run += s_part[j][d];
+  if (tid < RADIX) {
+    uint32_t pre = x - t;
+    for (uint32_t w = 0; w < warp; ++w) pre += s_wtot[w];
+    s_base[tid] = pre;
+  }
+  // warp w sums its slices for the CTA's 32 digits
+  const uint32_t d = blockIdx.x * 32 + lane;
+  const uint32_t per = (sl.count + SCAN_WARPS - 1) / SCAN_WARPS;
+  const uint32_t c0 = warp * per < sl.count ? warp * per : sl.count;
+  const uint32_t c1 = c0 + per < sl.count ? c0 + per : sl.count;
+  uint32_t sum = 0;
+  for (uint32_t c = c0; c < c1; ++c) sum += counts[(size_t)c * RADIX + d];
+  s_part[warp][lane] = sum;
+  __syncthreads();
+  uint32_t run = s_base[d];
+  for (uint32_t w = 0; w < warp; ++w) run += s_part[w][lane];
   for (uint32_t c = c0; c < c1; ++c) {
-    const uint32_t v = src[(size_t)c * stride + d];
+    const uint32_t v = counts[(size_t)c * RADIX + d];
     offsets[(size_t)c * RADIX + d] = run;
     run += v;
   }
@@ -480,8 +514,9 @@ struct ScatterLayout {
   //    warp digit owners | staged digits]
   static constexpr size_t STAGE_OFF = 2 * SLOT;
   static constexpr size_t CNT_OFF = STAGE_OFF + KEYS + VALB;
-  static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;  // per-warp digit owners
-  static constexpr size_t DIG_OFF = REP_OFF + (size_t)WARPS * RADIX;
+  static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;  // per-warp digit owners, x2
+  static constexpr size_t MASK_OFF = REP_OFF + 2 * (size_t)WARPS * RADIX;   // per-warp group masks, x2
+  static constexpr size_t DIG_OFF = MASK_OFF + 2 * (size_t)WARPS * 32 * 4;
   static constexpr size_t BYTES = DIG_OFF + (STAGE_DIG ? (size_t)TILE : 0);
   static_assert(BLOCK >= RADIX && BLOCK % 32 == 0, "one thread per digit needed");
   static_assert(KEYS % 16 == 0, "bulk copies move multiples of 16 bytes");
@@ -508,6 +543,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   uint8_t* sdig = dsm + Ly::DIG_OFF;
   uint32_t* wcnt = cnt + warp * RADIX;
   uint8_t* wrep = dsm + Ly::REP_OFF + warp * RADIX;
+  uint32_t* wmask = reinterpret_cast<uint32_t*>(dsm + Ly::MASK_OFF) + warp * 32;
 
   // ---- A. keys -> registers ----------------------------------------------------
   K key[IPT];
@@ -539,6 +575,47 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       const bool valid = FULL || (wofs + k * 32) < tile_n;
       const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
       rank[k] = valid ? atomicAdd(&wcnt[d], 1u) : 0u;
+    }
+  } else if constexpr (FS_RANK_BALLOT == 4 || FS_RANK_BALLOT == 5) {
+    // Owner election with double-buffered owner bytes (iteration k uses
+    // buffer k & 1, so one warp barrier per key orders every reuse); only the
+    // owner reads and advances the running count and shuffles the old value
+    // to its group.  5: the group mask comes from shared atomicOr into the
+    // owner's word instead of five ballots.
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      uint8_t* rp = wrep + (k & 1) * (Ly::WARPS * RADIX);
+      const bool valid = FULL || (wofs + k * 32) < tile_n;
+      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
+      if (valid) rp[d] = (uint8_t)lane;
+      uint32_t peers;
+      if constexpr (FS_RANK_BALLOT == 5) {
+        uint32_t* mp = wmask + (k & 1) * (Ly::WARPS * 32);
+        mp[lane] = 0u;
+        __syncwarp();
+        const uint32_t own = valid ? rp[d] : lane;
+        atomicOr(&mp[own], 1u << lane);
+        __syncwarp();
+        peers = mp[own];
+      } else {
+        __syncwarp();
+        const uint32_t own = valid ? rp[d] : lane;
+        uint32_t diff = 0;
+#pragma unroll
+        for (int b = 0; b < 5; ++b) {
+          const uint32_t bit = (own >> b) & 1u;
+          diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
+        }
+        peers = ~diff;
+      }
+      const uint32_t own = 31u - __clz(peers);  // the group's highest lane leads
+      uint32_t old = 0;
+      if (valid && lane == own) {
+        old = wcnt[d];
+        wcnt[d] = old + __popc(peers);
+      }
+      old = __shfl_sync(0xffffffffu, old, own);
+      rank[k] = old + __popc(peers & lt_mask);
     }
   } else if constexpr (FS_RANK_BALLOT == 3) {
     // Owner election: every lane writes its lane number into its digit's

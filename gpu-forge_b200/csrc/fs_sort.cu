@@ -23,8 +23,6 @@ struct fs_sorter {
   SortCtl* ctl = nullptr;
   int* host_err = nullptr;      // mapped pinned word written by k_finalize
   int* host_err_dev = nullptr;  // its device alias
-  void* slice_hist = nullptr;  // [slices][P][256] u32 from the upfront histogram
-  size_t slice_hist_bytes = 0;
   void* counts = nullptr;      // [slices][256] u32 per-pass slice counts
   size_t counts_bytes = 0;
   void* offsets = nullptr;     // [slices][256] u32 per-pass output offsets
@@ -185,7 +183,6 @@ struct Exec {
   uint64_t timeout_ns;
   SortCtl* ctl;
   int* err_out;
-  uint32_t* slice_hist;  // >= slices * P * 256 words
   uint32_t* counts;      // >= slices * 256 words
   uint32_t* offsets;     // >= slices * 256 words
   fs_sorter* s;
@@ -266,25 +263,28 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
   const uint64_t n = a.n;
   const unsigned sg = stream_grid(e, sl);
   if (e.s) e.s->ev_used = 0;
-  // 1. histograms of every digit (global + per slice)
+  // 1. clear the accumulators; digit-0 slice counts + which digits vary
   t_begin(e);
+  FS_CUDA(e.s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
   if ((reinterpret_cast<uintptr_t>(a.kin) & 15) == 0)
-    k_upfront_hist<K, XF, HIST_BLOCK, true>
-        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
+    k_first_count<K, XF, HIST_BLOCK, true>
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts);
   else
-    k_upfront_hist<K, XF, HIST_BLOCK, false>
-        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.slice_hist);
+    k_first_count<K, XF, HIST_BLOCK, false>
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts);
   t_end(e);
   // 2. plan
+  PlanArgs pa = a;
+  pa.trivial_from_bits = 1;
   t_begin(e);
-  k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
+  k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, pa);
   t_end(e);
-  // 3. passes: count (not for the first executed pass), slice scan, scatter
+  // 3. passes: count (pass 0 was counted above), slice scan, scatter
   int nl = 2;
   for (int p = 0; p < P; ++p) {
     t_begin(e);
-    k_count<K, HIST_BLOCK><<<sg, HIST_BLOCK, 0, e.stream>>>(e.ctl, p, n, sl, e.counts);
-    k_slice_scan<<<1, RADIX * SCAN_LANES, 0, e.stream>>>(e.ctl, p, P, sl, e.slice_hist, e.counts, e.offsets);
+    k_count<K, XF, HIST_BLOCK><<<sg, HIST_BLOCK, 0, e.stream>>>(e.ctl, p, n, sl, e.counts);
+    k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, p, sl, e.counts, e.offsets);
     t_end(e);
     t_begin(e);
     const RadixDigit dg{p * RADIX_BITS};
@@ -341,9 +341,8 @@ int dispatch_enqueue(const Exec& e, int dtype, const PlanArgs& a, const Slices& 
   }
 }
 
-int ensure_slice_buffers(fs_sorter* s, const Slices& sl, int passes) {
-  int rc = grow(s, &s->slice_hist, &s->slice_hist_bytes, (size_t)sl.count * passes * RADIX * 4, false);
-  if (!rc) rc = grow(s, &s->counts, &s->counts_bytes, (size_t)sl.count * RADIX * 4, false);
+int ensure_slice_buffers(fs_sorter* s, const Slices& sl) {
+  int rc = grow(s, &s->counts, &s->counts_bytes, (size_t)sl.count * RADIX * 4, false);
   if (!rc) rc = grow(s, &s->offsets, &s->offsets_bytes, (size_t)sl.count * RADIX * 4, false);
   return rc;
 }
@@ -364,9 +363,8 @@ Exec exec_of(fs_sorter* s) {
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   Exec e = exec_of(s);
   const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);
-  int rc = ensure_slice_buffers(s, sl, a.passes);
+  int rc = ensure_slice_buffers(s, sl);
   if (rc) return rc;
-  e.slice_hist = static_cast<uint32_t*>(s->slice_hist);
   e.counts = static_cast<uint32_t*>(s->counts);
   e.offsets = static_cast<uint32_t*>(s->offsets);
   return dispatch_enqueue(e, dtype, a, sl, &s->last_launches);
@@ -383,9 +381,8 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
   const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
   Exec e = exec_of(s);
   const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
-  int rc = ensure_slice_buffers(s, sl, 1);
+  int rc = ensure_slice_buffers(s, sl);
   if (rc) return rc;
-  e.slice_hist = static_cast<uint32_t*>(s->slice_hist);
   e.counts = static_cast<uint32_t*>(s->counts);
   e.offsets = static_cast<uint32_t*>(s->offsets);
   PlanArgs a{};
@@ -399,10 +396,11 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
   a.key_bytes = (int)sizeof(K);
   a.counts_out = counts_out;
   a.ncounts = nsplit + 1;
+  FS_CUDA(s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
   k_bucket_hist<K, XF, HIST_BLOCK><<<stream_grid(e, sl), HIST_BLOCK, 0, e.stream>>>(
-      static_cast<const K*>(keys_in), n, e.ctl, sl, e.slice_hist, dfn, gpos_base);
+      static_cast<const K*>(keys_in), n, e.ctl, sl, e.counts, dfn, gpos_base);
   k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
-  k_slice_scan<<<1, RADIX * SCAN_LANES, 0, e.stream>>>(e.ctl, 0, 1, sl, e.slice_hist, e.counts, e.offsets);
+  k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, 0, sl, e.counts, e.offsets);
   if ((rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base))) return rc;
   uint64_t fb = (n + 255) / 256;
   const uint64_t fcap = (uint64_t)e.sm_count * 4;
@@ -443,13 +441,12 @@ int set_device(fs_sorter* s) {
 // Scratch for fs_sort_keys_noalloc lives in one file-scope device array sized
 // for NA_MAX_KEY_BYTES of keys.  Every device that loads this library holds it
 // until the process exits.  Carved as:
-//   [other-key buffer | slice histograms | slice counts | slice offsets |
-//    control block | error word]
+//   [other-key buffer | slice counts | slice offsets | control block |
+//    error word]
 constexpr uint64_t NA_MAX_KEY_BYTES = 4ull << 20;  // 2^20 u32/i32/f32 or 2^19 u64/i64/f64 keys
 constexpr uint32_t NA_MAX_SLICES = 256;            // >= tiles of the largest allowed sort
 constexpr size_t NA_OFF_KEYS = 0;
-constexpr size_t NA_OFF_HIST = NA_OFF_KEYS + NA_MAX_KEY_BYTES;
-constexpr size_t NA_OFF_COUNTS = NA_OFF_HIST + (size_t)NA_MAX_SLICES * MAX_PASSES * RADIX * 4;
+constexpr size_t NA_OFF_COUNTS = NA_OFF_KEYS + NA_MAX_KEY_BYTES;
 constexpr size_t NA_OFF_OFFSETS = NA_OFF_COUNTS + (size_t)NA_MAX_SLICES * RADIX * 4;
 constexpr size_t NA_OFF_CTL = NA_OFF_OFFSETS + (size_t)NA_MAX_SLICES * RADIX * 4;
 constexpr size_t NA_OFF_ERR = NA_OFF_CTL + ((sizeof(SortCtl) + 255) / 256) * 256;
@@ -536,7 +533,7 @@ int fs_destroy(fs_sorter* s) {
   cudaSetDevice(s->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
   for (auto& kv : s->allocs) cudaFree(kv.first);
-  void* bufs[] = {s->slice_hist, s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->ctl};
+  void* bufs[] = {s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->ctl};
   for (void* b : bufs)
     if (b) cudaFree(b);
   if (s->host_err) cudaFreeHost(s->host_err);
@@ -841,7 +838,6 @@ int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream) {
   e.timeout_ns = 2000000000ull;
   e.ctl = reinterpret_cast<SortCtl*>(base + NA_OFF_CTL);
   e.err_out = reinterpret_cast<int*>(base + NA_OFF_ERR);
-  e.slice_hist = reinterpret_cast<uint32_t*>(base + NA_OFF_HIST);
   e.counts = reinterpret_cast<uint32_t*>(base + NA_OFF_COUNTS);
   e.offsets = reinterpret_cast<uint32_t*>(base + NA_OFF_OFFSETS);
   e.s = nullptr;
@@ -909,7 +905,7 @@ int fs_partition(fs_sorter* s, int dtype, const void* keys_in, uint64_t n, uint6
 
 uint64_t fs_scratch_bytes(const fs_sorter* s) {
   if (!s) return 0;
-  return s->slice_hist_bytes + s->counts_bytes + s->offsets_bytes + s->kother_bytes + s->kfinal2_bytes + s->vother_bytes + s->dkeys_bytes +
+  return s->counts_bytes + s->offsets_bytes + s->kother_bytes + s->kfinal2_bytes + s->vother_bytes + s->dkeys_bytes +
          s->dvals_bytes + sizeof(SortCtl);
 }
 
