@@ -1,0 +1,295 @@
+// forge_sort.hpp -- the forge-sort GpuSorter / SortBuffer API in C++ over the
+// libforgesort C ABI (include/forgesort.h).  Header-only; link -lforgesort.
+//
+// Mirrors metal-forge-compute/forge-sort/src/lib.rs of kavanaghpatrick/gpu-forge
+// method for method: the same names, the same argument meaning, the same
+// n <= 1 short-cuts and the same four error variants with the same Display
+// strings.  Rust-to-C++ mapping:
+//   Result<T, SortError>      -> T, or throws forge_sort::SortError
+//   &mut [T] / &[T]           -> std::span<T> / std::span<const T>
+//   Vec<u32>                  -> std::vector<uint32_t>
+//   SortBuffer<T>             -> SortBuffer<T> (managed memory: host slices and
+//                                the kernels see the same pages, as
+//                                StorageModeShared did)
+//   MTLDevice + command queue -> CUDA device ordinal + cudaStream_t (void*)
+//   metal_buffer()            -> device_ptr()
+// Sealed SortKey (lib.rs:15-88) -> SortKey<T>, defined for the six key types
+// only, with the same constants.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <span>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <type_traits>
+#include <utility>
+#include <vector>
+
+#include "forgesort.h"
+
+namespace forge_sort {
+
+// ---- SortError (lib.rs:94-104) ----------------------------------------------
+class SortError : public std::runtime_error {
+ public:
+  enum class Kind { DeviceNotFound, ShaderCompilation, GpuExecution, LengthMismatch };
+
+  static SortError device_not_found() { return SortError(Kind::DeviceNotFound, "no Metal GPU device found"); }
+  static SortError shader_compilation(const std::string& m) {
+    return SortError(Kind::ShaderCompilation, "shader compilation failed: " + m, m);
+  }
+  static SortError gpu_execution(const std::string& m) {
+    return SortError(Kind::GpuExecution, "GPU execution failed: " + m, m);
+  }
+  static SortError length_mismatch(std::size_t keys, std::size_t values) {
+    SortError e(Kind::LengthMismatch,
+                "length mismatch: keys=" + std::to_string(keys) + ", values=" + std::to_string(values));
+    e.keys_ = keys;
+    e.values_ = values;
+    return e;
+  }
+
+  Kind kind() const noexcept { return kind_; }
+  const std::string& message() const noexcept { return msg_; }  // the variant's String payload
+  std::size_t keys() const noexcept { return keys_; }           // LengthMismatch fields
+  std::size_t values() const noexcept { return values_; }
+
+ private:
+  SortError(Kind k, const std::string& display, std::string msg = {})
+      : std::runtime_error(display), kind_(k), msg_(std::move(msg)) {}
+  Kind kind_;
+  std::string msg_;
+  std::size_t keys_ = 0, values_ = 0;
+};
+
+// Status codes that are not one of the four variants (invalid arguments) map
+// to std::invalid_argument, as a Rust caller would have met a panic or a type
+// error for them.
+namespace detail {
+inline void check(int rc, fs_sorter* h, std::size_t keys = 0, std::size_t values = 0) {
+  if (rc == FS_OK) return;
+  const char* t = fs_last_error(h);
+  const std::string m = t ? t : "";
+  switch (rc) {
+    case FS_E_DEVICE_NOT_FOUND: throw SortError::device_not_found();
+    case FS_E_KERNEL_IMAGE: throw SortError::shader_compilation(m);
+    case FS_E_LENGTH_MISMATCH: throw SortError::length_mismatch(keys, values);
+    case FS_E_INVALID: throw std::invalid_argument(m);
+    default: throw SortError::gpu_execution(m);
+  }
+}
+}  // namespace detail
+
+// ---- SortKey (lib.rs:29-88) -------------------------------------------------
+template <typename T>
+struct SortKey;  // only the six key types below are sort keys
+
+#define FORGE_SORT_KEY(T, DT, SIZE, XF, W64, FWD, INV)         \
+  template <>                                                  \
+  struct SortKey<T> {                                          \
+    static constexpr int DTYPE = DT;                           \
+    static constexpr std::size_t KEY_SIZE = SIZE;              \
+    static constexpr bool NEEDS_TRANSFORM = XF;                \
+    static constexpr bool IS_64BIT = W64;                      \
+    static constexpr uint32_t TRANSFORM_MODE_FORWARD = FWD;    \
+    static constexpr uint32_t TRANSFORM_MODE_INVERSE = INV;    \
+  };
+FORGE_SORT_KEY(uint32_t, FS_U32, 4, false, false, 0, 0)
+FORGE_SORT_KEY(int32_t, FS_I32, 4, true, false, 0, 0)
+FORGE_SORT_KEY(float, FS_F32, 4, true, false, 1, 2)
+FORGE_SORT_KEY(uint64_t, FS_U64, 8, false, true, 0, 0)
+FORGE_SORT_KEY(int64_t, FS_I64, 8, true, true, 0, 0)
+FORGE_SORT_KEY(double, FS_F64, 8, true, true, 1, 2)
+#undef FORGE_SORT_KEY
+
+class GpuSorter;
+
+// ---- SortBuffer<T> (lib.rs:160-281) -----------------------------------------
+template <typename T>
+class SortBuffer {
+  static_assert(sizeof(SortKey<T>) > 0, "SortBuffer<T> needs a SortKey type");
+
+ public:
+  SortBuffer(SortBuffer&& o) noexcept { *this = std::move(o); }
+  SortBuffer& operator=(SortBuffer&& o) noexcept {
+    if (this != &o) {
+      release();
+      owner_ = std::exchange(o.owner_, nullptr);
+      ptr_ = std::exchange(o.ptr_, nullptr);
+      len_ = std::exchange(o.len_, 0);
+      cap_ = std::exchange(o.cap_, 0);
+    }
+    return *this;
+  }
+  SortBuffer(const SortBuffer&) = delete;
+  SortBuffer& operator=(const SortBuffer&) = delete;
+  ~SortBuffer() { release(); }
+
+  std::size_t len() const { return len_; }
+  bool is_empty() const { return len_ == 0; }
+  std::size_t capacity() const { return cap_; }
+
+  // Writable view of all capacity() elements: write, then set_len().
+  std::span<T> as_mut_slice() { return {static_cast<T*>(ptr_), cap_}; }
+  // The first len() elements (the sorted result after a sort).
+  std::span<const T> as_slice() const { return {static_cast<const T*>(ptr_), len_}; }
+
+  void set_len(std::size_t len) {
+    if (len > cap_)
+      throw std::length_error("len " + std::to_string(len) + " exceeds capacity " + std::to_string(cap_));
+    len_ = len;
+  }
+  void copy_from_slice(std::span<const T> data) {
+    if (data.size() > cap_)
+      throw std::length_error("data len " + std::to_string(data.size()) + " exceeds capacity " +
+                              std::to_string(cap_));
+    if (!data.empty()) std::memcpy(ptr_, data.data(), data.size_bytes());
+    len_ = data.size();
+  }
+  void copy_to_slice(std::span<T> dest) const {
+    const std::size_t n = len_ < dest.size() ? len_ : dest.size();
+    if (n) std::memcpy(dest.data(), ptr_, n * sizeof(T));
+  }
+
+  // Device address of element 0 (replaces metal_buffer()).
+  void* device_ptr() const { return ptr_; }
+
+  // Wrap an allocation the caller owns (managed or device memory of at least
+  // capacity * sizeof(T) bytes); the SortBuffer will not free it.
+  static SortBuffer from_raw_parts(void* ptr, std::size_t len, std::size_t capacity) {
+    if (len > capacity)
+      throw std::length_error("len " + std::to_string(len) + " exceeds capacity " + std::to_string(capacity));
+    return SortBuffer(nullptr, ptr, len, capacity);
+  }
+  // Give up ownership: (pointer, len, capacity).  The caller frees the
+  // pointer with fs_free on the sorter that allocated it.
+  std::tuple<void*, std::size_t, std::size_t> into_raw_parts() && {
+    owner_ = nullptr;
+    return {std::exchange(ptr_, nullptr), std::exchange(len_, 0), std::exchange(cap_, 0)};
+  }
+
+ private:
+  friend class GpuSorter;
+  SortBuffer(fs_sorter* owner, void* ptr, std::size_t len, std::size_t cap)
+      : owner_(owner), ptr_(ptr), len_(len), cap_(cap) {}
+  void release() noexcept {
+    if (owner_ && ptr_) fs_free(owner_, ptr_);
+    owner_ = nullptr;
+    ptr_ = nullptr;
+  }
+  fs_sorter* owner_ = nullptr;  // frees ptr_ when set
+  void* ptr_ = nullptr;
+  std::size_t len_ = 0, cap_ = 0;
+};
+
+// ---- GpuSorter (lib.rs:132-3015) ---------------------------------------------
+class GpuSorter {
+ public:
+  // lib.rs:596 -- device 0, a private stream.
+  static GpuSorter create() { return GpuSorter(0, nullptr); }
+  // lib.rs:606 -- the caller's device and stream (a cudaStream_t).
+  static GpuSorter with_context(int device, void* stream) { return GpuSorter(device, stream); }
+
+  GpuSorter(GpuSorter&& o) noexcept : h_(std::exchange(o.h_, nullptr)) {}
+  GpuSorter& operator=(GpuSorter&& o) noexcept {
+    if (this != &o) {
+      if (h_) fs_destroy(h_);
+      h_ = std::exchange(o.h_, nullptr);
+    }
+    return *this;
+  }
+  GpuSorter(const GpuSorter&) = delete;
+  GpuSorter& operator=(const GpuSorter&) = delete;
+  ~GpuSorter() {
+    if (h_) fs_destroy(h_);
+  }
+
+  fs_sorter* handle() const { return h_; }
+  void synchronize() { detail::check(fs_synchronize(h_), h_); }
+
+  // -- zero-copy buffers (lib.rs:694-738, 1000-1117, 2301-2590) ----------------
+  template <typename T>
+  SortBuffer<T> alloc_sort_buffer(std::size_t capacity) {
+    void* p = nullptr;
+    detail::check(fs_alloc(h_, capacity * sizeof(T), 1, &p), h_);
+    return SortBuffer<T>(h_, p, 0, capacity);
+  }
+  void sort_buffer(const SortBuffer<uint32_t>& b) { sort_buf(b); }
+  void sort_i32_buffer(const SortBuffer<int32_t>& b) { sort_buf(b); }
+  void sort_f32_buffer(const SortBuffer<float>& b) { sort_buf(b); }
+  void sort_u64_buffer(const SortBuffer<uint64_t>& b) { sort_buf(b); }
+  void sort_i64_buffer(const SortBuffer<int64_t>& b) { sort_buf(b); }
+  void sort_f64_buffer(const SortBuffer<double>& b) { sort_buf(b); }
+
+  // lib.rs:749 -- enqueue an in-place u32 sort on `stream` (the sorter's own
+  // stream when null) and return; the caller synchronises that stream before
+  // reading the buffer.
+  void encode_sort(void* stream, const SortBuffer<uint32_t>& b) {
+    if (b.len() <= 1) return;
+    if (stream) detail::check(fs_set_stream(h_, stream), h_);
+    detail::check(fs_sort_keys(h_, FS_U32, b.device_ptr(), b.len(), 0), h_);
+  }
+
+  // -- host slices, in place (lib.rs:791-998, 2238-2485) ----------------------
+  void sort_u32(std::span<uint32_t> d) { sort_host(d); }
+  void sort_i32(std::span<int32_t> d) { sort_host(d); }
+  void sort_f32(std::span<float> d) { sort_host(d); }
+  void sort_u64(std::span<uint64_t> d) { sort_host(d); }
+  void sort_i64(std::span<int64_t> d) { sort_host(d); }
+  void sort_f64(std::span<double> d) { sort_host(d); }
+
+  // -- argsort: stable permutation, input untouched (lib.rs:1675-1921, 2595-2825)
+  std::vector<uint32_t> argsort_u32(std::span<const uint32_t> d) { return argsort_host(d); }
+  std::vector<uint32_t> argsort_i32(std::span<const int32_t> d) { return argsort_host(d); }
+  std::vector<uint32_t> argsort_f32(std::span<const float> d) { return argsort_host(d); }
+  std::vector<uint32_t> argsort_u64(std::span<const uint64_t> d) { return argsort_host(d); }
+  std::vector<uint32_t> argsort_i64(std::span<const int64_t> d) { return argsort_host(d); }
+  std::vector<uint32_t> argsort_f64(std::span<const double> d) { return argsort_host(d); }
+
+  // -- stable key/value sort, u32 values (lib.rs:1923-2236, 2826-3015) --------
+  void sort_pairs_u32(std::span<uint32_t> k, std::span<uint32_t> v) { pairs_host(k, v); }
+  void sort_pairs_i32(std::span<int32_t> k, std::span<uint32_t> v) { pairs_host(k, v); }
+  void sort_pairs_f32(std::span<float> k, std::span<uint32_t> v) { pairs_host(k, v); }
+  void sort_pairs_u64(std::span<uint64_t> k, std::span<uint32_t> v) { pairs_host(k, v); }
+  void sort_pairs_i64(std::span<int64_t> k, std::span<uint32_t> v) { pairs_host(k, v); }
+
+ private:
+  GpuSorter(int device, void* stream) {
+    const int rc = fs_create(device, stream, &h_);
+    if (rc != FS_OK) {
+      h_ = nullptr;
+      detail::check(rc, nullptr);
+    }
+  }
+
+  template <typename T>
+  void sort_buf(const SortBuffer<T>& b) {
+    if (b.len() <= 1) return;
+    detail::check(fs_sort_keys(h_, SortKey<T>::DTYPE, b.device_ptr(), b.len(), 1), h_);
+  }
+  template <typename T>
+  void sort_host(std::span<T> d) {
+    if (d.size() <= 1) return;
+    detail::check(fs_host_sort_keys(h_, SortKey<T>::DTYPE, d.data(), d.size()), h_);
+  }
+  template <typename T>
+  std::vector<uint32_t> argsort_host(std::span<const T> d) {
+    if (d.empty()) return {};
+    if (d.size() == 1) return {0u};
+    std::vector<uint32_t> idx(d.size());
+    detail::check(fs_host_argsort(h_, SortKey<T>::DTYPE, d.data(), idx.data(), d.size()), h_);
+    return idx;
+  }
+  template <typename T>
+  void pairs_host(std::span<T> k, std::span<uint32_t> v) {
+    detail::check(fs_host_sort_pairs(h_, SortKey<T>::DTYPE, k.data(), k.size(), v.data(), v.size()), h_, k.size(),
+                  v.size());
+  }
+
+  fs_sorter* h_ = nullptr;
+};
+
+}  // namespace forge_sort
