@@ -433,11 +433,11 @@ def run_multi(args):
     piece = out.numel()
     achieved = piece * 2 * kb / (pass_avg * 1e-3) / 1e9
     # phase-summed roofline of the whole job (slowest rank holds max_piece):
-    # partition hist+pass (3K), local sort (K(1+2P) + K(P-1) counts),
-    # send read + receive write (2K) over HBM, and (G-1)/G of the keys over
-    # NVLink at the measured 770 GB/s per direction
+    # bucket count + dispatch pass (3K; the dispatch's stores are the
+    # exchange), local sort (K(1+2P) + K(P-1) counts) over HBM, and (G-1)/G
+    # of the keys over NVLink at the measured 770 GB/s per direction
     nvlink = 770.0
-    hbm_b = m * 3 * kb + max_piece * (kb * (1 + 2 * P) + kb * (P - 1)) + 2 * m * kb
+    hbm_b = m * 3 * kb + max_piece * (kb * (1 + 2 * P) + kb * (P - 1))
     t_roof = hbm_b / (peak * 1e9) + m * kb * (world - 1) / world / (nvlink * 1e9)
     roofline = {
         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -445,7 +445,7 @@ def run_multi(args):
         "kernel": "k_scatter, stable ranking (local sort pass)", "alg_bytes_per_launch": piece * 2 * kb,
         "pass_ms": round(pass_avg, 4),
         "job_roofline_ms": round(t_roof * 1e3, 3), "job_frac": round(t_roof * 1e3 / ms, 4),
-        "job_model": "HBM: partition 3K + local sort K(1+2P)+K(P-1) + exchange 2K per key; NVLink (G-1)/G*K at 770 GB/s",
+        "job_model": "HBM: bucket count K + dispatch pass 2K (its stores land in the peers' inboxes) + local sort K(1+2P)+K(P-1) per key; NVLink (G-1)/G*K at 770 GB/s",
     }
     value = n_total / (ms * 1e-3) / 1e6
 
@@ -481,6 +481,7 @@ def run_multi(args):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    ss.close()
     sorter.close()
     tdist.barrier()
     tdist.destroy_process_group()

@@ -161,6 +161,7 @@ struct PlanArgs {
   unsigned long long* counts_out;  // optional copy of pass-0 digit counts
   int ncounts;                     // entries of counts_out
   int unstable_first;              // keys-only LSD sort: first pass may reorder ties
+  int force_exec;                  // single-pass plans: run the pass even if trivial
   int trivial_from_bits;           // 1: a pass is trivial when kor/kandn show its
                                    // digit never varies; 0: when hist[0] has one
                                    // digit holding all n keys (single-pass plans)

@@ -86,7 +86,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // equal keys still spread over ranks in input order.
 struct RadixDigit {
   int shift;
-  static constexpr bool STAGE = false;  // recomputed from the staged key
+  static constexpr int DIGITS = RADIX;     // digit values 0 .. DIGITS-1
+  static constexpr bool STAGE = false;     // recomputed from the staged key
+  static constexpr bool DISPATCH = false;  // output is one contiguous array
   template <typename K>
   __device__ __forceinline__ uint32_t operator()(K k, uint64_t) const {
     // one byte-permute instruction instead of shift + mask
@@ -104,19 +106,64 @@ struct SplitterDigit {
   const K* keys;         // nsplit raw splitter keys, ascending by (key, gpos)
   const uint64_t* gpos;  // their global positions
   int nsplit;
+  // shared-memory copy (ordered keys), set by stage_in before any lookup
+  const K* s_keys = nullptr;
+  const uint64_t* s_gpos = nullptr;
+  uint32_t top = 0;  // largest power of two <= nsplit (0 if none)
+  static constexpr int DIGITS = RADIX;
   static constexpr bool STAGE = true;  // digits staged in shared memory
-  // number of splitters <= (k, g) in (ordered key, position) order
+  static constexpr bool DISPATCH = false;
+  // Number of splitters <= (k, g) in (ordered key, position) order.  First
+  // the splitters whose key is below k: a branch-free lower bound over the
+  // shared-memory copy, log2(nsplit) + 1 steps, the same for every lane.
+  // Then, only for a key equal to splitter keys (rare but possible: heavy
+  // duplicates), the positions break the tie.
   __device__ __forceinline__ uint32_t operator()(K k, uint64_t g) const {
-    int lo = 0, hi = nsplit;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      const K sk = to_ordered<K, XF>(__ldg(keys + mid));
-      const bool le = sk < k || (sk == k && __ldg(gpos + mid) <= g);
-      lo = le ? mid + 1 : lo;
-      hi = le ? hi : mid;
+    __builtin_assume(__isShared(s_keys) && __isShared(s_gpos));
+    uint32_t pos = 0;
+    if (top <= 4) {
+      // up to 7 splitters (8 GPUs): three fixed steps over the copy, whose
+      // entries nsplit..7 hold the largest key (never below k)
+      pos += s_keys[3] < k ? 4u : 0u;
+      pos += s_keys[pos + 1] < k ? 2u : 0u;
+      pos += s_keys[pos] < k ? 1u : 0u;
+    } else {
+      for (uint32_t step = top; step != 0; step >>= 1) {
+        const uint32_t j = pos + step - 1;
+        if (j < (uint32_t)nsplit && s_keys[j] < k) pos += step;
+      }
     }
-    return (uint32_t)lo;
+    if (pos < (uint32_t)nsplit && s_keys[pos] == k)
+      while (pos < (uint32_t)nsplit && s_keys[pos] == k && s_gpos[pos] <= g) ++pos;
+    return pos;
   }
+  // Copy the splitters (ordered) into shared memory (at least 8 entries,
+  // the unused ones set to the largest key) and point there; the caller
+  // synchronises the CTA before the first lookup.
+  __device__ __forceinline__ void stage_in(K* sk, uint64_t* sg) {
+    const int len = nsplit > 8 ? nsplit : 8;
+    for (int i = threadIdx.x; i < len; i += blockDim.x) {
+      sk[i] = i < nsplit ? to_ordered<K, XF>(keys[i]) : ~K(0);
+      sg[i] = i < nsplit ? gpos[i] : 0ull;
+    }
+    s_keys = sk;
+    s_gpos = sg;
+    top = nsplit > 0 ? 1u << (31 - __clz(nsplit)) : 0u;
+  }
+};
+
+// Sample-sort dispatch: the splitter bucket is the digit, and bucket b's keys
+// go to dst[b] -- this rank's region of rank b's inbox, which may be another
+// GPU's memory reached with plain stores over NVLink -- at their stable rank
+// within the bucket.
+// NB = bucket capacity of the instantiation: 8 covers the GPUs of one box
+// (tile counters and scans sized for 8 digits, ranking by three ballots);
+// 256 covers any splitter count.
+template <typename K, int XF, int NB = RADIX>
+struct SplitterDispatch : SplitterDigit<K, XF> {
+  static constexpr int DIGITS = NB;
+  static constexpr bool DISPATCH = true;
+  K* const* dst;  // device array of nsplit + 1 destinations
 };
 
 // Visit the keys of [lo, hi) with the CTA's threads in coalesced order, 16-byte
@@ -232,30 +279,88 @@ __global__ void __launch_bounds__(BLOCK)
 // --------------------------------------------------------------------------
 // Bucket histogram of the sample sort's partition pass (one pass, digit =
 // splitter bucket): global counts into ctl->hist[0], slice counts into
-// counts[c][*].
+// counts[c][*].  With few buckets (one per GPU) most lanes of a warp share a
+// bucket, so the warp counts each bucket with one ballot instead of 32
+// same-address atomics.
 // --------------------------------------------------------------------------
-template <typename K, int XF, int BLOCK>
+template <typename K, int XF, int BLOCK, typename D>
 __global__ void __launch_bounds__(BLOCK)
     k_bucket_hist(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
-                  uint32_t* __restrict__ counts, const SplitterDigit<K, XF> dfn, const uint64_t gpos_base) {
+                  uint32_t* __restrict__ counts, const D dfn_in, const uint64_t gpos_base) {
+  constexpr int KV = 16 / (int)sizeof(K);  // keys per 16-byte load
   __shared__ uint32_t h[RADIX];
-  for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[i] = 0;
+  __shared__ uint32_t tot[RADIX];
+  __shared__ K s_spk[RADIX];
+  __shared__ uint64_t s_spg[RADIX];
+  D dfn = dfn_in;
+  dfn.stage_in(s_spk, s_spg);
+  const uint32_t nb = (uint32_t)dfn.nsplit + 1, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[i] = tot[i] = 0;
   __syncthreads();
+  // Up to 8 buckets (one per GPU of a box): each thread counts in eight
+  // 16-bit fields of two registers and the warp adds them up once per slice
+  // (a thread sees at most keys_per_slice / BLOCK < 2^16 keys of a slice).
+  const bool packed = nb <= 8 && sl.keys_per_slice / BLOCK < 60000;
+  uint64_t c01 = 0, c23 = 0;  // buckets 0-3 and 4-7, 16 bits each
+  auto add = [&](uint32_t b, bool valid) {
+    if (packed) {
+      const uint64_t one = valid ? 1ull << (16 * (b & 3)) : 0ull;
+      if (b < 4) c01 += one; else c23 += one;
+    } else if (valid) {
+      atomicAdd(&h[b], 1u);
+    }
+  };
+  const bool vec = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
   for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
     const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
     const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
-    for (uint64_t i = lo + threadIdx.x; i < hi; i += BLOCK)
-      atomicAdd(&h[dfn(to_ordered<K, XF>(keys[i]), gpos_base + i)], 1u);
+    const uint32_t len = (uint32_t)(hi - lo);  // < 2^32: positions fit 32 bits
+    const uint64_t g0 = gpos_base + lo;
+    // slices start on whole tiles, so lo is a multiple of KV
+    uint32_t done = 0;
+    if (vec) {  // whole 16-byte vectors, two loads in flight per thread
+      const uint4* kv = reinterpret_cast<const uint4*>(keys + lo);
+      const uint32_t nv = len / KV;
+      uint32_t v = threadIdx.x;
+      for (; v + BLOCK < nv; v += 2 * BLOCK) {
+        const uint4 a0 = __ldcs(kv + v), a1 = __ldcs(kv + v + BLOCK);
+        const K* k0 = reinterpret_cast<const K*>(&a0);
+        const K* k1 = reinterpret_cast<const K*>(&a1);
+#pragma unroll
+        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k0[q]), g0 + v * KV + q), true);
+#pragma unroll
+        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k1[q]), g0 + (v + BLOCK) * KV + q), true);
+      }
+      for (; v < nv; v += BLOCK) {
+        const uint4 a0 = __ldcs(kv + v);
+        const K* k0 = reinterpret_cast<const K*>(&a0);
+#pragma unroll
+        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k0[q]), g0 + v * KV + q), true);
+      }
+      done = nv * KV;
+    }
+    for (uint32_t i = done + threadIdx.x; i < len; i += BLOCK) add(dfn(to_ordered<K, XF>(keys[lo + i]), g0 + i), true);
+    if (packed) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint32_t v = (uint32_t)(((q < 4 ? c01 : c23) >> (16 * (q & 3))) & 0xffffu);
+        v = __reduce_add_sync(0xffffffffu, v);
+        if (lane == 0 && v) atomicAdd(&h[q], v);
+      }
+      c01 = c23 = 0;
+    }
     __syncthreads();
     uint32_t* out = counts + (size_t)c * RADIX;
-    for (int b = threadIdx.x; b < RADIX; b += BLOCK) {
-      const uint32_t v = h[b];
-      out[b] = v;
-      h[b] = 0;
-      if (v) atomicAdd(&ctl->hist[0][b], (unsigned long long)v);
+    for (int q = threadIdx.x; q < RADIX; q += BLOCK) {
+      const uint32_t v = h[q];
+      out[q] = v;
+      tot[q] += v;
+      h[q] = 0;
     }
     __syncthreads();
   }
+  for (int q = threadIdx.x; q < RADIX; q += BLOCK)
+    if (tot[q]) atomicAdd(&ctl->hist[0][q], (unsigned long long)tot[q]);
 }
 
 // --------------------------------------------------------------------------
@@ -274,7 +379,7 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
     if (d < a.passes) s_exec[d] = ((varying >> (RADIX_BITS * d)) & (RADIX - 1)) != 0;
   } else {
     const int trivial = __syncthreads_or(c0 == a.n);
-    if (d == 0) s_exec[0] = !trivial;
+    if (d == 0) s_exec[0] = a.force_exec || !trivial;
   }
   __syncthreads();
   if (d != 0) return;
@@ -404,7 +509,9 @@ __global__ void __launch_bounds__(BLOCK)
 
 // --------------------------------------------------------------------------
 // Slice scan: offsets[c][d] = (keys of digit < d in the whole pass) + (keys
-// of digit d in slices c' < c), mod 2^32 (positions are < 2^32).
+// of digit d in slices c' < c), mod 2^32 (positions are < 2^32).  With
+// `relative` the first term is dropped (positions within the digit's bucket,
+// for the sample-sort dispatch).
 // SCAN_GROUPS CTAs of 32 digits each; in a CTA, warp w owns a run of slices
 // and lane l digit 32*blockIdx.x + l, so every load is one 128-byte row.
 // --------------------------------------------------------------------------
@@ -412,7 +519,7 @@ constexpr int SCAN_GROUPS = RADIX / 32;
 constexpr int SCAN_WARPS = 32;
 __global__ void __launch_bounds__(SCAN_WARPS * 32)
     k_slice_scan(SortCtl* __restrict__ ctl, const int pass, const Slices sl,
-                 const uint32_t* __restrict__ counts, uint32_t* __restrict__ offsets) {
+                 const uint32_t* __restrict__ counts, uint32_t* __restrict__ offsets, const int relative) {
   const uint32_t flags = ctl->pass[pass].flags;
   if (!(flags & PD_EXEC)) return;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -435,7 +542,7 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32)
   if (tid < RADIX) {
     uint32_t pre = x - t;
     for (uint32_t w = 0; w < warp; ++w) pre += s_wtot[w];
-    s_base[tid] = pre;
+    s_base[tid] = relative ? 0u : pre;  // relative: offsets within each digit's bucket
   }
   // warp w sums its slices for the CTA's 32 digits
   const uint32_t d = blockIdx.x * 32 + lane;
@@ -485,23 +592,24 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32)
 //   FS_RANK_BALLOT=0: __match_any_sync                      ~2x slower again
 // warp_peers serves 2 and 0; owner election is written out in scatter_tile.
 // Invalid lanes of a partial tile match nobody but themselves.
-template <bool FULL>
+template <bool FULL, int BITS = RADIX_BITS>
 __device__ __forceinline__ uint32_t warp_peers(uint32_t d, bool valid) {
 #if FS_RANK_BALLOT == 0
-  return __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
-#else
+  if (BITS == RADIX_BITS) return __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
+#endif
   // lanes whose digit differs from mine in some bit, then complement
   uint32_t diff = FULL ? 0u : ~__ballot_sync(0xffffffffu, valid);
 #pragma unroll
-  for (int b = 0; b < RADIX_BITS; ++b) {
+  for (int b = 0; b < BITS; ++b) {
     const uint32_t bit = (d >> b) & 1u;
     diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
   }
   return valid ? ~diff : (1u << (threadIdx.x & 31));
-#endif
 }
 
-template <typename K, bool VALS, int BLOCK, int IPT, bool STAGE_DIG>
+__host__ __device__ constexpr int log2_of(int v) { return v <= 1 ? 0 : 1 + log2_of(v >> 1); }
+
+template <typename K, bool VALS, int BLOCK, int IPT, bool STAGE_DIG, int R = RADIX>
 struct ScatterLayout {
   static constexpr int WARPS = BLOCK / 32;
   static constexpr int TILE = BLOCK * IPT;
@@ -514,11 +622,11 @@ struct ScatterLayout {
   //    warp digit owners | staged digits]
   static constexpr size_t STAGE_OFF = 2 * SLOT;
   static constexpr size_t CNT_OFF = STAGE_OFF + KEYS + VALB;
-  static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;  // per-warp digit owners, x2
-  static constexpr size_t MASK_OFF = REP_OFF + 2 * (size_t)WARPS * RADIX;   // per-warp group masks, x2
-  static constexpr size_t DIG_OFF = MASK_OFF + 2 * (size_t)WARPS * 32 * 4;
+  static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * R * 4;  // per-warp digit owners
+  static constexpr size_t DIG_OFF = REP_OFF + (((size_t)WARPS * R + 15) & ~(size_t)15);
   static constexpr size_t BYTES = DIG_OFF + (STAGE_DIG ? (size_t)TILE : 0);
-  static_assert(BLOCK >= RADIX && BLOCK % 32 == 0, "one thread per digit needed");
+  static_assert(BLOCK >= R && BLOCK % 32 == 0, "one thread per digit needed");
+  static_assert((R & (R - 1)) == 0 && R <= RADIX, "digit count: a power of two <= 256");
   static_assert(KEYS % 16 == 0, "bulk copies move multiples of 16 bytes");
 };
 
@@ -529,8 +637,9 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
                                              uint32_t* __restrict__ vout, const unsigned char* slot,
                                              unsigned char* dsm, uint32_t* s_run, uint32_t* s_off,
                                              uint32_t* s_wsum, SortCtl* __restrict__ ctl, const D& dfn,
-                                             const uint64_t gpos_base) {
-  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE>;
+                                             const uint64_t gpos_base, K* const* s_dst, const uint32_t* s_lim) {
+  constexpr int R = D::DIGITS;
+  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R>;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t lt_mask = (1u << lane) - 1u;
   const uint64_t gbase = gpos_base + tbase;
@@ -541,9 +650,8 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   uint32_t* svals = reinterpret_cast<uint32_t*>(dsm + Ly::STAGE_OFF + Ly::KEYS);
   uint32_t* cnt = reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF);
   uint8_t* sdig = dsm + Ly::DIG_OFF;
-  uint32_t* wcnt = cnt + warp * RADIX;
-  uint8_t* wrep = dsm + Ly::REP_OFF + warp * RADIX;
-  uint32_t* wmask = reinterpret_cast<uint32_t*>(dsm + Ly::MASK_OFF) + warp * 32;
+  uint32_t* wcnt = cnt + warp * R;
+  uint8_t* wrep = dsm + Ly::REP_OFF + warp * R;
 
   // ---- A. keys -> registers ----------------------------------------------------
   K key[IPT];
@@ -562,6 +670,28 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     }
   }
 
+  // Digits: a radix digit is one byte-permute and is recomputed where it is
+  // needed; a splitter bucket (binary search) is computed once and kept
+  // packed, four to a register.
+  constexpr int DPK = D::STAGE ? (IPT + 3) / 4 : 1;
+  uint32_t dpk[DPK];
+  if constexpr (D::STAGE) {
+#pragma unroll
+    for (int q = 0; q < DPK; ++q) dpk[q] = 0;
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      const bool valid = FULL || (wofs + k * 32) < tile_n;
+      const uint32_t d = valid ? dfn(key[k], gbase + wofs + k * 32) : 0u;
+      dpk[k >> 2] |= d << (8 * (k & 3));
+    }
+  }
+  auto digit = [&](int k) -> uint32_t {
+    if constexpr (D::STAGE)
+      return (dpk[k >> 2] >> (8 * (k & 3))) & 0xffu;
+    else
+      return dfn(key[k], 0ull);  // the radix digit does not depend on the position
+  };
+
   // ---- B. warp-local ranks -------------------------------------------------------
   // Per key: the lanes sharing its digit; all read the warp's running count
   // for that digit, the group's highest lane advances it.  After the loop
@@ -573,51 +703,10 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
-      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
+      const uint32_t d = digit(k);
       rank[k] = valid ? atomicAdd(&wcnt[d], 1u) : 0u;
     }
-  } else if constexpr (FS_RANK_BALLOT == 4 || FS_RANK_BALLOT == 5) {
-    // Owner election with double-buffered owner bytes (iteration k uses
-    // buffer k & 1, so one warp barrier per key orders every reuse); only the
-    // owner reads and advances the running count and shuffles the old value
-    // to its group.  5: the group mask comes from shared atomicOr into the
-    // owner's word instead of five ballots.
-#pragma unroll
-    for (int k = 0; k < IPT; ++k) {
-      uint8_t* rp = wrep + (k & 1) * (Ly::WARPS * RADIX);
-      const bool valid = FULL || (wofs + k * 32) < tile_n;
-      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
-      if (valid) rp[d] = (uint8_t)lane;
-      uint32_t peers;
-      if constexpr (FS_RANK_BALLOT == 5) {
-        uint32_t* mp = wmask + (k & 1) * (Ly::WARPS * 32);
-        mp[lane] = 0u;
-        __syncwarp();
-        const uint32_t own = valid ? rp[d] : lane;
-        atomicOr(&mp[own], 1u << lane);
-        __syncwarp();
-        peers = mp[own];
-      } else {
-        __syncwarp();
-        const uint32_t own = valid ? rp[d] : lane;
-        uint32_t diff = 0;
-#pragma unroll
-        for (int b = 0; b < 5; ++b) {
-          const uint32_t bit = (own >> b) & 1u;
-          diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
-        }
-        peers = ~diff;
-      }
-      const uint32_t own = 31u - __clz(peers);  // the group's highest lane leads
-      uint32_t old = 0;
-      if (valid && lane == own) {
-        old = wcnt[d];
-        wcnt[d] = old + __popc(peers);
-      }
-      old = __shfl_sync(0xffffffffu, old, own);
-      rank[k] = old + __popc(peers & lt_mask);
-    }
-  } else if constexpr (FS_RANK_BALLOT == 3) {
+  } else if constexpr (FS_RANK_BALLOT == 3 && R > 32) {
     // Owner election: every lane writes its lane number into its digit's
     // byte; after the warp syncs, all lanes of a digit read the same owner
     // (whichever write landed).  Lanes sharing a digit are then exactly the
@@ -626,7 +715,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
-      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
+      const uint32_t d = digit(k);
       if (valid) wrep[d] = (uint8_t)lane;
       __syncwarp();
       const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
@@ -648,8 +737,8 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
-      const uint32_t d = dfn(key[k], gbase + wofs + k * 32);
-      const uint32_t peers = warp_peers<FULL>(d, valid);
+      const uint32_t d = digit(k);
+      const uint32_t peers = warp_peers<FULL, (R > 32 ? RADIX_BITS : log2_of(R))>(d, valid);
       uint32_t old = 0;
       if (valid) old = wcnt[d];
       __syncwarp();
@@ -662,11 +751,11 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
 
   // ---- C. per-digit bases and output offsets ------------------------------------
   uint32_t tot = 0;
-  if (tid < RADIX) {
+  if (tid < R) {
 #pragma unroll
     for (int w = 0; w < Ly::WARPS; ++w) {
-      const uint32_t c = cnt[w * RADIX + tid];
-      cnt[w * RADIX + tid] = tot;
+      const uint32_t c = cnt[w * R + tid];
+      cnt[w * R + tid] = tot;
       tot += c;
     }
   }
@@ -676,13 +765,13 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
     if ((int)lane >= o) x += y;
   }
-  if (lane == 31 && tid < RADIX) s_wsum[warp] = x;
+  if (lane == 31 && tid < R) s_wsum[warp] = x;
   __syncthreads();
-  if (tid < RADIX) {
+  if (tid < R) {
     uint32_t start = x - tot;
     for (uint32_t w = 0; w < warp; ++w) start += s_wsum[w];
 #pragma unroll
-    for (int w = 0; w < Ly::WARPS; ++w) cnt[w * RADIX + tid] += start;
+    for (int w = 0; w < Ly::WARPS; ++w) cnt[w * R + tid] += start;
     s_off[tid] = s_run[tid] - start;
     s_run[tid] += tot;
   }
@@ -695,7 +784,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   for (int k = 0; k < IPT; ++k) {
     const uint32_t li = wofs + k * 32;
     if (FULL || li < tile_n) {
-      const uint32_t d = dfn(key[k], gbase + li);
+      const uint32_t d = digit(k);
       const uint32_t pos = wcnt[d] + rank[k];
       skeys[pos] = key[k];
       if constexpr (VALS) {
@@ -731,7 +820,13 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       else
         d = dfn(kk, 0);
       const uint32_t pos = s_off[d] + i;
-      if (pos <= last) {
+      if constexpr (D::DISPATCH) {
+        // position within bucket d; its region holds exactly s_lim[d] keys
+        if (pos < s_lim[d])
+          s_dst[d][pos] = xout ? from_ordered<K, XF>(kk) : kk;
+        else
+          oob = true;
+      } else if (pos <= last) {
         if (wkeys) kout[pos] = xout ? from_ordered<K, XF>(kk) : kk;
         if constexpr (VALS) vout[pos] = svals[i];
       } else {
@@ -740,7 +835,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     }
   }
   if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
-  for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
+  for (int i = tid; i < Ly::WARPS * R; i += BLOCK) cnt[i] = 0;
   __syncthreads();  // staging reads done, counters zeroed: next tile may start
 }
 
@@ -758,15 +853,20 @@ enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1, SCATTER_STABLE =
 template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, int MODE, typename D>
 __global__ void __launch_bounds__(BLOCK, MINB)
     k_scatter(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
-              const uint32_t* __restrict__ offsets, const uint64_t timeout_ns, const D dfn,
+              const uint32_t* __restrict__ offsets, const uint64_t timeout_ns, const D dfn_in,
               const uint64_t gpos_base) {
-  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE>;
+  constexpr int R = D::DIGITS;
+  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R>;
   extern __shared__ __align__(128) unsigned char dsm[];
-  __shared__ uint32_t s_run[RADIX];
-  __shared__ uint32_t s_off[RADIX];
+  __shared__ uint32_t s_run[R];
+  __shared__ uint32_t s_off[R];
   __shared__ uint32_t s_wsum[Ly::WARPS];
   __shared__ __align__(8) uint64_t s_bar[2];
   __shared__ int s_abort;
+  __shared__ K* s_dst[D::DISPATCH ? R : 1];
+  __shared__ uint32_t s_lim[D::DISPATCH ? R : 1];
+  __shared__ K s_spk[D::STAGE ? (R < 8 ? 8 : R) : 1];  // the splitter search pads to 8
+  __shared__ uint64_t s_spg[D::STAGE ? (R < 8 ? 8 : R) : 1];
 
   const PassDesc pd = ctl->pass[pass];
   if (!(pd.flags & PD_EXEC)) return;
@@ -794,7 +894,16 @@ __global__ void __launch_bounds__(BLOCK, MINB)
   };
 
   uint32_t* cnt = reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF);
-  for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
+  for (int i = tid; i < Ly::WARPS * R; i += BLOCK) cnt[i] = 0;
+  D dfn = dfn_in;
+  if constexpr (D::STAGE) dfn.stage_in(s_spk, s_spg);  // visible after the slice loop's first barrier
+  if constexpr (D::DISPATCH) {
+    for (int b = tid; b < R; b += BLOCK) {
+      const bool used = b <= dfn.nsplit;
+      s_dst[b] = used ? dfn.dst[b] : nullptr;
+      s_lim[b] = used ? (uint32_t)ctl->hist[0][b] : 0u;
+    }
+  }
   if (tid == 0) {
     mbar_init(&s_bar[0], 1);
     mbar_init(&s_bar[1], 1);
@@ -809,7 +918,7 @@ __global__ void __launch_bounds__(BLOCK, MINB)
     const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
     const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
     __syncthreads();  // the previous slice's last tile is done with s_run
-    if (tid < RADIX) s_run[tid] = offsets[(size_t)c * RADIX + tid];
+    if (tid < R) s_run[tid] = offsets[(size_t)c * RADIX + tid];  // row stride stays 256
     if (tid == 0) issue(lo, hi, s);
     __syncthreads();
     for (uint64_t t0 = lo; t0 < hi; t0 += Ly::TILE, s ^= 1) {
@@ -833,13 +942,13 @@ __global__ void __launch_bounds__(BLOCK, MINB)
       const unsigned char* slot = dsm + (size_t)s * Ly::SLOT;
       if (from_slot)
         scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                         slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+                                                         slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim);
       else if (full)
         scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim);
       else
         scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                           slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base);
+                                                           slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim);
     }
   }
   // never leave a bulk copy into this CTA's shared memory in flight
@@ -847,6 +956,9 @@ __global__ void __launch_bounds__(BLOCK, MINB)
     for (int q = 0; q < 2; ++q)
       if (armed & (1u << q)) mbar_wait_bounded(&s_bar[q], (parity >> q) & 1u, timeout_ns, &ctl->err);
   }
+  // dispatch: stores to peer GPUs are ordered before whatever this GPU does
+  // next (the stream-ordered barrier that tells the peers their inbox is full)
+  if constexpr (D::DISPATCH) __threadfence_system();
 }
 
 // --------------------------------------------------------------------------

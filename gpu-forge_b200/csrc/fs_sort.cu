@@ -37,6 +37,14 @@ struct fs_sorter {
   size_t dkeys_bytes = 0;
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
+  void* dst_tab = nullptr;  // sample-sort dispatch: 256 destination pointers
+  // what the last fs_partition_count counted (fs_partition_dispatch must match)
+  struct {
+    bool ready = false;
+    int dtype = -1, nsplit = -1;
+    const void* keys = nullptr;
+    uint64_t n = 0;
+  } part;
   int sm_count = 0;
   uint64_t timeout_ns = 2000000000ull;
   int last_launches = 0;
@@ -119,6 +127,19 @@ template <> struct UnstableCfg<uint32_t> {
 };
 template <> struct UnstableCfg<uint64_t> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
+};
+// Sample-sort partition / dispatch pass: the stable tile with room for the
+// splitter search (2 CTAs/SM; same tile as StableCfg<K, false>).
+#ifndef FS_PART_MINB
+#define FS_PART_MINB 4
+#endif
+#ifndef FS_PART_IPT
+#define FS_PART_IPT 8
+#endif
+template <typename K> struct PartCfg {
+  static constexpr int BLOCK = 256, IPT = FS_PART_IPT, MINB = FS_PART_MINB;
+  static_assert(StableCfg<K, false>::BLOCK * StableCfg<K, false>::IPT % (BLOCK * IPT) == 0,
+                "partition tiles must divide the slice unit");
 };
 template <typename C> constexpr uint64_t tile_of() { return (uint64_t)C::BLOCK * C::IPT; }
 constexpr uint64_t gcd64(uint64_t a, uint64_t b) { return b ? gcd64(b, a % b) : a; }
@@ -212,7 +233,7 @@ int blocks_per_sm(fs_sorter* s, Kern k, int block, size_t smem) {
 // limit on the current device the first time; allocates nothing.
 template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int scatter_occupancy(const Exec& e) {
-  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE>;
+  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS>;
   auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D>;
   static int configured_mask = 0;  // bit per device (the attribute is per context)
   static int bps = 0;
@@ -229,7 +250,7 @@ int scatter_occupancy(const Exec& e) {
 
 template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
-  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE>;
+  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS>;
   const int bps = scatter_occupancy<K, VALS, XF, C, MODE, D>(e);
   if (bps < 0) return -bps;
   const uint64_t cap = (uint64_t)bps * e.sm_count;
@@ -284,7 +305,7 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
   for (int p = 0; p < P; ++p) {
     t_begin(e);
     k_count<K, XF, HIST_BLOCK><<<sg, HIST_BLOCK, 0, e.stream>>>(e.ctl, p, n, sl, e.counts);
-    k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, p, sl, e.counts, e.offsets);
+    k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, p, sl, e.counts, e.offsets, 0);
     t_end(e);
     t_begin(e);
     const RadixDigit dg{p * RADIX_BITS};
@@ -397,17 +418,98 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
   a.counts_out = counts_out;
   a.ncounts = nsplit + 1;
   FS_CUDA(s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
-  k_bucket_hist<K, XF, HIST_BLOCK><<<stream_grid(e, sl), HIST_BLOCK, 0, e.stream>>>(
+  k_bucket_hist<K, XF, HIST_BLOCK, D><<<stream_grid(e, sl), HIST_BLOCK, 0, e.stream>>>(
       static_cast<const K*>(keys_in), n, e.ctl, sl, e.counts, dfn, gpos_base);
   k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
-  k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, 0, sl, e.counts, e.offsets);
-  if ((rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base))) return rc;
+  k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, 0, sl, e.counts, e.offsets, 0);
+  if ((rc = launch_scatter<K, false, XF, PartCfg<K>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base))) return rc;
   uint64_t fb = (n + 255) / 256;
   const uint64_t fcap = (uint64_t)e.sm_count * 4;
   k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, e.stream>>>(e.ctl, n, e.err_out);
   s->last_launches = 5;
   FS_CUDA(s, cudaGetLastError());
   return FS_OK;
+}
+
+// ---- sample-sort dispatch -----------------------------------------------------
+// Count: per-slice bucket counts (kept in the sorter's scratch for the
+// dispatch that follows) and the bucket totals, copied to the host.
+template <typename K, int XF>
+int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t gpos_base, const void* spl_keys,
+                            const uint64_t* spl_gpos, int nsplit, unsigned long long* host_counts) {
+  using D = SplitterDigit<K, XF>;
+  const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
+  Exec e = exec_of(s);
+  const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
+  int rc = ensure_slice_buffers(s, sl);
+  if (rc) return rc;
+  e.counts = static_cast<uint32_t*>(s->counts);
+  s->ev_used = 0;
+  FS_CUDA(s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
+  t_begin(e);
+  k_bucket_hist<K, XF, HIST_BLOCK, D><<<stream_grid(e, sl), HIST_BLOCK, 0, e.stream>>>(
+      static_cast<const K*>(keys), n, e.ctl, sl, e.counts, dfn, gpos_base);
+  t_end(e);
+  FS_CUDA(s, cudaGetLastError());
+  FS_CUDA(s, cudaMemcpyAsync(host_counts, &e.ctl->hist[0][0], (size_t)(nsplit + 1) * sizeof(unsigned long long),
+                             cudaMemcpyDeviceToHost, e.stream));
+  FS_CUDA(s, cudaStreamSynchronize(e.stream));
+  s->last_launches = 1;
+  return FS_OK;
+}
+
+// Dispatch: one stable pass that stores every key at its rank within its
+// bucket, straight into that bucket's destination (dst[b], this rank's region
+// of rank b's inbox: plain stores over NVLink when it is another GPU's).
+template <typename K, int XF, int NB>
+int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, uint64_t n, uint64_t gpos_base,
+                                  const void* spl_keys, const uint64_t* spl_gpos, int nsplit, void* const* dst_host) {
+  using D = SplitterDispatch<K, XF, NB>;
+  D dfn{};
+  dfn.keys = static_cast<const K*>(spl_keys);
+  dfn.gpos = spl_gpos;
+  dfn.nsplit = nsplit;
+  if (!s->dst_tab) FS_CUDA(s, cudaMalloc(&s->dst_tab, RADIX * sizeof(void*)));
+  // pageable source: the copy is staged before cudaMemcpyAsync returns
+  FS_CUDA(s, cudaMemcpyAsync(s->dst_tab, dst_host, (size_t)(nsplit + 1) * sizeof(void*), cudaMemcpyHostToDevice,
+                             s->stream));
+  dfn.dst = static_cast<K* const*>(s->dst_tab);
+  Exec e = exec_of(s);
+  const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
+  e.counts = static_cast<uint32_t*>(s->counts);
+  e.offsets = static_cast<uint32_t*>(s->offsets);
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys;
+  a.kfinal = dst_host[0];  // not written: dispatch stores through dst[]
+  a.kother = nullptr;
+  a.passes = 1;
+  a.write_keys = 1;
+  a.key_bytes = (int)sizeof(K);
+  a.force_exec = 1;
+  s->ev_used = 0;
+  t_begin(e);
+  k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
+  k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, 0, sl, e.counts, e.offsets, 1);
+  t_end(e);
+  int rc;
+  t_begin(e);
+  rc = launch_scatter<K, false, XF, PartCfg<K>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base);
+  t_end(e);
+  if (rc) return rc;
+  k_finalize<K><<<1, 256, 0, e.stream>>>(e.ctl, 0, e.err_out);  // error hand-off only
+  s->last_launches = 4;
+  FS_CUDA(s, cudaGetLastError());
+  return FS_OK;
+}
+
+// Up to 8 buckets (the GPUs of one box) take the 8-digit instantiation.
+template <typename K, int XF>
+int enqueue_partition_dispatch(fs_sorter* s, const void* keys, uint64_t n, uint64_t gpos_base, const void* spl_keys,
+                               const uint64_t* spl_gpos, int nsplit, void* const* dst_host) {
+  if (nsplit < 8)
+    return enqueue_partition_dispatch_nb<K, XF, 8>(s, keys, n, gpos_base, spl_keys, spl_gpos, nsplit, dst_host);
+  return enqueue_partition_dispatch_nb<K, XF, RADIX>(s, keys, n, gpos_base, spl_keys, spl_gpos, nsplit, dst_host);
 }
 
 int finish(fs_sorter* s, int sync) {
@@ -533,7 +635,7 @@ int fs_destroy(fs_sorter* s) {
   cudaSetDevice(s->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
   for (auto& kv : s->allocs) cudaFree(kv.first);
-  void* bufs[] = {s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->ctl};
+  void* bufs[] = {s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->dst_tab, s->ctl};
   for (void* b : bufs)
     if (b) cudaFree(b);
   if (s->host_err) cudaFreeHost(s->host_err);
@@ -901,6 +1003,96 @@ int fs_partition(fs_sorter* s, int dtype, const void* keys_in, uint64_t n, uint6
   }
   if (rc) return rc;
   return finish(s, sync);
+}
+
+#define FS_PARTITION_DTYPES(CALL)                \
+  switch (dtype) {                               \
+    case FS_U32: rc = CALL(uint32_t, XF_NONE); break;  \
+    case FS_I32: rc = CALL(uint32_t, XF_SIGN); break;  \
+    case FS_F32: rc = CALL(uint32_t, XF_FLOAT); break; \
+    case FS_U64: rc = CALL(uint64_t, XF_NONE); break;  \
+    case FS_I64: rc = CALL(uint64_t, XF_SIGN); break;  \
+    default: rc = CALL(uint64_t, XF_FLOAT); break;     \
+  }
+
+int fs_partition_count(fs_sorter* s, int dtype, const void* keys, uint64_t n, uint64_t gpos_base,
+                       const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,
+                       uint64_t* bucket_counts_host) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (nsplit < 0 || nsplit > RADIX - 1) return fail(s, FS_E_INVALID, "nsplit = %d outside [0, 255]", nsplit);
+  if (!bucket_counts_host) return fail(s, FS_E_INVALID, "bucket_counts_host is NULL");
+  s->part.ready = false;
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  if (n == 0) {  // nothing to send; the dispatch that follows is a no-op
+    std::memset(bucket_counts_host, 0, (size_t)(nsplit + 1) * 8);
+    s->part = {true, dtype, nsplit, keys, 0};
+    return FS_OK;
+  }
+  if ((rc = prepare_ptr(s, keys, (size_t)n * kb, "keys"))) return rc;
+  if (nsplit > 0) {
+    if ((rc = prepare_ptr(s, splitter_keys, (size_t)nsplit * kb, "splitter_keys"))) return rc;
+    if ((rc = prepare_ptr(s, splitter_gpos, (size_t)nsplit * 8, "splitter_gpos"))) return rc;
+  }
+  auto* hc = reinterpret_cast<unsigned long long*>(bucket_counts_host);
+#define FS_PC(K, XF) enqueue_partition_count<K, XF>(s, keys, n, gpos_base, splitter_keys, splitter_gpos, nsplit, hc)
+  FS_PARTITION_DTYPES(FS_PC)
+#undef FS_PC
+  if (rc) return rc;
+  s->part = {true, dtype, nsplit, keys, n};
+  return finish(s, 1);
+}
+
+int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n, uint64_t gpos_base,
+                          const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,
+                          void* const* bucket_dst, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (!s->part.ready || s->part.dtype != dtype || s->part.nsplit != nsplit || s->part.keys != keys ||
+      s->part.n != n)
+    return fail(s, FS_E_INVALID, "fs_partition_dispatch must follow fs_partition_count of the same keys and splitters");
+  s->part.ready = false;
+  if (n == 0) return FS_OK;
+  if (!bucket_dst) return fail(s, FS_E_INVALID, "bucket_dst is NULL");
+  for (int b = 0; b <= nsplit; ++b)
+    if (!bucket_dst[b]) return fail(s, FS_E_INVALID, "bucket_dst[%d] is NULL", b);
+  if ((rc = set_device(s))) return rc;
+#define FS_PD(K, XF) \
+  enqueue_partition_dispatch<K, XF>(s, keys, n, gpos_base, splitter_keys, splitter_gpos, nsplit, bucket_dst)
+  FS_PARTITION_DTYPES(FS_PD)
+#undef FS_PD
+  if (rc) return rc;
+  return finish(s, sync);
+}
+
+int fs_ipc_export(fs_sorter* s, void* ptr, void* handle_out) {
+  if (!s || !ptr || !handle_out) return s ? fail(s, FS_E_INVALID, "fs_ipc_export: NULL argument") : FS_E_INVALID;
+  static_assert(sizeof(cudaIpcMemHandle_t) == FS_IPC_HANDLE_BYTES, "IPC handle size");
+  int rc = set_device(s);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  FS_CUDA(s, cudaIpcGetMemHandle(&h, ptr));
+  std::memcpy(handle_out, &h, sizeof h);
+  return FS_OK;
+}
+
+int fs_ipc_open(fs_sorter* s, const void* handle, void** ptr_out) {
+  if (!s || !handle || !ptr_out) return s ? fail(s, FS_E_INVALID, "fs_ipc_open: NULL argument") : FS_E_INVALID;
+  int rc = set_device(s);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  FS_CUDA(s, cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess));
+  return FS_OK;
+}
+
+int fs_ipc_close(fs_sorter* s, void* ptr) {
+  if (!s || !ptr) return s ? fail(s, FS_E_INVALID, "fs_ipc_close: NULL argument") : FS_E_INVALID;
+  int rc = set_device(s);
+  if (rc) return rc;
+  FS_CUDA(s, cudaIpcCloseMemHandle(ptr));
+  return FS_OK;
 }
 
 uint64_t fs_scratch_bytes(const fs_sorter* s) {

@@ -16,6 +16,8 @@ LIB_PATH = os.path.join(HERE, LIB_NAME)
 # fs_dtype (include/forgesort.h)
 U32, I32, F32, U64, I64, F64 = range(6)
 
+IPC_HANDLE_BYTES = 64  # FS_IPC_HANDLE_BYTES
+
 # fs_status
 OK = 0
 E_DEVICE_NOT_FOUND = 1
@@ -49,6 +51,11 @@ SIGNATURES = {
     "fs_set_kernel_timing": (_i32, [_vp, _i32]),
     "fs_last_kernel_times": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), _i32]),
     "fs_partition": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _i32]),
+    "fs_partition_count": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp]),
+    "fs_partition_dispatch": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _i32]),
+    "fs_ipc_export": (_i32, [_vp, _vp, _vp]),
+    "fs_ipc_open": (_i32, [_vp, _vp, _pp]),
+    "fs_ipc_close": (_i32, [_vp, _vp]),
     "fs_sort_keys_noalloc": (_i32, [_i32, _vp, _u64, _vp]),
     "fs_scratch_bytes": (_u64, [_vp]),
     "fs_last_launch_count": (_i32, [_vp]),

@@ -12,14 +12,19 @@ Per call, on every rank:
      G*S tuples on the host and picks the same G-1 splitters (every S-th);
      the (key, global position) order breaks ties, so duplicate-heavy input
      still splits evenly;
-  2. partition: one stable GPU pass sends every key to its splitter bucket
-     (fs_partition: the radix scatter machinery with the bucket as digit);
-  3. exchange: bucket sizes, then one all-to-all of the buckets (NCCL over
-     NVLink on GPUs);
+  2-3. partition + exchange.  On GPUs (CudaOps.exchange) one stable pass
+     stores every key straight into its destination rank's inbox: bucket
+     counts are all-gathered, every rank learns where its keys start in each
+     inbox, and the scatter kernel writes peers' inboxes with plain stores
+     over NVLink (CUDA IPC mappings; fs_partition_dispatch).  A stream-
+     ordered NCCL all-reduce then tells every rank its inbox is complete.
+     Without an exchange capability (the CPU stand-in of the tests), a
+     partition pass (fs_partition semantics) is followed by an all-to-all of
+     the bucket sizes and one of the buckets;
   4. local sort of the received keys (the single-GPU radix sort).
 
-The local steps go through a LocalOps object so the host logic can run on
-CPU ranks (gloo) in tests with a CPU stand-in; CudaOps is the product path.
+The local steps go through an ops object so the host logic can run on CPU
+ranks (gloo) in tests with a CPU stand-in; CudaOps is the product path.
 """
 from __future__ import annotations
 
@@ -67,11 +72,89 @@ def sample_positions(m: int, per_rank: int) -> np.ndarray:
 
 
 class CudaOps:
-    """Product path: the partition and the local sort run in libforgesort."""
+    """Product path: partition, exchange and local sort run in libforgesort.
 
-    def __init__(self, sorter: GpuSorter, torch):
+    exchange() keeps one inbox per rank (cudaMalloc, exported by CUDA IPC and
+    opened by every peer), grown collectively when a step needs more room;
+    close() releases it (collective)."""
+
+    def __init__(self, sorter: GpuSorter, torch, dispatch: bool = True):
         self.s = sorter
         self.torch = torch
+        self.dispatch = dispatch
+        self._inbox = 0
+        self._cap = 0
+        self._peers: List[int] = []
+
+    def _splitters(self, dt, dev, spl_raw: np.ndarray, spl_gpos: np.ndarray):
+        torch = self.torch
+        if len(spl_gpos) == 0:
+            return None, None, 0, 0
+        sk = torch.from_numpy(np.ascontiguousarray(spl_raw).view(
+            np.int32 if _WIDTH[dt] == 32 else np.int64)).to(dev)
+        sg = torch.from_numpy(spl_gpos.astype(np.int64)).to(dev)
+        return sk, sg, sk.data_ptr(), sg.data_ptr()
+
+    def _ensure_inbox(self, nbytes: int, group, dev) -> None:
+        """Collective: every rank calls it with the same nbytes."""
+        if nbytes <= self._cap:
+            return
+        torch, dist = self.torch, self.torch.distributed
+        self.close(group)
+        G, r = dist.get_world_size(group), dist.get_rank(group)
+        cap = max(int(nbytes * 1.0625), 1 << 20)
+        self._inbox = self.s.alloc_device(cap)
+        self._cap = cap
+        mine = torch.tensor(list(self.s.ipc_export(self._inbox)), dtype=torch.uint8, device=dev)
+        handles = [torch.empty_like(mine) for _ in range(G)]
+        dist.all_gather(handles, mine, group=group)
+        self._peers = [self._inbox if b == r else self.s.ipc_open(bytes(handles[b].cpu().tolist()))
+                       for b in range(G)]
+
+    def close(self, group=None) -> None:
+        """Collective: unmap the peers' inboxes, wait for every rank, free."""
+        if not self._inbox:
+            return
+        dist = self.torch.distributed
+        r = dist.get_rank(group)
+        for b, p in enumerate(self._peers):
+            if b != r:
+                self.s.ipc_close(p)
+        self._peers = []
+        dist.barrier(group=group)  # no rank frees an inbox a peer still maps
+        self.s.free_device(self._inbox)
+        self._inbox = 0
+        self._cap = 0
+
+    def exchange(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray, group):
+        """Partition + all-to-all + local sort; returns (sorted piece, send
+        counts, receive counts).  Runs on the current torch stream."""
+        torch, dist = self.torch, self.torch.distributed
+        G, r = dist.get_world_size(group), dist.get_rank(group)
+        dev, kb, m = keys.device, keys.element_size(), keys.numel()
+        torch.cuda.current_stream(dev).synchronize()  # keys are ready whatever stream wrote them
+        sk, sg, skp, sgp = self._splitters(dt, dev, spl_raw, spl_gpos)
+        send = self.s.partition_count(dt, keys.data_ptr(), m, gpos_base, skp, sgp, G - 1)
+        cnt = torch.tensor(send, dtype=torch.int64, device=dev)
+        rows = [torch.empty_like(cnt) for _ in range(G)]
+        dist.all_gather(rows, cnt, group=group)
+        M = torch.stack(rows).cpu().numpy()  # M[s, b]: keys rank s sends to rank b
+        self._ensure_inbox(int(M.sum(axis=0).max()) * kb, group, dev)
+        start = M[:r, :].sum(axis=0)  # where this rank's keys begin in every inbox
+        dst = [self._peers[b] + int(start[b]) * kb for b in range(G)]
+        self.s.partition_dispatch(dt, keys.data_ptr(), m, gpos_base, skp, sgp, G - 1, dst, sync=True)
+        # every rank enters this collective after its dispatch finished, so
+        # once it completes every inbox is full
+        done = torch.zeros(1, dtype=torch.int32, device=dev)
+        dist.all_reduce(done, group=group)
+        torch.cuda.current_stream(dev).synchronize()
+        del sk, sg
+        recv = [int(x) for x in M[:, r]]
+        total = sum(recv)
+        out = torch.empty(total, dtype=keys.dtype, device=dev)
+        if total:
+            self.s.sort_device_copy(dt, self._inbox, out.data_ptr(), total, sync=True)
+        return out, send, recv
 
     def partition(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray) -> Tuple[object, List[int]]:
         torch = self.torch
@@ -165,6 +248,12 @@ class SampleSorter:
         spl_raw = a_raw[picks].astype(_BITS[dt])
         spl_gpos = a_gpos[picks]
 
+        # 2-4 on GPUs: dispatch straight into the peers' inboxes, local sort
+        if getattr(self.ops, "dispatch", False):
+            out, send, recv = self.ops.exchange(dt, keys, gpos_base, spl_raw, spl_gpos, self.group)
+            self.last = SampleSortStats(send, recv)
+            return out
+
         # 2. stable partition into G buckets
         part, send = self.ops.partition(dt, keys, gpos_base, spl_raw, spl_gpos)
 
@@ -180,3 +269,8 @@ class SampleSorter:
         # 4. local sort of this rank's bucket
         self.last = SampleSortStats(send, recv)
         return self.ops.sort(dt, inbox)
+
+    def close(self) -> None:
+        """Collective: release the ops' exchange resources (CUDA IPC inboxes)."""
+        if hasattr(self.ops, "close"):
+            self.ops.close(self.group)

@@ -440,6 +440,51 @@ class GpuSorter:
                                             ctypes.c_void_p(out_ptr), ctypes.c_void_p(counts_ptr), int(sync)))
         self._pending = self._pending or not sync
 
+    def partition_count(self, dt, in_ptr: int, n: int, gpos_base: int, spl_keys_ptr: int, spl_gpos_ptr: int,
+                        nsplit: int) -> list:
+        """Dispatch step 1: bucket sizes of n device keys (host list of
+        nsplit+1 ints); waits for the stream."""
+        name = dtype_name(dt)
+        out = (ctypes.c_uint64 * (nsplit + 1))()
+        self._call(_lib.load().fs_partition_count(self._h, _DT[name][0], ctypes.c_void_p(in_ptr), n, gpos_base,
+                                                  ctypes.c_void_p(spl_keys_ptr), ctypes.c_void_p(spl_gpos_ptr),
+                                                  nsplit, out))
+        return [int(x) for x in out]
+
+    def partition_dispatch(self, dt, in_ptr: int, n: int, gpos_base: int, spl_keys_ptr: int, spl_gpos_ptr: int,
+                           nsplit: int, dst_ptrs, sync: bool = False) -> None:
+        """Dispatch step 2: store bucket b's keys at dst_ptrs[b] (device
+        pointers, possibly peer GPUs' memory opened with ipc_open)."""
+        name = dtype_name(dt)
+        tab = (ctypes.c_void_p * (nsplit + 1))(*[ctypes.c_void_p(int(p)) for p in dst_ptrs])
+        self._call(_lib.load().fs_partition_dispatch(self._h, _DT[name][0], ctypes.c_void_p(in_ptr), n, gpos_base,
+                                                     ctypes.c_void_p(spl_keys_ptr), ctypes.c_void_p(spl_gpos_ptr),
+                                                     nsplit, tab, int(sync)))
+        self._pending = self._pending or not sync
+
+    def alloc_device(self, nbytes: int) -> int:
+        """Plain device memory (cudaMalloc) owned by the sorter; free_device()."""
+        ptr = ctypes.c_void_p()
+        self._call(_lib.load().fs_alloc(self._h, nbytes, 0, ctypes.byref(ptr)))
+        return int(ptr.value)
+
+    def free_device(self, ptr: int) -> None:
+        self._call(_lib.load().fs_free(self._h, ctypes.c_void_p(ptr)))
+
+    def ipc_export(self, ptr: int) -> bytes:
+        h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+        self._call(_lib.load().fs_ipc_export(self._h, ctypes.c_void_p(ptr), h))
+        return bytes(h)
+
+    def ipc_open(self, handle: bytes) -> int:
+        h = (ctypes.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(handle)
+        ptr = ctypes.c_void_p()
+        self._call(_lib.load().fs_ipc_open(self._h, h, ctypes.byref(ptr)))
+        return int(ptr.value)
+
+    def ipc_close(self, ptr: int) -> None:
+        self._call(_lib.load().fs_ipc_close(self._h, ctypes.c_void_p(ptr)))
+
     def host_sort_ptr(self, dt, host_ptr: int, n: int) -> None:
         """sort_<dt> on raw (e.g. pinned) host memory; H2D + sort + D2H."""
         name = dtype_name(dt)

@@ -148,8 +148,9 @@ int fs_host_sort_keys_copy(fs_sorter* s, int dtype, const void* host_in,
 int fs_set_kernel_timing(fs_sorter* s, int on);
 /* After a synchronous sort with timing on: write up to `cap` durations in ms
  * and return how many were written (negative fs_status on failure).  Order:
- * histogram, plan, then per digit pass (count + slice scan, scatter), then
- * finalize -- 3 + 2*P entries for P = key bytes. */
+ * first count (digit-0 counts + which digits vary), plan, then per digit pass
+ * (count + slice scan, scatter), then finalize -- 3 + 2*P entries for
+ * P = key bytes. */
 int fs_last_kernel_times(fs_sorter* s, float* ms, int cap);
 
 /* ---- multi-GPU sample sort building block -------------------------------- */
@@ -167,6 +168,35 @@ int fs_partition(fs_sorter* s, int dtype, const void* keys_in, uint64_t n,
                  uint64_t gpos_base, const void* splitter_keys,
                  const uint64_t* splitter_gpos, int nsplit, void* keys_out,
                  uint64_t* bucket_counts, int sync);
+
+/* Sample-sort dispatch: partition and exchange in one pass over peer memory.
+ * Step 1 counts: writes the nsplit+1 bucket sizes of the n keys to
+ * bucket_counts_host (host memory) and keeps the per-slice counts in the
+ * sorter's scratch; waits for the stream.  Same buckets as fs_partition. */
+int fs_partition_count(fs_sorter* s, int dtype, const void* keys, uint64_t n,
+                       uint64_t gpos_base, const void* splitter_keys,
+                       const uint64_t* splitter_gpos, int nsplit,
+                       uint64_t* bucket_counts_host);
+/* Step 2 stores every key of bucket b, in input order, at bucket_dst[b][0 ..
+ * count_b) -- bucket_dst (host array of nsplit+1 device pointers) may point
+ * into other GPUs' memory (fs_ipc_open), which the kernel writes with plain
+ * stores over NVLink; it makes those stores visible system-wide before it
+ * ends.  Must directly follow fs_partition_count on the same sorter with the
+ * same keys, n, dtype and splitters.  The caller orders the peers' reads of
+ * their inboxes after this call (e.g. a stream-ordered collective). */
+int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n,
+                          uint64_t gpos_base, const void* splitter_keys,
+                          const uint64_t* splitter_gpos, int nsplit,
+                          void* const* bucket_dst, int sync);
+
+/* CUDA IPC for the dispatch inboxes (one process per GPU): export a handle to
+ * device memory from cudaMalloc (fs_alloc with managed = 0), open a peer's
+ * handle into this process (peer access enabled lazily), close it again
+ * before the owner frees the memory. */
+#define FS_IPC_HANDLE_BYTES 64
+int fs_ipc_export(fs_sorter* s, void* dev_ptr, void* handle_out);
+int fs_ipc_open(fs_sorter* s, const void* handle, void** peer_ptr);
+int fs_ipc_close(fs_sorter* s, void* peer_ptr);
 
 /* ---- allocation-free form ------------------------------------------------ */
 
