@@ -73,7 +73,8 @@ def config(args, world):
 
 # ------------------------------------------------------------------ clocks
 class Clocks:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """nvidia-smi sampled every 50 ms while the timed region runs (the
+    sampler is running before the region starts)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -88,7 +89,12 @@ class Clocks:
             self.f = tempfile.TemporaryFile(mode="w+")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+            t_end = time.time() + 5.0  # wait for the first sample
+            while time.time() < t_end and self.proc.poll() is None and os.fstat(self.f.fileno()).st_size == 0:
+                time.sleep(0.01)
+            self.f.seek(0, os.SEEK_END)
+            self.skip = self.f.tell()  # samples taken before the region are not counted
         except Exception:
             self.proc = None
         return self
@@ -104,7 +110,7 @@ class Clocks:
     def summary(self):
         if not self.proc or not self.f:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.f.seek(0)
+        self.f.seek(getattr(self, "skip", 0))
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.f.read().splitlines():

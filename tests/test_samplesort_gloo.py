@@ -114,3 +114,18 @@ def test_other_key_types(dt, dist_name, tmp_path):
 
 def test_uneven_and_empty_shards(tmp_path):
     _run(3, "u32", "u32", tmp_path, per_rank_sizes=[25_000, 0, 7_000])
+
+
+@pytest.mark.parametrize("distinct", [7, 1000, 1 << 40])
+def test_choose_splitters_matches_lexicographic_order(distinct):
+    """Splitter picks equal the per_rank-th tuples of a full (key, position)
+    lexicographic sort, with heavy, light and no key duplication."""
+    from forge_sort.samplesort import choose_splitters
+    rng = np.random.default_rng(distinct % 97)
+    G, S = 8, 512
+    keys = rng.integers(0, distinct, G * S, dtype=np.uint64)
+    gpos = rng.permutation(G * S * 3)[: G * S].astype(np.uint64)
+    order = np.lexsort((gpos, keys))
+    want = [order[j * S] for j in range(1, G)]
+    got = choose_splitters(keys, gpos, G, S)
+    assert [(keys[i], gpos[i]) for i in got] == [(keys[i], gpos[i]) for i in want]
