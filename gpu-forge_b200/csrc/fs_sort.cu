@@ -38,6 +38,18 @@ struct fs_sorter {
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
   void* dst_tab = nullptr;  // sample-sort dispatch: 256 destination pointers
+  // fs_host_sort_keys_copy_async: two device buffers used in turn, and copy
+  // streams of their own so one call's copies overlap the next call's work
+  struct PipeSlot {
+    void* dkeys = nullptr;
+    size_t bytes = 0;
+    cudaEvent_t in_done = nullptr, sorted = nullptr, out_done = nullptr;
+    bool used = false;
+  } pipe[2];
+  int pipe_next = 0;
+  bool pipe_open = false;  // async calls since the last fs_synchronize
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t pipe_start = nullptr;
   // what the last fs_partition_count counted (fs_partition_dispatch must match)
   struct {
     bool ready = false;
@@ -635,6 +647,16 @@ int fs_destroy(fs_sorter* s) {
   cudaSetDevice(s->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
   for (auto& kv : s->allocs) cudaFree(kv.first);
+  if (s->h2d) cudaStreamSynchronize(s->h2d);
+  if (s->d2h) cudaStreamSynchronize(s->d2h);
+  for (auto& sl : s->pipe) {
+    if (sl.dkeys) cudaFree(sl.dkeys);
+    for (cudaEvent_t e : {sl.in_done, sl.sorted, sl.out_done})
+      if (e) cudaEventDestroy(e);
+  }
+  if (s->h2d) cudaStreamSynchronize(s->h2d), cudaStreamDestroy(s->h2d);
+  if (s->d2h) cudaStreamSynchronize(s->d2h), cudaStreamDestroy(s->d2h);
+  if (s->pipe_start) cudaEventDestroy(s->pipe_start);
   void* bufs[] = {s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->dst_tab, s->ctl};
   for (void* b : bufs)
     if (b) cudaFree(b);
@@ -665,7 +687,76 @@ int fs_synchronize(fs_sorter* s) {
   if (!s) return FS_E_INVALID;
   int rc = set_device(s);
   if (rc) return rc;
+  // join the asynchronous host sorts: later work on the stream waits for
+  // their copies back, then the host waits for the stream
+  for (auto& sl : s->pipe)
+    if (sl.used) FS_CUDA(s, cudaStreamWaitEvent(s->stream, sl.out_done, 0));
+  s->pipe_open = false;
   return finish(s, 1);
+}
+
+int fs_host_sort_keys_copy_async(fs_sorter* s, int dtype, const void* host_in, void* host_out, uint64_t n) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n == 0) return FS_OK;
+  if (!host_in || !host_out) return fail(s, FS_E_INVALID, "host_in or host_out is NULL");
+  if ((rc = set_device(s))) return rc;
+  const size_t bytes = (size_t)n * key_bytes_of(dtype);
+  if (!s->h2d) {
+    FS_CUDA(s, cudaStreamCreateWithFlags(&s->h2d, cudaStreamNonBlocking));
+    FS_CUDA(s, cudaStreamCreateWithFlags(&s->d2h, cudaStreamNonBlocking));
+    FS_CUDA(s, cudaEventCreateWithFlags(&s->pipe_start, cudaEventDisableTiming));
+    for (auto& sl : s->pipe) {
+      FS_CUDA(s, cudaEventCreateWithFlags(&sl.in_done, cudaEventDisableTiming));
+      FS_CUDA(s, cudaEventCreateWithFlags(&sl.sorted, cudaEventDisableTiming));
+      FS_CUDA(s, cudaEventCreateWithFlags(&sl.out_done, cudaEventDisableTiming));
+    }
+  }
+  fs_sorter::PipeSlot& sl = s->pipe[s->pipe_next];
+  s->pipe_next ^= 1;
+  if (sl.bytes < bytes) {  // grow: the buffer's previous copy back must be done
+    if (sl.used) FS_CUDA(s, cudaEventSynchronize(sl.out_done));
+    if (sl.dkeys) FS_CUDA(s, cudaFree(sl.dkeys));
+    sl.dkeys = nullptr;
+    sl.bytes = 0;
+    const cudaError_t e = cudaMalloc(&sl.dkeys, bytes);
+    if (e != cudaSuccess) {
+      sl.dkeys = nullptr;
+      cudaGetLastError();
+      return fail(s, FS_E_OOM, "device allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+    }
+    sl.bytes = bytes;
+  }
+  // The first call after a synchronize orders the copy streams after the
+  // caller's work on the sorter's stream; later calls only wait for their
+  // own buffer (waiting on the stream again would wait for the previous
+  // call's sort and serialise the pipeline).
+  if (!s->pipe_open) {
+    FS_CUDA(s, cudaEventRecord(s->pipe_start, s->stream));
+    FS_CUDA(s, cudaStreamWaitEvent(s->h2d, s->pipe_start, 0));
+    FS_CUDA(s, cudaStreamWaitEvent(s->d2h, s->pipe_start, 0));
+    s->pipe_open = true;
+  }
+  if (n == 1) {  // nothing to sort: a host copy in order with the copies out
+    FS_CUDA(s, cudaMemcpyAsync(host_out, host_in, bytes, cudaMemcpyHostToHost, s->d2h));
+    FS_CUDA(s, cudaEventRecord(sl.out_done, s->d2h));
+    sl.used = true;
+    return FS_OK;
+  }
+  // copy in once this buffer's last copy out is done
+  if (sl.used) FS_CUDA(s, cudaStreamWaitEvent(s->h2d, sl.out_done, 0));
+  FS_CUDA(s, cudaMemcpyAsync(sl.dkeys, host_in, bytes, cudaMemcpyHostToDevice, s->h2d));
+  FS_CUDA(s, cudaEventRecord(sl.in_done, s->h2d));
+  // sort on the sorter's stream (its scratch is used by one sort at a time)
+  FS_CUDA(s, cudaStreamWaitEvent(s->stream, sl.in_done, 0));
+  if ((rc = fs_sort_keys(s, dtype, sl.dkeys, n, 0))) return rc;
+  FS_CUDA(s, cudaEventRecord(sl.sorted, s->stream));
+  // copy out
+  FS_CUDA(s, cudaStreamWaitEvent(s->d2h, sl.sorted, 0));
+  FS_CUDA(s, cudaMemcpyAsync(host_out, sl.dkeys, bytes, cudaMemcpyDeviceToHost, s->d2h));
+  FS_CUDA(s, cudaEventRecord(sl.out_done, s->d2h));
+  sl.used = true;
+  return FS_OK;
 }
 
 int fs_alloc(fs_sorter* s, size_t bytes, int managed, void** ptr) {

@@ -51,6 +51,7 @@ SIGNATURES = {
     "fs_set_kernel_timing": (_i32, [_vp, _i32]),
     "fs_last_kernel_times": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), _i32]),
     "fs_partition": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _i32]),
+    "fs_host_sort_keys_copy_async": (_i32, [_vp, _i32, _vp, _vp, _u64]),
     "fs_partition_count": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp]),
     "fs_partition_dispatch": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _i32]),
     "fs_ipc_export": (_i32, [_vp, _vp, _vp]),

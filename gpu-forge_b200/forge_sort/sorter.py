@@ -413,6 +413,14 @@ class GpuSorter:
                                                  ctypes.c_void_p(out_ptr), n, int(sync)))
         self._pending = self._pending or not sync
 
+    def host_sort_copy_async_ptr(self, dt, host_in: int, host_out: int, n: int) -> None:
+        """Enqueue host-memory out-of-place sort (H2D + sort + D2H) and return;
+        consecutive calls overlap their copies.  synchronize() waits."""
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_host_sort_keys_copy_async(self._h, _DT[name][0], ctypes.c_void_p(host_in),
+                                                            ctypes.c_void_p(host_out), n))
+        self._pending = True
+
     def host_sort_copy_ptr(self, dt, host_in: int, host_out: int, n: int) -> None:
         """Host-memory out-of-place sort: H2D + sort + D2H (synchronous)."""
         name = dtype_name(dt)

@@ -140,6 +140,20 @@ int fs_host_argsort(fs_sorter* s, int dtype, const void* host_keys,
 int fs_host_sort_keys_copy(fs_sorter* s, int dtype, const void* host_in,
                            void* host_out, uint64_t n);
 
+/* Enqueue an out-of-place sort of n keys in host memory (host_in -> GPU ->
+ * sort -> host_out) and return at once.  Consecutive calls overlap: the copy
+ * of one call's keys to the GPU runs while the previous call sorts and copies
+ * back (the sorter alternates between two device buffers and has copy
+ * streams of its own).  host_in and host_out must stay untouched until
+ * fs_synchronize returns; page-locked host memory (cudaHostAlloc) lets the
+ * copies overlap.  Work enqueued on the sorter's stream before the first call
+ * since the last fs_synchronize runs first; fs_synchronize waits for every
+ * call and makes later work on the sorter's stream wait for it too.  No counterpart in the reference (its
+ * sort_* calls are synchronous); this is the streaming form of
+ * fs_host_sort_keys_copy. */
+int fs_host_sort_keys_copy_async(fs_sorter* s, int dtype, const void* host_in,
+                                 void* host_out, uint64_t n);
+
 /* ---- per-kernel timing ---------------------------------------------------- */
 
 /* on != 0: record a CUDA event pair around every kernel the sorter launches,

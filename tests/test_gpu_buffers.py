@@ -123,3 +123,28 @@ def test_launch_count(sorter):
     k, v = orc.gen("u32", 1000, seed=2), np.arange(1000, dtype=np.uint32)
     sorter.sort_pairs_u32(k, v)  # payload: every pass ranks stably, one scatter each
     assert sorter.last_launch_count() == 3 + 3 * 4
+
+
+def test_async_host_sorts_overlap_and_match(sorter):
+    """fs_host_sort_keys_copy_async: a stream of calls (mixed types, sizes
+    that grow the two device buffers, n = 0 and 1), one synchronize, every
+    output bit-exact; inputs untouched."""
+    import torch
+    cases = [("u32", "u32", 1 << 20), ("f32", "f32_mix", 300_001), ("u64", "u64", 1 << 19),
+             ("u32", "skew_u32", 3 << 20), ("i64", "i64", 1), ("i32", "i32", 0), ("f64", "f64_logu", 77_777),
+             ("u32", "zipf_u32", 2 << 20)]
+    ins, outs, keep = [], [], []
+    for dt, dist, n in cases:
+        x = orc.gen(dist, n, seed=n + 3)
+        tdt = torch.int32 if x.itemsize == 4 else torch.int64
+        h_in = torch.from_numpy(np.ascontiguousarray(x).view(np.int32 if x.itemsize == 4 else np.int64)).pin_memory()
+        h_out = torch.zeros(n, dtype=tdt).pin_memory()
+        sorter.host_sort_copy_async_ptr(dt, h_in.data_ptr(), h_out.data_ptr(), n)
+        ins.append(h_in)
+        outs.append(h_out)
+        keep.append((dt, x))
+    sorter.synchronize()
+    for (dt, x), h_in, h_out in zip(keep, ins, outs):
+        bits = orc.BITS_DTYPE[dt]
+        assert np.array_equal(h_in.numpy().view(bits), np.ascontiguousarray(x).view(bits))
+        assert np.array_equal(h_out.numpy().view(bits), orc.sort_keys(x, dt).view(bits)), dt
