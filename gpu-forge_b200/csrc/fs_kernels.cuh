@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
       uint32_t* vdst = slot_final ? a.vfinal : a.vother;
       uint32_t f = PD_EXEC;
       if (i == 1) f |= PD_XF_IN | PD_FIRST;
-      if (i == 1 && !a.has_vals && a.unstable_first) f |= PD_UNSTABLE;
+      if (i == 1 && p == 0 && !a.has_vals && a.unstable_first) f |= PD_UNSTABLE;
       if (i == 1 && a.has_vals && a.vin == nullptr) f |= PD_SYNTH_IDX;
       if (i == m) f |= PD_XF_OUT;
       if (a.write_keys || i < m) f |= PD_WRITE_KEYS;
@@ -841,10 +841,10 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   __syncthreads();  // staging reads done, counters zeroed: next tile may start
 }
 
-// Which passes a scatter instantiation takes (the plan decides on the
-// device whether a pass ranks stably, so both instantiations are launched and
-// the one that does not match exits at once).  The rank method is compiled
-// in: SCATTER_UNSTABLE ranks with shared atomics, the others with ballots.
+// Which passes a scatter instantiation takes.  The rank method is compiled
+// in: SCATTER_UNSTABLE ranks with shared atomics and only runs a pass the
+// plan marked PD_UNSTABLE (pass 0 of a keys-only sort when it executes);
+// the others rank stably with ballots.
 enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1, SCATTER_STABLE = 2 };
 
 // CTAs loop over slices (c = blockIdx.x, +gridDim.x, ...); tiles of a slice

@@ -325,10 +325,11 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
     if (a.has_vals) {
       rc = launch_scatter<K, true, XF, StableCfg<K, true>, SCATTER_ANY>(e, p, n, sl, dg, 0ull);
       nl += 3;
-    } else if (a.unstable_first) {
+    } else if (a.unstable_first && p == 0) {
+      // pass 0, when it runs, is the first executed pass: it may rank
+      // unstably.  (If it is trivial, the stable pass 1 kernel ranks pass 1.)
       rc = launch_scatter<K, false, XF, UnstableCfg<K>, SCATTER_UNSTABLE>(e, p, n, sl, dg, 0ull);
-      if (!rc) rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_STABLE>(e, p, n, sl, dg, 0ull);
-      nl += 4;
+      nl += 3;
     } else {
       rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_ANY>(e, p, n, sl, dg, 0ull);
       nl += 3;

@@ -114,12 +114,12 @@ def test_device_pointer_checks(sorter):
 def test_launch_count(sorter):
     x = orc.gen("u32", 100_000, seed=1)
     sorter.sort_u32(x.copy())
-    # histogram, plan, per pass (count, scan, unstable-rank scatter,
-    # stable-rank scatter -- one of the two exits at once), finalize
-    assert sorter.last_launch_count() == 3 + 4 * 4
+    # first count, plan, per pass (count, scan, scatter -- pass 0 ranks
+    # unstably, the others stably), finalize
+    assert sorter.last_launch_count() == 3 + 3 * 4
     y = orc.gen("u64", 100_000, seed=1)
     sorter.sort_u64(y.copy())
-    assert sorter.last_launch_count() == 3 + 4 * 8
+    assert sorter.last_launch_count() == 3 + 3 * 8
     k, v = orc.gen("u32", 1000, seed=2), np.arange(1000, dtype=np.uint32)
     sorter.sort_pairs_u32(k, v)  # payload: every pass ranks stably, one scatter each
     assert sorter.last_launch_count() == 3 + 3 * 4
