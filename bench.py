@@ -3,20 +3,25 @@
 
 Workload: sort 2^32 u32 keys -- elements [0, 2^32) of
 the seed-42 xorshift64 stream, uniform over [0, 2^32) -- partitioned over N
-GPUs (strong scaling: total keys fixed).  N = 1 is the single-GPU onesweep
-radix sort; N > 1 is the sample sort (local sort, regular-sampling
-splitters, one NCCL all-to-all, merge).
+GPUs (strong scaling: total keys fixed).  N = 1 is the single-GPU LSD radix
+sort; N > 1 is the sample sort (regular-sampling splitters, one fused
+partition + exchange pass into the peers' inboxes over NVLink, local radix
+sort).
 
   value : sorted Mkeys/s, inputs resident in HBM, out-of-place device sort
           (the pristine input is re-read every step; 16 GiB >> 126 MB L2)
   e2e   : the same through the host API: pinned host keys -> device -> sort
-          -> pinned host output, every step
-  roofline : dominant kernel = one onesweep pass, algorithmic bytes per key
-          = 2 x key bytes (read + write), timed live with CUDA events
+          -> pinned host output, every step (streaming calls; the synchronous
+          call is reported beside it)
+  roofline : dominant kernel = the stable-rank scatter pass, algorithmic
+          bytes per key = 2 x key bytes (read + write), timed live with CUDA
+          events on the library's stream
   cpu_baseline : the oracle's parallel sort (C++ stand-in for rayon
           par_sort_unstable) on a bounded sample, rank 0 at N = 1
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --suite     # every BASELINE config on one GPU, one JSON
+                              # line each (not part of the driver contract)
 """
 from __future__ import annotations
 
@@ -48,6 +53,7 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile-steps", type=int, default=3)
+    p.add_argument("--suite", action="store_true", help="time every BASELINE config on one GPU")
     return p.parse_args()
 
 
@@ -513,8 +519,125 @@ def run_multi(args):
     tdist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ suite
+SUITE = [  # (config, op, dtype, generator, log2 n or n, alg bytes per key)
+    ("configs[0]", "keys", "u32", "u32", 1 << 20, 36),
+    ("configs[1]", "keys", "u32", "u32", 1 << 24, 36),
+    ("configs[1]", "keys", "i32", "i32", 1 << 24, 36),
+    ("configs[1]", "keys", "f32", "f32_mix", 1 << 24, 36),
+    ("configs[2]", "keys", "u64", "u64", 1 << 26, 136),
+    ("configs[2]", "keys", "i64", "i64", 1 << 26, 136),
+    ("configs[2]", "keys", "f64", "f64_logu", 1 << 26, 136),
+    ("configs[2]", "argsort", "f32", "f32_mix", 1 << 24, 64),
+    ("configs[3]", "pairs", "u32", "zipf_u32", 1 << 28, 68),
+    ("1G u32", "keys", "u32", "u32", 1 << 30, 36),
+    ("configs[4] skewed", "keys", "u32", "skew_u32", 1 << 32, 36),
+    ("configs[4] u64", "keys", "u64", "u64", 1 << 30, 136),
+]
+
+
+def run_suite(args):
+    """Every BASELINE config on one GPU: device-resident sorts (CUDA events,
+    median of the timed reps), plus the host-slice call (H2D + sort + D2H)
+    and the zero-copy SortBuffer path where the reference reports them."""
+    import numpy as np
+    import torch
+
+    import forge_sort
+    from forge_sort import _lib
+    from oracle import oracle as orc
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(device=dev)
+    sorter = forge_sort.GpuSorter.with_context(0, stream)
+    L = _lib.load()
+    peak, peak_kind = measured_peak_hbm()
+    gen_dev = {"u32": _lib.GEN_U32, "u64": _lib.GEN_U64, "skew_u32": _lib.GEN_SKEW_U32}
+
+    def timed(fn, reps):
+        ts = []
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                fn()
+            sorter.synchronize()
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                e1.synchronize()
+                ts.append(e0.elapsed_time(e1))
+        sorter.synchronize()
+        ts.sort()
+        return ts[len(ts) // 2]
+
+    for cfg, op, dt, gen, n, bpk in SUITE:
+        kb = 8 if dt in ("u64", "i64", "f64") else 4
+        tdt = torch.int32 if kb == 4 else torch.int64
+        if gen in gen_dev:
+            kin = torch.empty(n, dtype=tdt, device=dev)
+            assert L.fs_generate(gen_dev[gen], 42, 0, n, kin.data_ptr(), stream.cuda_stream) == 0
+            stream.synchronize()
+            host = None
+        else:
+            host = orc.gen(gen, n, seed=42)
+            kin = torch.from_numpy(np.ascontiguousarray(host).view(np.int32 if kb == 4 else np.int64)).to(dev)
+        reps = max(3, min(20, (1 << 28) // n * 3))
+        row = {"config": cfg, "op": op, "dtype": dt, "dist": gen, "n": n}
+        if op == "keys":
+            kout = torch.empty_like(kin)
+            ms = timed(lambda: sorter.sort_device_copy(dt, kin.data_ptr(), kout.data_ptr(), n, sync=False), reps)
+        elif op == "argsort":
+            idx = torch.empty(n, dtype=torch.int32, device=dev)
+            ms = timed(lambda: sorter.argsort_device(dt, kin.data_ptr(), idx.data_ptr(), n, sync=False), reps)
+        else:  # pairs through the zero-copy SortBuffer path (managed memory)
+            kb_buf = sorter.alloc_sort_buffer(dt, n)
+            vb_buf = sorter.alloc_sort_buffer("u32", n)
+            src = kin.cpu().numpy().view(np.uint32)
+            vals = np.arange(n, dtype=np.uint32)
+
+            def pairs_step():
+                kb_buf.copy_from_slice(src)
+                vb_buf.copy_from_slice(vals)
+                sorter.sort_pairs_buffer(kb_buf, vb_buf)
+            # device part only: keys/values resident, sort in place each rep
+            kd, vd = kin.clone(), torch.arange(n, dtype=torch.int32, device=dev)
+            kw, vw = torch.empty_like(kd), torch.empty_like(vd)
+
+            def dev_pairs():
+                kw.copy_(kd)
+                vw.copy_(vd)
+                sorter.sort_pairs_device(dt, kw.data_ptr(), vw.data_ptr(), n, sync=False)
+            copy_ms = timed(lambda: (kw.copy_(kd), vw.copy_(vd)), reps)
+            ms = timed(dev_pairs, reps) - copy_ms
+            t0 = time.perf_counter()
+            pairs_step()
+            row["sort_buffer_ms"] = round((time.perf_counter() - t0) * 1e3, 3)
+            kb_buf.free()
+            vb_buf.free()
+        row.update({"ms": round(ms, 4), "mkeys_s": round(n / (ms * 1e-3) / 1e6, 1),
+                    "alg_bytes_per_key": bpk,
+                    "hbm_frac": round(n * bpk / (ms * 1e-3) / 1e9 / peak, 4), "peak_kind": peak_kind})
+        if op == "keys" and n <= (1 << 24):  # the host-slice call, as the reference times it
+            h = host if host is not None else kin.cpu().numpy().view(orc.NP_DTYPE[dt])
+            hs = [np.array(h, copy=True) for _ in range(5)]
+            getattr(sorter, f"sort_{dt}")(np.array(h, copy=True))
+            t0 = time.perf_counter()
+            for a in hs:
+                getattr(sorter, f"sort_{dt}")(a)
+            hms = (time.perf_counter() - t0) / len(hs) * 1e3
+            row["host_slice"] = {"ms": round(hms, 3), "mkeys_s": round(n / (hms * 1e-3) / 1e6, 1)}
+        print(json.dumps(row), flush=True)
+        del kin
+        torch.cuda.empty_cache()
+    sorter.close()
+
+
 def main():
     args = parse()
+    if args.suite:
+        run_suite(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -8,9 +8,9 @@
 //   Result<T, SortError>      -> T, or throws forge_sort::SortError
 //   &mut [T] / &[T]           -> std::span<T> / std::span<const T>
 //   Vec<u32>                  -> std::vector<uint32_t>
-//   SortBuffer<T>             -> SortBuffer<T> (managed memory: host slices and
-//                                the kernels see the same pages, as
-//                                StorageModeShared did)
+//   SortBuffer<T>             -> SortBuffer<T> (page-locked host memory: host
+//                                slices at full speed; a sort copies it
+//                                through HBM at PCIe rate)
 //   MTLDevice + command queue -> CUDA device ordinal + cudaStream_t (void*)
 //   metal_buffer()            -> device_ptr()
 // Sealed SortKey (lib.rs:15-88) -> SortKey<T>, defined for the six key types
@@ -157,7 +157,7 @@ class SortBuffer {
   // Device address of element 0 (replaces metal_buffer()).
   void* device_ptr() const { return ptr_; }
 
-  // Wrap an allocation the caller owns (managed or device memory of at least
+  // Wrap an allocation the caller owns (page-locked host, managed or device memory of at least
   // capacity * sizeof(T) bytes); the SortBuffer will not free it.
   static SortBuffer from_raw_parts(void* ptr, std::size_t len, std::size_t capacity) {
     if (len > capacity)

@@ -7,8 +7,9 @@ variants); every call goes through libforgesort.so (include/forgesort.h).
 Type mapping from the Rust API:
   &mut [u32] / &[f32] ...   -> 1-D C-contiguous numpy arrays of that dtype
   Vec<u32> (argsort result) -> numpy uint32 array
-  SortBuffer<T>             -> SortBuffer (managed device memory; as_slice()
-                               is a numpy view the host reads in place)
+  SortBuffer<T>             -> SortBuffer (page-locked host memory; as_slice()
+                               is a numpy view the host reads in place, and
+                               sorting copies it through HBM at PCIe rate)
   MTLDevice / command queue -> CUDA device ordinal / cudaStream_t handle
   Result<_, SortError>      -> return value, or raises SortError
 """
@@ -81,9 +82,10 @@ def _check_array(a, name: str, want: str) -> np.ndarray:
 
 class SortBuffer:
     """A device buffer the host can also read and write (reference
-    SortBuffer<T>, src/lib.rs:160-281).  Backed by CUDA managed memory, so
-    as_slice()/as_mut_slice() are numpy views of the same pages the kernels
-    sort; sorting prefetches them to the GPU."""
+    SortBuffer<T>, src/lib.rs:160-281).  Backed by page-locked host memory, so
+    as_slice()/as_mut_slice() are numpy views the host reads and writes at
+    full speed; sorting copies the buffer into HBM, sorts and copies it back
+    (the discrete-GPU form of the reference's unified-memory zero-copy)."""
 
     def __init__(self, sorter: "GpuSorter", dt: str, ptr: int, length: int, capacity: int,
                  owned: bool = True):
@@ -152,7 +154,7 @@ class SortBuffer:
 
     @classmethod
     def from_raw_parts(cls, sorter: "GpuSorter", dt, ptr: int, length: int, capacity: int):
-        """Wrap an existing managed/device allocation (not owned)."""
+        """Wrap an existing page-locked host, managed or device allocation (not owned)."""
         if length > capacity:
             raise AssertionError(f"len {length} exceeds capacity {capacity}")
         return cls(sorter, dtype_name(dt), ptr, length, capacity, owned=False)
@@ -225,7 +227,7 @@ class GpuSorter:
         raise from_status(rc, self._err_text(), **kw)
 
     def _host_access(self) -> None:
-        # encode_sort leaves work in flight; the host must not touch managed
+        # encode_sort leaves work in flight; the host must not touch buffer
         # pages until it has finished.
         if self._pending:
             self.synchronize()

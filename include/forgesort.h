@@ -83,17 +83,24 @@ int fs_synchronize(fs_sorter* s);
 
 /* ---- memory (SortBuffer backing) --------------------------------------- */
 
-/* Allocate `bytes` on the sorter's device.  managed != 0 gives memory that the
- * host may also read and write through the same pointer (cudaMallocManaged),
- * which is what SortBuffer::as_slice/as_mut_slice rely on
- * (src/lib.rs:694-706, src/metal_helpers.rs:194-202).  Sorting a managed
- * buffer prefetches it to the device first. */
+/* managed == 0: allocate `bytes` of device memory (cudaMalloc) for the
+ * sorter's device.  managed != 0: a SortBuffer backing -- page-locked host
+ * memory (cudaHostAlloc, portable + mapped) that the host reads and writes at
+ * full speed through the same pointer, which is what
+ * SortBuffer::as_slice/as_mut_slice rely on (src/lib.rs:694-706,
+ * src/metal_helpers.rs:194-202).  The sorts below accept such a pointer:
+ * they copy it into device staging memory at PCIe rate, sort in HBM and copy
+ * it back, all on the sorter's stream.  (Managed memory from
+ * cudaMallocManaged also works, prefetched to the device; but the host's
+ * first read of pages that came back from the GPU maps them one fault at a
+ * time: 436 ms for 1 GB measured, against ~20 ms for the copy back.) */
 int fs_alloc(fs_sorter* s, size_t bytes, int managed, void** ptr);
 int fs_free(fs_sorter* s, void* ptr);
 
 /* ---- device-resident sorts (zero-copy path) ----------------------------- */
 
-/* Sort n keys of type `dtype` in place at device (or managed) pointer `keys`.
+/* Sort n keys of type `dtype` in place at `keys`: device memory, managed
+ * memory, or page-locked host memory (staged through the device).
  * Order: unsigned order for u32/u64, signed for i32/i64, IEEE totalOrder
  * (Rust f32::total_cmp) for f32/f64.  sync != 0 waits for completion and
  * reports device failures; sync == 0 only enqueues (encode_sort semantics:
