@@ -54,6 +54,7 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile-steps", type=int, default=3)
     p.add_argument("--suite", action="store_true", help="time every BASELINE config on one GPU")
+    p.add_argument("--only", default="", help="--suite: run only the rows whose config or op contains this")
     return p.parse_args()
 
 
@@ -520,20 +521,44 @@ def run_multi(args):
 
 
 # ------------------------------------------------------------------ suite
-SUITE = [  # (config, op, dtype, generator, log2 n or n, alg bytes per key)
-    ("configs[0]", "keys", "u32", "u32", 1 << 20, 36),
-    ("configs[1]", "keys", "u32", "u32", 1 << 24, 36),
-    ("configs[1]", "keys", "i32", "i32", 1 << 24, 36),
-    ("configs[1]", "keys", "f32", "f32_mix", 1 << 24, 36),
-    ("configs[2]", "keys", "u64", "u64", 1 << 26, 136),
-    ("configs[2]", "keys", "i64", "i64", 1 << 26, 136),
-    ("configs[2]", "keys", "f64", "f64_logu", 1 << 26, 136),
-    ("configs[2]", "argsort", "f32", "f32_mix", 1 << 24, 64),
-    ("configs[3]", "pairs", "u32", "zipf_u32", 1 << 28, 68),
-    ("1G u32", "keys", "u32", "u32", 1 << 30, 36),
-    ("configs[4] skewed", "keys", "u32", "skew_u32", 1 << 32, 36),
-    ("configs[4] u64", "keys", "u64", "u64", 1 << 30, 136),
+SUITE = [  # (config, op, dtype, generator, n)
+    ("configs[0]", "keys", "u32", "u32", 1 << 20),
+    ("configs[1]", "keys", "u32", "u32", 1 << 24),
+    ("configs[1]", "keys", "i32", "i32", 1 << 24),
+    ("configs[1]", "keys", "f32", "f32_mix", 1 << 24),
+    ("configs[2]", "keys", "u64", "u64", 1 << 26),
+    ("configs[2]", "keys", "i64", "i64", 1 << 26),
+    ("configs[2]", "keys", "f64", "f64_logu", 1 << 26),
+    ("configs[2]", "argsort", "f32", "f32_mix", 1 << 24),
+    ("configs[3]", "pairs", "u32", "zipf_u32", 1 << 28),
+    ("1G u32", "keys", "u32", "u32", 1 << 30),
+    ("configs[4] skewed", "keys", "u32", "skew_u32", 1 << 32),
+    ("configs[4] u64", "keys", "u64", "u64", 1 << 30),
+    ("configs[4] sample-sort kernels, 2 buckets", "dispatch", "u32", "u32", 1 << 28),
+    ("configs[4] sample-sort kernels, 8 buckets", "dispatch", "u32", "u32", 1 << 28),
 ]
+
+
+def alg_bytes_per_key(op: str, kb: int, passes: int) -> int:
+    """Bytes an LSD sort must move per key with `passes` executed digit
+    passes: one read to count, then per pass the key read and written
+    (argsort: plus the index, synthesised on the first pass; pairs: plus the
+    u32 value read and written)."""
+    if op == "keys":
+        return kb * (1 + 2 * passes)
+    if op == "argsort":
+        return kb * (1 + 2 * passes) + 8 * passes - 4
+    return kb * (1 + 2 * passes) + 8 * passes
+
+
+def executed_passes(host, dt: str) -> int:
+    """Digit passes that run: bytes of the order-transformed keys that vary."""
+    import numpy as np
+    from forge_sort.samplesort import ordered_bits
+    o = ordered_bits(host, dt)
+    varying = int(np.bitwise_or.reduce(o)) & ~int(np.bitwise_and.reduce(o))
+    kb = 8 if dt in ("u64", "i64", "f64") else 4
+    return sum(1 for b in range(kb) if (varying >> (8 * b)) & 0xff)
 
 
 def run_suite(args):
@@ -571,7 +596,9 @@ def run_suite(args):
         ts.sort()
         return ts[len(ts) // 2]
 
-    for cfg, op, dt, gen, n, bpk in SUITE:
+    for cfg, op, dt, gen, n in SUITE:
+        if args.only and args.only not in cfg and args.only != op:
+            continue
         kb = 8 if dt in ("u64", "i64", "f64") else 4
         tdt = torch.int32 if kb == 4 else torch.int64
         if gen in gen_dev:
@@ -583,10 +610,42 @@ def run_suite(args):
             host = orc.gen(gen, n, seed=42)
             kin = torch.from_numpy(np.ascontiguousarray(host).view(np.int32 if kb == 4 else np.int64)).to(dev)
         reps = max(3, min(20, (1 << 28) // n * 3))
-        row = {"config": cfg, "op": op, "dtype": dt, "dist": gen, "n": n}
+        passes = executed_passes(host, dt) if host is not None else kb  # uniform device data: all vary
+        bpk = alg_bytes_per_key(op, kb, passes) if op != "dispatch" else 3 * kb
+        row = {"config": cfg, "op": op, "dtype": dt, "dist": gen, "n": n, "executed_passes": passes}
         if op == "keys":
             kout = torch.empty_like(kin)
             ms = timed(lambda: sorter.sort_device_copy(dt, kin.data_ptr(), kout.data_ptr(), n, sync=False), reps)
+        elif op == "dispatch":
+            # the sample sort's count + dispatch kernels on one GPU: splitters
+            # at the bucket quantiles, every destination on this GPU (the
+            # kernels are the same; over NVLink the stores go to peers)
+            G = 2 if "2 buckets" in cfg else 8
+            spl = np.array([(j << 32) // G for j in range(1, G)], dtype=np.uint64).astype(np.uint32)
+            sk = torch.from_numpy(spl.view(np.int32)).to(dev)
+            sg = torch.zeros(G - 1, dtype=torch.int64, device=dev)
+            out = torch.empty_like(kin)
+            cnt = sorter.partition_count(dt, kin.data_ptr(), n, 0, sk.data_ptr(), sg.data_ptr(), G - 1)
+            dst = [out.data_ptr() + kb * sum(cnt[:b]) for b in range(G)]
+            sorter.set_kernel_timing(True)
+            kc, kd = [], []
+            for _ in range(reps):
+                sorter.partition_count(dt, kin.data_ptr(), n, 0, sk.data_ptr(), sg.data_ptr(), G - 1)
+                kc.append(sorter.last_kernel_times()[0])
+                sorter.partition_dispatch(dt, kin.data_ptr(), n, 0, sk.data_ptr(), sg.data_ptr(), G - 1, dst,
+                                          sync=True)
+                kd.append(sum(sorter.last_kernel_times()))
+            sorter.set_kernel_timing(False)
+            kc.sort()
+            kd.sort()
+            ms = kc[len(kc) // 2] + kd[len(kd) // 2]
+            row["count_ms"] = round(kc[len(kc) // 2], 4)
+            row["dispatch_ms"] = round(kd[len(kd) // 2], 4)
+            row["count_frac"] = round(n * kb / (row["count_ms"] * 1e-3) / 1e9 / peak, 4)
+            row["dispatch_frac"] = round(n * 2 * kb / (row["dispatch_ms"] * 1e-3) / 1e9 / peak, 4)
+            head = out[: min(cnt[0], 1 << 20)].cpu().numpy().view(np.uint32)
+            tail = out[n - min(cnt[-1], 1 << 20):].cpu().numpy().view(np.uint32)
+            assert (head < spl[0]).all() and (tail >= spl[-1]).all(), "dispatch put keys in the wrong bucket"
         elif op == "argsort":
             idx = torch.empty(n, dtype=torch.int32, device=dev)
             ms = timed(lambda: sorter.argsort_device(dt, kin.data_ptr(), idx.data_ptr(), n, sync=False), reps)
