@@ -73,7 +73,7 @@ def config(args, world):
         "keys_per_gpu": (1 << args.log2n) // world,
         "key_type": args.dtype,
         "generator": "xorshift64 seed 42 (element i = state after i+1 steps; shard r = elements [r*m,(r+1)*m))",
-        "parallelism": f"sample sort x{world}" if world > 1 else "single GPU onesweep",
+        "parallelism": f"sample sort x{world}" if world > 1 else "single GPU LSD radix sort",
         "l2": "inputs (>= 2 GiB per GPU) larger than the 126 MB L2; no flush needed",
     }
 

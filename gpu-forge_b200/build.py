@@ -24,7 +24,7 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
 # target -> sources (the first is compiled; headers listed for staleness)
 TARGETS = {
     os.path.join(PKG, "forge_sort", "libforgesort.so"): {
-        "srcs": ["fs_sort.cu", "fs_datagen.cu"],
+        "srcs": ["fs_sort.cu", "fs_multi.cu", "fs_datagen.cu"],
         "deps": ["fs_device.cuh", "fs_kernels.cuh"],
         "hdrs": ["forgesort.h", "forgesort_bench.h"],
         "libs": [],

@@ -292,4 +292,54 @@ class GpuSorter {
   fs_sorter* h_ = nullptr;
 };
 
+// ---- MultiGpuSorter (no reference counterpart) ---------------------------------
+// The sample sort over several GPUs of this process (fs_mg_*): shards in,
+// pieces of the globally sorted sequence out, piece i on devices[i].
+class MultiGpuSorter {
+ public:
+  explicit MultiGpuSorter(const std::vector<int>& devices) {
+    const int rc = fs_mg_create(devices.data(), (int)devices.size(), &h_);
+    if (rc != FS_OK) {
+      h_ = nullptr;
+      detail::check(rc, nullptr);
+    }
+    g_ = devices.size();
+  }
+  MultiGpuSorter(const MultiGpuSorter&) = delete;
+  MultiGpuSorter& operator=(const MultiGpuSorter&) = delete;
+  ~MultiGpuSorter() {
+    if (h_) fs_mg_destroy(h_);
+  }
+
+  // shards[i]: device pointer on devices[i] with shard_n[i] keys of T;
+  // out[i]: device pointer on devices[i] with room for out_cap[i] keys.
+  // Returns the piece sizes.  Throws std::length_error (with the sizes
+  // needed in `needed`) when a piece would not fit its out_cap.
+  template <typename T>
+  std::vector<uint64_t> sort(const std::vector<T*>& shards, const std::vector<uint64_t>& shard_n,
+                             const std::vector<T*>& out, const std::vector<uint64_t>& out_cap,
+                             std::vector<uint64_t>* needed = nullptr) {
+    if (shards.size() != g_ || shard_n.size() != g_ || out.size() != g_ || out_cap.size() != g_)
+      throw std::invalid_argument("one shard and one output per device");
+    std::vector<void*> sp(shards.begin(), shards.end()), op(out.begin(), out.end());
+    std::vector<uint64_t> out_n(g_);
+    const int rc = fs_mg_sort_keys(h_, SortKey<T>::DTYPE, sp.data(), shard_n.data(), op.data(), out_cap.data(),
+                                   out_n.data());
+    if (rc == FS_E_INVALID) {
+      bool over = false;
+      for (size_t i = 0; i < g_; ++i) over = over || out_n[i] > out_cap[i];
+      if (over) {
+        if (needed) *needed = out_n;
+        throw std::length_error(fs_mg_last_error(h_));
+      }
+    }
+    if (rc != FS_OK) throw SortError::gpu_execution(fs_mg_last_error(h_));
+    return out_n;
+  }
+
+ private:
+  fs_mg* h_ = nullptr;
+  size_t g_ = 0;
+};
+
 }  // namespace forge_sort

@@ -1,6 +1,6 @@
-// fs_device.cuh -- device-side building blocks of the onesweep radix sort:
-// key-order transforms, digit extraction, lookback status words, and the
-// device-resident control block the host enqueues against.
+// fs_device.cuh -- device-side building blocks of the LSD radix sort:
+// key-order transforms, digit extraction, and the device-resident control
+// block the host enqueues against.
 #pragma once
 
 #include <cstddef>
@@ -89,8 +89,7 @@ enum PassFlags : uint32_t {
   PD_XF_OUT = 1u << 2,      // last executed pass: apply the inverse transform
   PD_SYNTH_IDX = 1u << 3,   // payload = input position (argsort), not loaded
   PD_WRITE_KEYS = 1u << 4,  // write keys (argsort's last pass does not)
-  PD_FIRST = 1u << 5,       // first executed pass: slice counts come from the
-                            // upfront histogram (input order is unchanged)
+  PD_FIRST = 1u << 5,       // first executed pass (reads the caller's keys)
   PD_UNSTABLE = 1u << 6,    // keys-only first pass: order among equal digits is free
 };
 

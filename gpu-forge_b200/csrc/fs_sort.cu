@@ -1,7 +1,8 @@
 // fs_sort.cu -- host orchestration and the C ABI (include/forgesort.h) of the
-// single-GPU sort.  One fs_sorter = one device + one stream + a grow-only
-// scratch arena; every sort is enqueued as
-//   upfront_hist -> plan -> P x onesweep -> finalize
+// single-GPU sort and the sample sort's partition kernels.  One fs_sorter =
+// one device + one stream + a grow-only scratch arena; every sort is
+// enqueued as
+//   first count -> plan -> P x (count, slice scan, scatter) -> finalize
 // on that stream (P = key bytes), with no host round trip in between.
 #include "forgesort.h"
 #include "fs_kernels.cuh"
@@ -443,6 +444,7 @@ Exec exec_of(fs_sorter* s) {
 
 // The sorter's path: size the slices, grow its scratch, enqueue.
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
+  s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
   Exec e = exec_of(s);
   const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);
   int rc = ensure_slice_buffers(s, sl);
@@ -461,6 +463,7 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
                       const void* spl_keys, const uint64_t* spl_gpos, int nsplit, unsigned long long* counts_out) {
   using D = SplitterDigit<K, XF>;
   const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
+  s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
   Exec e = exec_of(s);
   const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
   int rc = ensure_slice_buffers(s, sl);
@@ -683,7 +686,7 @@ int fs_create(int device, void* stream, fs_sorter** out) {
   *s->host_err = 0;
   e = cudaHostGetDevicePointer((void**)&s->host_err_dev, s->host_err, 0);
   if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaHostGetDevicePointer"));
-  if (const char* t = getenv("FORGESORT_LOOKBACK_TIMEOUT_MS")) {
+  if (const char* t = getenv("FORGESORT_WAIT_TIMEOUT_MS")) {
     const long long ms = atoll(t);
     if (ms > 0) s->timeout_ns = (uint64_t)ms * 1000000ull;
   }

@@ -1,0 +1,74 @@
+"""MultiGpuSorter -- the sample sort over several GPUs of this process
+(fs_mg_* in include/forgesort.h).
+
+No counterpart in the reference (forge-sort is single-device).  The shards
+are torch tensors, one per device; sort() returns the pieces of the globally
+sorted sequence, piece i on device i, and concatenating them in device order
+gives the sorted input bit for bit.  The one-process-per-GPU form of the
+same algorithm is samplesort.SampleSorter.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Sequence
+
+from . import _lib
+from .errors import from_status
+from .sorter import _DT, dtype_name
+
+
+class MultiGpuSorter:
+    def __init__(self, devices: Sequence[int]):
+        L = _lib.load()
+        arr = (ctypes.c_int * len(devices))(*[int(d) for d in devices])
+        h = ctypes.c_void_p()
+        rc = L.fs_mg_create(arr, len(devices), ctypes.byref(h))
+        if rc != _lib.OK:
+            raise from_status(rc, L.fs_last_error(None).decode() or "fs_mg_create failed")
+        self._h = h
+        self.devices = [int(d) for d in devices]
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.load().fs_mg_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def sort(self, dt, shards: List, headroom: float = 1.125) -> List:
+        """Sort the concatenation of `shards` (1-D torch tensors holding raw
+        key bits, shard i on devices[i]); returns the sorted pieces."""
+        import torch
+        name = dtype_name(dt)
+        G = len(self.devices)
+        if len(shards) != G:
+            raise ValueError(f"{len(shards)} shards for {G} devices")
+        for i, t in enumerate(shards):
+            if t.device.type != "cuda" or t.device.index != self.devices[i] or not t.is_contiguous():
+                raise ValueError(f"shard {i} must be a contiguous tensor on cuda:{self.devices[i]}")
+            if t.element_size() != _DT[name][2]:
+                raise TypeError(f"shard {i} has {t.element_size()}-byte elements, {name} needs {_DT[name][2]}")
+        total = sum(t.numel() for t in shards)
+        cap = [int(total / G * headroom) + 1024] * G
+        L = _lib.load()
+        U64 = ctypes.c_uint64 * G
+        PV = ctypes.c_void_p * G
+        for _attempt in range(2):
+            outs = [torch.empty(cap[i], dtype=shards[i].dtype, device=shards[i].device) for i in range(G)]
+            for t in shards:
+                torch.cuda.current_stream(t.device).synchronize()  # shards ready
+            out_n = U64()
+            rc = L.fs_mg_sort_keys(self._h, _DT[name][0], PV(*[t.data_ptr() for t in shards]),
+                                   U64(*[t.numel() for t in shards]), PV(*[t.data_ptr() for t in outs]),
+                                   U64(*cap), out_n)
+            if rc == _lib.OK:
+                return [outs[i][: out_n[i]] for i in range(G)]
+            if rc == _lib.E_INVALID and any(out_n[i] > cap[i] for i in range(G)):
+                cap = [max(cap[i], int(out_n[i])) for i in range(G)]  # resize and retry once
+                continue
+            raise from_status(rc, L.fs_mg_last_error(self._h).decode())
+        raise RuntimeError("MultiGpuSorter: output sizing failed")

@@ -219,6 +219,33 @@ int fs_ipc_export(fs_sorter* s, void* dev_ptr, void* handle_out);
 int fs_ipc_open(fs_sorter* s, const void* handle, void** peer_ptr);
 int fs_ipc_close(fs_sorter* s, void* peer_ptr);
 
+/* ---- several GPUs of one process (MultiGpuSorter) ----------------------- */
+
+/* The sample sort driven from one process: one sorter (own stream) per
+ * device, peer access enabled between every pair; fails with
+ * FS_E_DEVICE_NOT_FOUND when a pair cannot reach each other.  1 <= g <= 16
+ * distinct device ordinals.  No counterpart in the reference (single-device
+ * only); the one-process-per-GPU form of the same algorithm is the Python
+ * SampleSorter over torch.distributed. */
+typedef struct fs_mg fs_mg;
+int fs_mg_create(const int* devices, int g, fs_mg** out);
+int fs_mg_destroy(fs_mg* mg);
+const char* fs_mg_last_error(const fs_mg* mg);
+
+/* Sort the concatenation shards[0] .. shards[g-1] (shard i: shard_n[i] keys
+ * of `dtype` in device memory of devices[i], ready on that device's legacy
+ * default stream; not modified).  On return out[i] (device memory of
+ * devices[i], room for out_cap[i] keys) holds the i-th piece of the sorted
+ * sequence and out_n[i] its length: concatenating the pieces in device order
+ * gives the sorted keys, bit-exact with fs_sort_keys on the whole input.
+ * Splitters come from regular samples with (key, global position) order, so
+ * pieces stay within a few percent of the mean size even for skewed or
+ * all-equal keys; if a piece would exceed its out_cap, nothing is sorted,
+ * out_n holds the sizes needed and the call returns FS_E_INVALID. */
+int fs_mg_sort_keys(fs_mg* mg, int dtype, void* const* shards,
+                    const uint64_t* shard_n, void* const* out,
+                    const uint64_t* out_cap, uint64_t* out_n);
+
 /* ---- allocation-free form ------------------------------------------------ */
 
 /* Sort n keys in place at `keys` (device memory of the current device),
@@ -235,7 +262,7 @@ int fs_ipc_close(fs_sorter* s, void* peer_ptr);
  * Its scratch is one fixed device array inside this library, sized for 4 MiB
  * of keys (2^20 u32/i32/f32 or 2^19 u64/i64/f64 keys); larger n returns
  * FS_E_INVALID with the limit in fs_last_error(NULL).  Every GPU that loads
- * the library holds that array (about 6.6 MB) until the process exits.
+ * the library holds that array (about 4.6 MB) until the process exits.
  *
  * The first call on a device looks up the array's device address (with that
  * device current); make that first call before any stream capture.  All
