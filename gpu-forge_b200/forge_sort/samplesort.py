@@ -55,6 +55,25 @@ def ordered_bits(raw: np.ndarray, dt: str) -> np.ndarray:
     return x
 
 
+def sample_sort_keys(torch, raw, dt: str):
+    """int64 keys whose signed order is the sort order of the raw key bits in
+    `raw` (int32 / int64 tensor): the order transform, then for 64-bit keys
+    the sign bit flipped so that unsigned order reads as signed order."""
+    if _WIDTH[dt] == 32:
+        x = raw.to(torch.int64) & 0xFFFFFFFF
+        if dt == "i32":
+            return x ^ 0x80000000
+        if dt == "f32":
+            return torch.where((x & 0x80000000) != 0, x ^ 0xFFFFFFFF, x ^ 0x80000000)
+        return x
+    lo = torch.iinfo(torch.int64).min
+    if dt == "i64":
+        return raw.clone()
+    if dt == "f64":
+        return torch.where(raw < 0, ~raw ^ lo, raw)
+    return raw ^ lo  # u64
+
+
 def choose_splitters(samples_ordered: np.ndarray, samples_gpos: np.ndarray, ranks: int,
                      per_rank: int) -> np.ndarray:
     """Indices (into the gathered sample arrays) of the G-1 splitters: every
@@ -220,6 +239,7 @@ class SampleSorter:
         self.group = group
         self.per_rank = samples_per_rank
         self.last: Optional[SampleSortStats] = None
+        self._pos_cache = {}
 
     def _world(self):
         return self.dist.get_world_size(self.group), self.dist.get_rank(self.group)
@@ -237,30 +257,37 @@ class SampleSorter:
             self.last = SampleSortStats([m], [m])
             return self.ops.sort(dt, keys)
 
-        # 1. regular samples with their global positions -> splitters
+        # 1. regular samples with their global positions -> splitters, on the
+        # keys' device: gather, one stable sort of the G*S sample keys (ties
+        # in (rank, sample) order), then only the G-1 picks go to the host
         S = self.per_rank
-        pos = sample_positions(m, S)
-        raw = keys[torch.from_numpy(pos).to(dev)].cpu().numpy() if m else np.zeros(0, keys.cpu().numpy().dtype)
-        ords = ordered_bits(raw, dt) if m else np.zeros(0, np.uint64)
-        gpos = (pos + gpos_base).astype(np.uint64)
-        # fixed-size exchange: pad empty shards with maximal tuples (never picked
-        # below index (G-1)*S unless most shards are empty; still a valid split)
-        if m == 0:
-            ords = np.full(S, np.iinfo(np.uint64).max, np.uint64)
-            gpos = np.full(S, np.iinfo(np.uint64).max, np.uint64)
-            raw = np.zeros(S, dtype=np.int32 if _WIDTH[dt] == 32 else np.int64)
-        mine = np.stack([ords.view(np.int64), gpos.view(np.int64),
-                         np.ascontiguousarray(raw).view(_BITS[dt]).astype(np.uint64).view(np.int64)], axis=1)
-        t_mine = torch.from_numpy(np.ascontiguousarray(mine)).to(dev)
-        gathered = [torch.empty_like(t_mine) for _ in range(G)]
-        dist.all_gather(gathered, t_mine, group=self.group)
-        allv = torch.cat(gathered).cpu().numpy()
-        a_ord = allv[:, 0].view(np.uint64)
-        a_gpos = allv[:, 1].view(np.uint64)
-        a_raw = allv[:, 2].view(np.uint64)
-        picks = choose_splitters(a_ord, a_gpos, G, S)
-        spl_raw = a_raw[picks].astype(_BITS[dt])
-        spl_gpos = a_gpos[picks]
+        wide = _WIDTH[dt] == 64
+        if m:
+            key = self._pos_cache.get((m, S, str(dev)))
+            if key is None:
+                key = torch.from_numpy(sample_positions(m, S)).to(dev)
+                self._pos_cache = {(m, S, str(dev)): key}
+            raw = keys[key]
+            skey = sample_sort_keys(torch, raw, dt)
+            gpos = key + gpos_base
+            raw64 = raw.to(torch.int64) if not wide else raw
+            if not wide:
+                raw64 = raw64 & 0xFFFFFFFF
+        else:  # an empty shard sends maximal tuples (never picked unless most shards are empty)
+            big = torch.iinfo(torch.int64).max
+            skey = torch.full((S,), big, dtype=torch.int64, device=dev)
+            gpos = torch.full((S,), big, dtype=torch.int64, device=dev)
+            raw64 = torch.zeros(S, dtype=torch.int64, device=dev)
+        mine = torch.stack([skey, gpos, raw64], dim=1).contiguous()
+        gathered = [torch.empty_like(mine) for _ in range(G)]
+        dist.all_gather(gathered, mine, group=self.group)
+        allv = torch.cat(gathered)
+        order = torch.sort(allv[:, 0], stable=True).indices
+        sel = allv[order[torch.arange(1, G, device=allv.device) * S]].cpu().numpy()
+        # splitters ascending by (key, global position), as the partition searches them
+        sel = sel[np.lexsort((sel[:, 1].view(np.uint64), sel[:, 0]))]
+        spl_raw = sel[:, 2].view(np.uint64).astype(_BITS[dt])
+        spl_gpos = sel[:, 1].view(np.uint64)
 
         # 2-4 on GPUs: dispatch straight into the peers' inboxes, local sort
         if getattr(self.ops, "dispatch", False):

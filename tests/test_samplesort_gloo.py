@@ -129,3 +129,18 @@ def test_choose_splitters_matches_lexicographic_order(distinct):
     want = [order[j * S] for j in range(1, G)]
     got = choose_splitters(keys, gpos, G, S)
     assert [(keys[i], gpos[i]) for i in got] == [(keys[i], gpos[i]) for i in want]
+
+
+@pytest.mark.parametrize("dt", ["u32", "i32", "f32", "u64", "i64", "f64"])
+def test_sample_sort_keys_order_matches_ordered_bits(dt):
+    """The device-side sample keys (signed int64 order) sort like the
+    oracle's order transform."""
+    import torch
+    from forge_sort.samplesort import ordered_bits, sample_sort_keys
+    from oracle import oracle as orc
+    gen = {"u32": "u32", "i32": "i32", "f32": "f32_mix", "u64": "u64", "i64": "i64", "f64": "f64_logu"}[dt]
+    x = orc.gen(gen, 5000, seed=11)
+    iv = np.int32 if x.itemsize == 4 else np.int64
+    k = sample_sort_keys(torch, torch.from_numpy(np.ascontiguousarray(x).view(iv)), dt).numpy()
+    o = ordered_bits(x, dt)
+    assert np.array_equal(np.argsort(k, kind="stable"), np.argsort(o, kind="stable"))
