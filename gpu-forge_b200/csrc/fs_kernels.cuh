@@ -110,6 +110,7 @@ struct SplitterDigit {
   const K* s_keys = nullptr;
   const uint64_t* s_gpos = nullptr;
   uint32_t top = 0;  // largest power of two <= nsplit (0 if none)
+  K r[7] = {};       // up to 7 splitters (8 GPUs) in registers, padded with the largest key
   static constexpr int DIGITS = RADIX;
   static constexpr bool STAGE = true;  // digits staged in shared memory
   static constexpr bool DISPATCH = false;
@@ -122,11 +123,12 @@ struct SplitterDigit {
     __builtin_assume(__isShared(s_keys) && __isShared(s_gpos));
     uint32_t pos = 0;
     if (top <= 4) {
-      // up to 7 splitters (8 GPUs): three fixed steps over the copy, whose
-      // entries nsplit..7 hold the largest key (never below k)
-      pos += s_keys[3] < k ? 4u : 0u;
-      pos += s_keys[pos + 1] < k ? 2u : 0u;
-      pos += s_keys[pos] < k ? 1u : 0u;
+      // up to 7 splitters (8 GPUs): three fixed steps over registers, whose
+      // entries nsplit..6 hold the largest key (never below k)
+      pos = r[3] < k ? 4u : 0u;
+      pos += (pos ? r[5] : r[1]) < k ? 2u : 0u;
+      const K m0 = (pos & 4) ? ((pos & 2) ? r[6] : r[4]) : ((pos & 2) ? r[2] : r[0]);
+      pos += m0 < k ? 1u : 0u;
     } else {
       for (uint32_t step = top; step != 0; step >>= 1) {
         const uint32_t j = pos + step - 1;
@@ -149,6 +151,8 @@ struct SplitterDigit {
     s_keys = sk;
     s_gpos = sg;
     top = nsplit > 0 ? 1u << (31 - __clz(nsplit)) : 0u;
+#pragma unroll
+    for (int i = 0; i < 7; ++i) r[i] = i < nsplit ? to_ordered<K, XF>(keys[i]) : ~K(0);
   }
 };
 

@@ -150,7 +150,8 @@ template <> struct UnstableCfg<uint64_t> {
 #define FS_PART_IPT 8
 #endif
 template <typename K> struct PartCfg {
-  static constexpr int BLOCK = 256, IPT = FS_PART_IPT, MINB = FS_PART_MINB;
+  // 64-bit keys need the registers of 3 CTAs/SM (the splitters sit in registers)
+  static constexpr int BLOCK = 256, IPT = FS_PART_IPT, MINB = sizeof(K) == 8 ? 3 : FS_PART_MINB;
   static_assert(StableCfg<K, false>::BLOCK * StableCfg<K, false>::IPT % (BLOCK * IPT) == 0,
                 "partition tiles must divide the slice unit");
 };
