@@ -14,11 +14,14 @@
 // then:
 //   k_finalize       copy-back / iota when the plan needs it; error hand-off
 //
-// The array is cut into as many contiguous slices as the scatter kernel keeps
-// CTAs resident, so no CTA ever waits on another: the offsets a slice needs
-// come from the counts, not from a chained scan across concurrently running
-// tiles.  That costs one extra read of the keys per pass after the first and
-// removes the latency-bound inter-CTA dependency chain.
+// The array is cut into contiguous slices (12 per SM, whole tiles each) that
+// the scatter CTAs take in turn; no CTA ever waits on another: the offsets a
+// slice needs come from the counts, not from a chained scan across
+// concurrently running tiles.  That costs one extra read of the keys per pass
+// after the first and removes the latency-bound inter-CTA dependency chain.
+// The sample sort's partition reuses count, scan and scatter with the
+// splitter bucket as the digit (k_bucket_hist, SplitterDigit, and
+// SplitterDispatch, which stores each bucket into another GPU's inbox).
 //
 // Replaces the reference pipeline sort_msd_histogram -> sort_msd_prep ->
 // sort_msd_atomic_scatter -> sort_inner_fused (+ sort_transform_*,
@@ -849,7 +852,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
 // in: SCATTER_UNSTABLE ranks with shared atomics and only runs a pass the
 // plan marked PD_UNSTABLE (pass 0 of a keys-only sort when it executes);
 // the others rank stably with ballots.
-enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1, SCATTER_STABLE = 2 };
+enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1 };
 
 // CTAs loop over slices (c = blockIdx.x, +gridDim.x, ...); tiles of a slice
 // are processed in order with per-digit running offsets.  The next tile's
@@ -877,7 +880,6 @@ __global__ void __launch_bounds__(BLOCK, MINB)
   const PassDesc pd = ctl->pass[pass];
   if (!(pd.flags & PD_EXEC)) return;
   if (MODE == SCATTER_UNSTABLE && !(pd.flags & PD_UNSTABLE)) return;
-  if (MODE == SCATTER_STABLE && (pd.flags & PD_UNSTABLE)) return;
   const K* kin = static_cast<const K*>(pd.kin);
   K* kout = static_cast<K*>(pd.kout);
   const bool copy_vals = VALS && !(pd.flags & PD_SYNTH_IDX);
