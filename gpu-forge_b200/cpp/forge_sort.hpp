@@ -249,6 +249,14 @@ class GpuSorter {
   std::vector<uint32_t> argsort_i64(std::span<const int64_t> d) { return argsort_host(d); }
   std::vector<uint32_t> argsort_f64(std::span<const double> d) { return argsort_host(d); }
 
+  // -- permutation apply (forge-runtime GpuGather): dst[i] = src[idx[i]] on device
+  // memory, T a 4- or 8-byte element (no reference counterpart in forge-sort) --
+  template <typename T>
+  void gather_device(const T* src, uint64_t src_n, const uint32_t* idx, T* dst, uint64_t n) {
+    static_assert(sizeof(T) == 4 || sizeof(T) == 8, "4- or 8-byte elements");
+    detail::check(fs_gather(h_, (int)sizeof(T), src, src_n, idx, dst, n, 1), h_);
+  }
+
   // -- stable key/value sort, u32 values (lib.rs:1923-2236, 2826-3015) --------
   void sort_pairs_u32(std::span<uint32_t> k, std::span<uint32_t> v) { pairs_host(k, v); }
   void sort_pairs_i32(std::span<int32_t> k, std::span<uint32_t> v) { pairs_host(k, v); }

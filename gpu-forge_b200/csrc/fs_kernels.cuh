@@ -970,6 +970,52 @@ __global__ void __launch_bounds__(BLOCK, MINB)
 }
 
 // --------------------------------------------------------------------------
+// Gather: dst[i] = src[idx[i]] -- applying a permutation (argsort result) to a
+// payload.  Replaces sort_gather_values (shaders/sort.metal:792-800) and
+// forge-runtime's GpuGather (forge-runtime/src/gather.rs:82-134).  Four
+// indices per thread from one 16-byte load when aligned; an index outside the
+// source is reported (DEV_ERR_BOUNDS to the mapped host word) and skipped.
+// --------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256)
+    k_gather(const T* __restrict__ src, const uint64_t src_n, const uint32_t* __restrict__ idx, T* __restrict__ dst,
+             const uint64_t n, int* __restrict__ host_err) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  bool oob = false;
+  if ((reinterpret_cast<uintptr_t>(idx) & 15) == 0) {
+    const uint64_t n4 = n / 4;
+    const uint4* iv = reinterpret_cast<const uint4*>(idx);
+    for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4; q += stride) {
+      const uint4 j = __ldcs(iv + q);
+      const uint32_t jj[4] = {j.x, j.y, j.z, j.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        if (jj[r] < src_n)
+          dst[4 * q + r] = src[jj[r]];
+        else
+          oob = true;
+      }
+    }
+    for (uint64_t i = 4 * n4 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+      const uint32_t j = idx[i];
+      if (j < src_n)
+        dst[i] = src[j];
+      else
+        oob = true;
+    }
+  } else {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+      const uint32_t j = idx[i];
+      if (j < src_n)
+        dst[i] = src[j];
+      else
+        oob = true;
+    }
+  }
+  if (oob) *(volatile int*)host_err = DEV_ERR_BOUNDS;
+}
+
+// --------------------------------------------------------------------------
 // Finalize: copy-back for in-place sorts that ended in scratch, iota for an
 // argsort whose keys were all equal; then hand any device error to the host
 // (mapped pinned word; set-only, the host clears it) and re-arm ctl->err.

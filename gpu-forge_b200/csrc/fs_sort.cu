@@ -585,7 +585,7 @@ int finish(fs_sorter* s, int sync) {
   if (he != 0) {
     *(volatile int*)s->host_err = 0;
     if (he == DEV_ERR_BOUNDS)
-      return fail(s, FS_E_GPU_EXECUTION, "scatter position out of range (histogram/offset inconsistency)");
+      return fail(s, FS_E_GPU_EXECUTION, "a device position fell out of range (scatter offset or gather index)");
     return fail(s, FS_E_TIMEOUT, "device wait timeout: a bulk copy did not complete within %llu ms",
                 (unsigned long long)(s->timeout_ns / 1000000ull));
   }
@@ -1231,6 +1231,30 @@ int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n,
   FS_PARTITION_DTYPES(FS_PD)
 #undef FS_PD
   if (rc) return rc;
+  return finish(s, sync);
+}
+
+int fs_gather(fs_sorter* s, int width, const void* src, uint64_t src_n, const uint32_t* idx, void* dst, uint64_t n,
+              int sync) {
+  if (!s) return FS_E_INVALID;
+  if (width != 4 && width != 8) return fail(s, FS_E_INVALID, "width must be 4 or 8 bytes, got %d", width);
+  if (n == 0) return FS_OK;
+  if (!src || !idx || !dst) return fail(s, FS_E_INVALID, "src, idx or dst is NULL");
+  int rc = set_device(s);
+  if (rc) return rc;
+  if ((rc = prepare_ptr(s, src, (size_t)src_n * width, "src"))) return rc;
+  if ((rc = prepare_ptr(s, idx, (size_t)n * 4, "idx"))) return rc;
+  if ((rc = prepare_ptr(s, dst, (size_t)n * width, "dst"))) return rc;
+  const uint64_t blocks = (n / 4 + 255) / 256 + 1;
+  const uint64_t cap = (uint64_t)s->sm_count * 8;
+  const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+  if (width == 4)
+    k_gather<uint32_t><<<grid, 256, 0, s->stream>>>(static_cast<const uint32_t*>(src), src_n, idx,
+                                                  static_cast<uint32_t*>(dst), n, s->host_err_dev);
+  else
+    k_gather<uint64_t><<<grid, 256, 0, s->stream>>>(static_cast<const uint64_t*>(src), src_n, idx,
+                                                  static_cast<uint64_t*>(dst), n, s->host_err_dev);
+  s->last_launches = 1;
   return finish(s, sync);
 }
 

@@ -52,6 +52,7 @@ SIGNATURES = {
     "fs_last_kernel_times": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), _i32]),
     "fs_partition": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _i32]),
     "fs_host_sort_keys_copy_async": (_i32, [_vp, _i32, _vp, _vp, _u64]),
+    "fs_gather": (_i32, [_vp, _i32, _vp, _u64, _vp, _vp, _u64, _i32]),
     "fs_mg_create": (_i32, [_vp, _i32, _pp]),
     "fs_mg_destroy": (_i32, [_vp]),
     "fs_mg_last_error": (ctypes.c_char_p, [_vp]),

@@ -472,6 +472,14 @@ class GpuSorter:
                                                      nsplit, tab, int(sync)))
         self._pending = self._pending or not sync
 
+    def gather_device(self, width: int, src_ptr: int, src_n: int, idx_ptr: int, dst_ptr: int, n: int,
+                      sync: bool = True) -> None:
+        """dst[i] = src[idx[i]] on device memory (width 4 or 8 bytes per
+        element, u32 indices) -- forge-runtime's GpuGather."""
+        self._call(_lib.load().fs_gather(self._h, int(width), ctypes.c_void_p(src_ptr), src_n,
+                                         ctypes.c_void_p(idx_ptr), ctypes.c_void_p(dst_ptr), n, int(sync)))
+        self._pending = self._pending or not sync
+
     def alloc_device(self, nbytes: int) -> int:
         """Plain device memory (cudaMalloc) owned by the sorter; free_device()."""
         ptr = ctypes.c_void_p()

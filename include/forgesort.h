@@ -161,6 +161,19 @@ int fs_host_sort_keys_copy(fs_sorter* s, int dtype, const void* host_in,
 int fs_host_sort_keys_copy_async(fs_sorter* s, int dtype, const void* host_in,
                                  void* host_out, uint64_t n);
 
+/* ---- permutation apply --------------------------------------------------- */
+
+/* dst[i] = src[idx[i]] for i < n: elements of `width` bytes (4 or 8), u32
+ * indices into a source of src_n elements; src, idx and dst are device (or
+ * managed) memory of the sorter's device and dst does not overlap src or
+ * idx.  An index >= src_n is skipped and reported as FS_E_GPU_EXECUTION at
+ * the next synchronisation.  Replaces sort_gather_values
+ * (shaders/sort.metal:792-800) and forge-runtime's GpuGather::gather_u32 /
+ * gather_u64 (forge-runtime/src/gather.rs:82-134): applying an argsort
+ * permutation to a payload. */
+int fs_gather(fs_sorter* s, int width, const void* src, uint64_t src_n,
+              const uint32_t* idx, void* dst, uint64_t n, int sync);
+
 /* ---- per-kernel timing ---------------------------------------------------- */
 
 /* on != 0: record a CUDA event pair around every kernel the sorter launches,

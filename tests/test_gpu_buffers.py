@@ -148,3 +148,29 @@ def test_async_host_sorts_overlap_and_match(sorter):
         bits = orc.BITS_DTYPE[dt]
         assert np.array_equal(h_in.numpy().view(bits), np.ascontiguousarray(x).view(bits))
         assert np.array_equal(h_out.numpy().view(bits), orc.sort_keys(x, dt).view(bits)), dt
+
+
+@pytest.mark.parametrize("width", [4, 8])
+def test_gather_applies_argsort_permutation(sorter, width):
+    """fs_gather: dst[i] = src[idx[i]] (forge-runtime GpuGather): applying the
+    argsort of keys to a payload equals the payload of a stable pairs sort;
+    an out-of-range index is an error, not a wild read."""
+    import torch
+    from forge_sort import GpuExecution
+    n = 1_000_003
+    keys = orc.gen("zipf_u32", n, seed=5)
+    payload = orc.gen("u64" if width == 8 else "u32", n, seed=6)
+    tdt = torch.int64 if width == 8 else torch.int32
+    idx = torch.from_numpy(sorter.argsort_u32(keys).view(np.int32)).cuda()
+    src = torch.from_numpy(np.ascontiguousarray(payload).view(np.int64 if width == 8 else np.int32)).cuda()
+    dst = torch.empty_like(src)
+    sorter.gather_device(width, src.data_ptr(), n, idx.data_ptr(), dst.data_ptr(), n)
+    want = payload[orc.argsort(keys, "u32")]
+    assert np.array_equal(dst.cpu().numpy().view(want.dtype), want)
+    # unaligned index pointer (scalar path) and a tail shorter than 4
+    sorter.gather_device(width, src.data_ptr(), n, idx.data_ptr() + 4, dst.data_ptr(), 7)
+    assert np.array_equal(dst[:7].cpu().numpy().view(want.dtype), want[1:8])
+    bad = idx.clone()
+    bad[123] = n
+    with pytest.raises(GpuExecution):
+        sorter.gather_device(width, src.data_ptr(), n, bad.data_ptr(), dst.data_ptr(), n)
