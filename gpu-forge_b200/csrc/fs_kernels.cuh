@@ -970,6 +970,62 @@ __global__ void __launch_bounds__(BLOCK, MINB)
 }
 
 // --------------------------------------------------------------------------
+// Small sorts (n <= SMALL_N): one CTA sorts everything in shared memory with
+// a bitonic network over (ordered key, input position), so equal keys keep
+// their input order (stable, as the radix passes are).  One launch instead of
+// fifteen, for the short arrays of e.g. gpu-search's argsort_u64
+// (gpu-search/src/search/content.rs:849-884).  Payloads are staged too, so
+// in-place calls are safe.
+// --------------------------------------------------------------------------
+constexpr uint32_t SMALL_N = 4096;
+constexpr int SMALL_BLOCK = 1024;
+template <typename K, int XF>
+__global__ void __launch_bounds__(SMALL_BLOCK)
+    k_small_sort(const K* __restrict__ kin, K* __restrict__ kout, const uint32_t* __restrict__ vin,
+                 uint32_t* __restrict__ vout, const uint32_t n, const uint32_t npad, const int has_vals,
+                 const int write_keys) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  K* sk = reinterpret_cast<K*>(sm);
+  uint32_t* si = reinterpret_cast<uint32_t*>(sm + (size_t)npad * sizeof(K));
+  uint32_t* sv = si + npad;
+  const bool synth = has_vals && vin == nullptr;
+  for (uint32_t i = threadIdx.x; i < npad; i += SMALL_BLOCK) {
+    if (i < n) {
+      sk[i] = to_ordered<K, XF>(kin[i]);
+      si[i] = i;
+      if (has_vals) sv[i] = synth ? i : vin[i];
+    } else {  // padding sorts after every real key: largest key, largest position
+      sk[i] = ~K(0);
+      si[i] = 0xffffffffu;
+    }
+  }
+  __syncthreads();
+  for (uint32_t k = 2; k <= npad; k <<= 1) {
+    for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+      for (uint32_t i = threadIdx.x; i < npad; i += SMALL_BLOCK) {
+        const uint32_t l = i ^ j;
+        if (l > i) {
+          const K a = sk[i], b = sk[l];
+          const uint32_t ia = si[i], ib = si[l];
+          const bool greater = a > b || (a == b && ia > ib);
+          if (greater == ((i & k) == 0)) {
+            sk[i] = b;
+            sk[l] = a;
+            si[i] = ib;
+            si[l] = ia;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (uint32_t i = threadIdx.x; i < n; i += SMALL_BLOCK) {
+    if (write_keys) kout[i] = from_ordered<K, XF>(sk[i]);
+    if (has_vals) vout[i] = sv[si[i]];
+  }
+}
+
+// --------------------------------------------------------------------------
 // Gather: dst[i] = src[idx[i]] -- applying a permutation (argsort result) to a
 // payload.  Replaces sort_gather_values (shaders/sort.metal:792-800) and
 // forge-runtime's GpuGather (forge-runtime/src/gather.rs:82-134).  Four

@@ -8,6 +8,7 @@
 #include "fs_kernels.cuh"
 
 #include <cstdarg>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -39,6 +40,7 @@ struct fs_sorter {
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
   void* dst_tab = nullptr;  // sample-sort dispatch: 256 destination pointers
+  bool no_small = false;  // FORGESORT_SMALL_SORT=0: small sorts take the radix passes
   // fs_host_sort_keys_copy_async: two device buffers used in turn, and copy
   // streams of their own so one call's copies overlap the next call's work
   struct PipeSlot {
@@ -443,9 +445,44 @@ Exec exec_of(fs_sorter* s) {
   return e;
 }
 
+// Small sorts: one CTA, everything in shared memory (k_small_sort).
+template <typename K, int XF>
+int enqueue_small(fs_sorter* s, const PlanArgs& a) {
+  const uint32_t n = (uint32_t)a.n;
+  uint32_t npad = 2;
+  while (npad < n) npad <<= 1;
+  const size_t smem = (size_t)npad * (sizeof(K) + 8);
+  auto kern = k_small_sort<K, XF>;
+  static std::atomic<unsigned> configured{0};  // opt-in shared memory, once per device
+  const unsigned bit = 1u << (s->device & 31);
+  if (!(configured.load() & bit)) {
+    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)(SMALL_N * (sizeof(K) + 8))));
+    configured.fetch_or(bit);
+  }
+  kern<<<1, SMALL_BLOCK, smem, s->stream>>>(static_cast<const K*>(a.kin), static_cast<K*>(a.kfinal), a.vin, a.vfinal,
+                                            n, npad, a.has_vals, a.write_keys);
+  s->last_launches = 1;
+  FS_CUDA(s, cudaGetLastError());
+  return FS_OK;
+}
+
+int dispatch_small(fs_sorter* s, int dtype, const PlanArgs& a) {
+  switch (dtype) {
+    case FS_U32: return enqueue_small<uint32_t, XF_NONE>(s, a);
+    case FS_I32: return enqueue_small<uint32_t, XF_SIGN>(s, a);
+    case FS_F32: return enqueue_small<uint32_t, XF_FLOAT>(s, a);
+    case FS_U64: return enqueue_small<uint64_t, XF_NONE>(s, a);
+    case FS_I64: return enqueue_small<uint64_t, XF_SIGN>(s, a);
+    case FS_F64: return enqueue_small<uint64_t, XF_FLOAT>(s, a);
+    default: return fail(s, FS_E_INVALID, "unknown dtype %d", dtype);
+  }
+}
+
 // The sorter's path: size the slices, grow its scratch, enqueue.
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
+  if (a.n <= SMALL_N && !s->no_small) return dispatch_small(s, dtype, a);
   Exec e = exec_of(s);
   const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);
   int rc = ensure_slice_buffers(s, sl);
@@ -687,6 +724,7 @@ int fs_create(int device, void* stream, fs_sorter** out) {
   *s->host_err = 0;
   e = cudaHostGetDevicePointer((void**)&s->host_err_dev, s->host_err, 0);
   if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaHostGetDevicePointer"));
+  if (const char* t = getenv("FORGESORT_SMALL_SORT")) s->no_small = atoi(t) == 0;
   if (const char* t = getenv("FORGESORT_WAIT_TIMEOUT_MS")) {
     const long long ms = atoll(t);
     if (ms > 0) s->timeout_ns = (uint64_t)ms * 1000000ull;

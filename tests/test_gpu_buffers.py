@@ -120,9 +120,45 @@ def test_launch_count(sorter):
     y = orc.gen("u64", 100_000, seed=1)
     sorter.sort_u64(y.copy())
     assert sorter.last_launch_count() == 3 + 3 * 8
-    k, v = orc.gen("u32", 1000, seed=2), np.arange(1000, dtype=np.uint32)
+    k, v = orc.gen("u32", 10_000, seed=2), np.arange(10_000, dtype=np.uint32)
     sorter.sort_pairs_u32(k, v)  # payload: every pass ranks stably, one scatter each
     assert sorter.last_launch_count() == 3 + 3 * 4
+    # up to 4096 keys: one single-CTA launch
+    for dt in ("u32", "f64"):
+        getattr(sorter, f"argsort_{dt}")(orc.gen("u32" if dt == "u32" else "f64_logu", 4096, seed=3))
+        assert sorter.last_launch_count() == 1
+
+
+@pytest.mark.parametrize("dt,dist", [("u32", "u32"), ("i32", "i32"), ("f32", "f32_mix"),
+                                     ("u64", "u64"), ("i64", "i64"), ("f64", "f64_logu")])
+def test_small_sort_matches_radix_path(sorter, monkeypatch, dt, dist):
+    """The single-CTA path (n <= 4096) and the radix passes
+    (FORGESORT_SMALL_SORT=0) give the same keys, the same stable argsort and
+    the same pairs, on inputs full of ties, and sort device memory in place."""
+    import torch
+    from forge_sort import GpuSorter
+    monkeypatch.setenv("FORGESORT_SMALL_SORT", "0")
+    radix = GpuSorter()
+    rng = np.random.default_rng(17)
+    for n in (1, 2, 3, 255, 1000, 2049, 4096):
+        x = orc.gen(dist, n, seed=n)
+        x[rng.integers(0, n, n // 2)] = x[0]  # ties
+        for srt in (sorter, radix):
+            a = x.copy()
+            getattr(srt, f"sort_{dt}")(a)
+            assert np.array_equal(a.view(orc.BITS_DTYPE[dt]), orc.sort_keys(x, dt).view(orc.BITS_DTYPE[dt]))
+            assert np.array_equal(getattr(srt, f"argsort_{dt}")(x), orc.argsort(x, dt))
+            k, v = x.copy(), orc.gen("u32", n, seed=5)
+            wk, wv = orc.sort_pairs(x, v, dt)
+            getattr(srt, f"sort_pairs_{dt}")(k, v)
+            assert np.array_equal(k.view(orc.BITS_DTYPE[dt]), wk.view(orc.BITS_DTYPE[dt]))
+            assert np.array_equal(v, wv)
+        # in place on the device
+        t = torch.from_numpy(x.view(orc.BITS_DTYPE[dt]).view(np.int32 if x.itemsize == 4 else np.int64)).cuda()
+        sorter.sort_device(dt, t.data_ptr(), n)
+        got = t.cpu().numpy().view(orc.BITS_DTYPE[dt])
+        assert np.array_equal(got, orc.sort_keys(x, dt).view(orc.BITS_DTYPE[dt]))
+    radix.close()
 
 
 def test_async_host_sorts_overlap_and_match(sorter):
