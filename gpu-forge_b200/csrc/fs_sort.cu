@@ -1280,20 +1280,80 @@ int fs_gather(fs_sorter* s, int width, const void* src, uint64_t src_n, const ui
   if (!src || !idx || !dst) return fail(s, FS_E_INVALID, "src, idx or dst is NULL");
   int rc = set_device(s);
   if (rc) return rc;
-  if ((rc = prepare_ptr(s, src, (size_t)src_n * width, "src"))) return rc;
-  if ((rc = prepare_ptr(s, idx, (size_t)n * 4, "idx"))) return rc;
-  if ((rc = prepare_ptr(s, dst, (size_t)n * width, "dst"))) return rc;
+  // Page-locked host operands (SortBuffers, ForgeContext buffers) go through
+  // device staging as the sorts do.  A page-locked source much larger than
+  // the gather is read in place over the bus instead: n random reads of one
+  // 32-byte sector each cost less than copying all of it.
+  void* srcv = const_cast<void*>(src);
+  void* idxv = nullptr;
+  void* dstv = nullptr;
+  bool src_in_place = false;
+  if (is_pinned_host(src) && n * 32 < src_n * (uint64_t)width) {
+    cudaPointerAttributes at{};
+    src_in_place = cudaPointerGetAttributes(&at, src) == cudaSuccess && at.devicePointer == src;
+    cudaGetLastError();
+  }
+  if (!src_in_place &&
+      (rc = device_view(s, src, (size_t)src_n * width, "src", &s->dkeys, &s->dkeys_bytes, true, &srcv)))
+    return rc;
+  if ((rc = device_view(s, idx, (size_t)n * 4, "idx", &s->dvals, &s->dvals_bytes, true, &idxv))) return rc;
+  if ((rc = device_view(s, dst, (size_t)n * width, "dst", &s->kother, &s->kother_bytes, false, &dstv))) return rc;
   const uint64_t blocks = (n / 4 + 255) / 256 + 1;
   const uint64_t cap = (uint64_t)s->sm_count * 8;
   const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
   if (width == 4)
-    k_gather<uint32_t><<<grid, 256, 0, s->stream>>>(static_cast<const uint32_t*>(src), src_n, idx,
-                                                  static_cast<uint32_t*>(dst), n, s->host_err_dev);
+    k_gather<uint32_t><<<grid, 256, 0, s->stream>>>(static_cast<const uint32_t*>(srcv), src_n,
+                                                  static_cast<const uint32_t*>(idxv), static_cast<uint32_t*>(dstv),
+                                                  n, s->host_err_dev);
   else
-    k_gather<uint64_t><<<grid, 256, 0, s->stream>>>(static_cast<const uint64_t*>(src), src_n, idx,
-                                                  static_cast<uint64_t*>(dst), n, s->host_err_dev);
+    k_gather<uint64_t><<<grid, 256, 0, s->stream>>>(static_cast<const uint64_t*>(srcv), src_n,
+                                                  static_cast<const uint32_t*>(idxv), static_cast<uint64_t*>(dstv),
+                                                  n, s->host_err_dev);
+  FS_CUDA(s, cudaGetLastError());
+  if ((rc = copy_back(s, dst, dstv, (size_t)n * width))) return rc;
   s->last_launches = 1;
   return finish(s, sync);
+}
+
+// ---- streams for callers without a CUDA runtime of their own ----------------
+int fs_stream_create(int device, void** stream) {
+  if (!stream) return fail(nullptr, FS_E_INVALID, "stream is NULL");
+  *stream = nullptr;
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return fail(nullptr, FS_E_DEVICE_NOT_FOUND, "no CUDA device");
+  }
+  if (device < 0 || device >= count) return fail(nullptr, FS_E_DEVICE_NOT_FOUND, "no CUDA device %d", device);
+  cudaStream_t st = nullptr;
+  if ((e = cudaSetDevice(device)) != cudaSuccess || (e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(nullptr, FS_E_GPU_EXECUTION, "cudaStreamCreate: %s", cudaGetErrorString(e));
+  }
+  *stream = st;
+  return FS_OK;
+}
+
+int fs_stream_synchronize(void* stream) {
+  if (!stream) return fail(nullptr, FS_E_INVALID, "stream is NULL");
+  const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(nullptr, FS_E_GPU_EXECUTION, "cudaStreamSynchronize: %s", cudaGetErrorString(e));
+  }
+  return FS_OK;
+}
+
+int fs_stream_destroy(void* stream) {
+  if (!stream) return FS_OK;
+  cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaStreamDestroy(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(nullptr, FS_E_GPU_EXECUTION, "cudaStreamDestroy: %s", cudaGetErrorString(e));
+  }
+  return FS_OK;
 }
 
 int fs_ipc_export(fs_sorter* s, void* ptr, void* handle_out) {

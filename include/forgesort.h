@@ -164,15 +164,30 @@ int fs_host_sort_keys_copy_async(fs_sorter* s, int dtype, const void* host_in,
 /* ---- permutation apply --------------------------------------------------- */
 
 /* dst[i] = src[idx[i]] for i < n: elements of `width` bytes (4 or 8), u32
- * indices into a source of src_n elements; src, idx and dst are device (or
- * managed) memory of the sorter's device and dst does not overlap src or
- * idx.  An index >= src_n is skipped and reported as FS_E_GPU_EXECUTION at
+ * indices into a source of src_n elements; src, idx and dst are device,
+ * managed or page-locked host memory (a SortBuffer) of the sorter's device,
+ * and dst does not overlap src or idx.  Page-locked operands are staged
+ * through device memory on the sorter's stream, except a page-locked source
+ * more than 32x the gathered bytes, which the kernel reads in place.  An index >= src_n is skipped and reported as FS_E_GPU_EXECUTION at
  * the next synchronisation.  Replaces sort_gather_values
  * (shaders/sort.metal:792-800) and forge-runtime's GpuGather::gather_u32 /
  * gather_u64 (forge-runtime/src/gather.rs:82-134): applying an argsort
  * permutation to a payload. */
 int fs_gather(fs_sorter* s, int width, const void* src, uint64_t src_n,
               const uint32_t* idx, void* dst, uint64_t n, int sync);
+
+/* ---- streams --------------------------------------------------------------- */
+
+/* A non-blocking CUDA stream on `device`, for callers that have no CUDA
+ * runtime of their own: the command queue of forge-runtime's ForgeContext
+ * (forge-runtime/src/context.rs:16-55), which sorters (fs_create) and
+ * gathers then share so that their work runs in submission order.
+ * fs_stream_synchronize is the analogue of commit + waitUntilCompleted
+ * (forge-runtime/src/pipeline.rs:129-139).  Failures: FS_E_DEVICE_NOT_FOUND,
+ * FS_E_GPU_EXECUTION; text via fs_last_error(NULL). */
+int fs_stream_create(int device, void** stream);
+int fs_stream_synchronize(void* stream);
+int fs_stream_destroy(void* stream);
 
 /* ---- per-kernel timing ---------------------------------------------------- */
 

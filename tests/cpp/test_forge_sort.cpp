@@ -19,6 +19,7 @@
 #include <string>
 #include <vector>
 
+#include "forge_runtime.hpp"
 #include "forge_sort.hpp"
 
 using forge_sort::GpuSorter;
@@ -398,6 +399,64 @@ GPU_TEST(test_cross_type_interleave) {
     s.sort_u64(w);
     CHECK(u == wu && i == wi && same_bits(f, wf) && w == ww);
   }
+}
+
+// ---- forge-runtime (forge-runtime/src, tests/pipeline_tests.rs) --------------
+CPU_TEST(test_runtime_error_display) {
+  using forge_runtime::GatherError;
+  using forge_runtime::PipelineError;
+  CHECK(std::string(GatherError::shader_compilation("x").what()) == "shader compilation failed: x");
+  CHECK(std::string(GatherError::gpu_execution("x").what()) == "GPU execution failed: x");
+  CHECK(std::string(PipelineError::command_buffer().what()) == "failed to create command buffer");
+  CHECK(std::string(PipelineError::encoder().what()) == "failed to create compute encoder");
+  CHECK(std::string(PipelineError::sort(SortError::gpu_execution("x")).what()) == "sort error: GPU execution failed: x");
+}
+
+// pipeline_tests.rs:172-210: sort 100K keys of a SortBuffer, then gather the
+// first 100 in the same pipeline.
+GPU_TEST(test_pipeline_sort_then_gather_100k) {
+  auto ctx = forge_runtime::ForgeContext::create();
+  auto sorter = GpuSorter::with_context(ctx.device(), ctx.queue());
+  auto gather = forge_runtime::GpuGather::with_context(ctx.device(), ctx.queue());
+  const auto data = random_u32(100000, 7);
+  auto buf = sorter.alloc_sort_buffer<uint32_t>(data.size());
+  buf.copy_from_slice(data);
+  auto idx = ctx.alloc_buffer(100 * 4);
+  for (uint32_t i = 0; i < 100; ++i) idx.as<uint32_t>()[i] = i;
+  auto out = ctx.alloc_buffer(100 * 4);
+  forge_runtime::Pipeline p(ctx);
+  p.sort(sorter, buf);
+  p.gather(gather, buf.device_ptr(), buf.len(), idx.device_ptr(), out.device_ptr(), 100, false);
+  p.execute();
+  const auto want = sorted_copy(data);
+  CHECK(std::equal(want.begin(), want.begin() + 100, out.as<uint32_t>()));
+  CHECK(std::equal(want.begin(), want.end(), buf.as_slice().begin()));
+}
+
+GPU_TEST(test_gather_u64_and_bounds) {
+  auto ctx = forge_runtime::ForgeContext::create();
+  auto g = forge_runtime::GpuGather::with_context(ctx.device(), ctx.queue());
+  const uint32_t n = 1 << 16;
+  auto src = ctx.alloc_buffer(n * 8);
+  auto idx = ctx.alloc_buffer(n * 4);
+  auto out = ctx.alloc_buffer(n * 8);
+  const auto r = random_u32(n, 11);
+  for (uint32_t i = 0; i < n; ++i) {
+    src.as<uint64_t>()[i] = ((uint64_t)r[i] << 32) | i;
+    idx.as<uint32_t>()[i] = r[i] % n;
+  }
+  g.gather_u64(src, idx, out, n);
+  for (uint32_t i = 0; i < n; ++i) CHECK(out.as<uint64_t>()[i] == src.as<uint64_t>()[idx.as<uint32_t>()[i]]);
+  idx.as<uint32_t>()[5] = n;  // one index past the source
+  forge_runtime::Pipeline p(ctx);
+  p.gather(g, src, idx, out, n, true);
+  bool threw = false;
+  try {
+    p.execute();
+  } catch (const forge_runtime::PipelineError& e) {
+    threw = e.kind() == forge_runtime::PipelineError::Kind::GpuExecution;
+  }
+  CHECK(threw);
 }
 
 }  // namespace
