@@ -166,11 +166,13 @@ struct SplitterDigit {
 // NB = bucket capacity of the instantiation: 8 covers the GPUs of one box
 // (tile counters and scans sized for 8 digits, ranking by three ballots);
 // 256 covers any splitter count.
+// With a payload, value i goes to vdst[b] at the same position as key i.
 template <typename K, int XF, int NB = RADIX>
 struct SplitterDispatch : SplitterDigit<K, XF> {
   static constexpr int DIGITS = NB;
   static constexpr bool DISPATCH = true;
-  K* const* dst;  // device array of nsplit + 1 destinations
+  K* const* dst;          // device array of nsplit + 1 key destinations
+  uint32_t* const* vdst;  // device array of nsplit + 1 value destinations (payload only)
 };
 
 // Visit the keys of [lo, hi) with the CTA's threads in coalesced order, 16-byte
@@ -646,7 +648,8 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
                                              uint32_t* __restrict__ vout, const unsigned char* slot,
                                              unsigned char* dsm, uint32_t* s_run, uint32_t* s_off,
                                              uint32_t* s_wsum, SortCtl* __restrict__ ctl, const D& dfn,
-                                             const uint64_t gpos_base, K* const* s_dst, const uint32_t* s_lim) {
+                                             const uint64_t gpos_base, K* const* s_dst, const uint32_t* s_lim,
+                                             uint32_t* const* s_vdst) {
   constexpr int R = D::DIGITS;
   using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R>;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -798,8 +801,8 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       skeys[pos] = key[k];
       if constexpr (VALS) {
         uint32_t v;
-        if (synth)
-          v = (uint32_t)(tbase + li);
+        if (synth)  // the key's (global) position: gpos_base is 0 except in a sample-sort dispatch
+          v = (uint32_t)(gbase + li);
         else if constexpr (FROM_SLOT)
           v = slot_vals[li];
         else
@@ -831,10 +834,12 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       const uint32_t pos = s_off[d] + i;
       if constexpr (D::DISPATCH) {
         // position within bucket d; its region holds exactly s_lim[d] keys
-        if (pos < s_lim[d])
+        if (pos < s_lim[d]) {
           s_dst[d][pos] = xout ? from_ordered<K, XF>(kk) : kk;
-        else
+          if constexpr (VALS) s_vdst[d][pos] = svals[i];
+        } else {
           oob = true;
+        }
       } else if (pos <= last) {
         if (wkeys) kout[pos] = xout ? from_ordered<K, XF>(kk) : kk;
         if constexpr (VALS) vout[pos] = svals[i];
@@ -874,6 +879,7 @@ __global__ void __launch_bounds__(BLOCK, MINB)
   __shared__ int s_abort;
   __shared__ K* s_dst[D::DISPATCH ? R : 1];
   __shared__ uint32_t s_lim[D::DISPATCH ? R : 1];
+  __shared__ uint32_t* s_vdst[D::DISPATCH && VALS ? R : 1];
   __shared__ K s_spk[D::STAGE ? (R < 8 ? 8 : R) : 1];  // the splitter search pads to 8
   __shared__ uint64_t s_spg[D::STAGE ? (R < 8 ? 8 : R) : 1];
 
@@ -910,6 +916,7 @@ __global__ void __launch_bounds__(BLOCK, MINB)
       const bool used = b <= dfn.nsplit;
       s_dst[b] = used ? dfn.dst[b] : nullptr;
       s_lim[b] = used ? (uint32_t)ctl->hist[0][b] : 0u;
+      if constexpr (VALS) s_vdst[b] = used ? dfn.vdst[b] : nullptr;
     }
   }
   if (tid == 0) {
@@ -950,13 +957,13 @@ __global__ void __launch_bounds__(BLOCK, MINB)
       const unsigned char* slot = dsm + (size_t)s * Ly::SLOT;
       if (from_slot)
         scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                         slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim);
+                                                         slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim, s_vdst);
       else if (full)
         scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim);
+                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim, s_vdst);
       else
         scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                           slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim);
+                                                           slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim, s_vdst);
     }
   }
   // never leave a bulk copy into this CTA's shared memory in flight

@@ -563,19 +563,25 @@ int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t
 // Dispatch: one stable pass that stores every key at its rank within its
 // bucket, straight into that bucket's destination (dst[b], this rank's region
 // of rank b's inbox: plain stores over NVLink when it is another GPU's).
-template <typename K, int XF, int NB>
-int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, uint64_t n, uint64_t gpos_base,
-                                  const void* spl_keys, const uint64_t* spl_gpos, int nsplit, void* const* dst_host) {
+template <typename K, int XF, int NB, bool VALS>
+int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t* vals, uint64_t n,
+                                  uint64_t gpos_base, const void* spl_keys, const uint64_t* spl_gpos, int nsplit,
+                                  void* const* dst_host, uint32_t* const* vdst_host) {
   using D = SplitterDispatch<K, XF, NB>;
   D dfn{};
   dfn.keys = static_cast<const K*>(spl_keys);
   dfn.gpos = spl_gpos;
   dfn.nsplit = nsplit;
-  if (!s->dst_tab) FS_CUDA(s, cudaMalloc(&s->dst_tab, RADIX * sizeof(void*)));
-  // pageable source: the copy is staged before cudaMemcpyAsync returns
-  FS_CUDA(s, cudaMemcpyAsync(s->dst_tab, dst_host, (size_t)(nsplit + 1) * sizeof(void*), cudaMemcpyHostToDevice,
-                             s->stream));
-  dfn.dst = static_cast<K* const*>(s->dst_tab);
+  // [key destinations | value destinations], RADIX entries each
+  if (!s->dst_tab) FS_CUDA(s, cudaMalloc(&s->dst_tab, 2 * RADIX * sizeof(void*)));
+  void** tab = static_cast<void**>(s->dst_tab);
+  // pageable sources: the copies are staged before cudaMemcpyAsync returns
+  FS_CUDA(s, cudaMemcpyAsync(tab, dst_host, (size_t)(nsplit + 1) * sizeof(void*), cudaMemcpyHostToDevice, s->stream));
+  if (VALS)
+    FS_CUDA(s, cudaMemcpyAsync(tab + RADIX, vdst_host, (size_t)(nsplit + 1) * sizeof(void*), cudaMemcpyHostToDevice,
+                               s->stream));
+  dfn.dst = reinterpret_cast<K* const*>(tab);
+  dfn.vdst = reinterpret_cast<uint32_t* const*>(tab + RADIX);
   Exec e = exec_of(s);
   const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
   e.counts = static_cast<uint32_t*>(s->counts);
@@ -589,6 +595,11 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, uint64_t n, ui
   a.write_keys = 1;
   a.key_bytes = (int)sizeof(K);
   a.force_exec = 1;
+  if (VALS) {
+    a.has_vals = 1;
+    a.vin = vals;  // nullptr: each key's global position, gpos_base + i
+    a.vfinal = vdst_host[0];  // not written either: dispatch stores through vdst[]
+  }
   s->ev_used = 0;
   t_begin(e);
   k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
@@ -596,7 +607,7 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, uint64_t n, ui
   t_end(e);
   int rc;
   t_begin(e);
-  rc = launch_scatter<K, false, XF, PartCfg<K>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base);
+  rc = launch_scatter<K, VALS, XF, PartCfg<K>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base);
   t_end(e);
   if (rc) return rc;
   k_finalize<K><<<1, 256, 0, e.stream>>>(e.ctl, 0, e.err_out);  // error hand-off only
@@ -607,11 +618,21 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, uint64_t n, ui
 
 // Up to 8 buckets (the GPUs of one box) take the 8-digit instantiation.
 template <typename K, int XF>
-int enqueue_partition_dispatch(fs_sorter* s, const void* keys, uint64_t n, uint64_t gpos_base, const void* spl_keys,
-                               const uint64_t* spl_gpos, int nsplit, void* const* dst_host) {
+int enqueue_partition_dispatch(fs_sorter* s, const void* keys, const uint32_t* vals, bool with_vals, uint64_t n,
+                               uint64_t gpos_base, const void* spl_keys, const uint64_t* spl_gpos, int nsplit,
+                               void* const* dst_host, uint32_t* const* vdst_host) {
+  if (with_vals) {
+    if (nsplit < 8)
+      return enqueue_partition_dispatch_nb<K, XF, 8, true>(s, keys, vals, n, gpos_base, spl_keys, spl_gpos, nsplit,
+                                                           dst_host, vdst_host);
+    return enqueue_partition_dispatch_nb<K, XF, RADIX, true>(s, keys, vals, n, gpos_base, spl_keys, spl_gpos, nsplit,
+                                                             dst_host, vdst_host);
+  }
   if (nsplit < 8)
-    return enqueue_partition_dispatch_nb<K, XF, 8>(s, keys, n, gpos_base, spl_keys, spl_gpos, nsplit, dst_host);
-  return enqueue_partition_dispatch_nb<K, XF, RADIX>(s, keys, n, gpos_base, spl_keys, spl_gpos, nsplit, dst_host);
+    return enqueue_partition_dispatch_nb<K, XF, 8, false>(s, keys, nullptr, n, gpos_base, spl_keys, spl_gpos, nsplit,
+                                                          dst_host, nullptr);
+  return enqueue_partition_dispatch_nb<K, XF, RADIX, false>(s, keys, nullptr, n, gpos_base, spl_keys, spl_gpos,
+                                                            nsplit, dst_host, nullptr);
 }
 
 int finish(fs_sorter* s, int sync) {
@@ -1250,9 +1271,10 @@ int fs_partition_count(fs_sorter* s, int dtype, const void* keys, uint64_t n, ui
   return finish(s, 1);
 }
 
-int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n, uint64_t gpos_base,
-                          const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,
-                          void* const* bucket_dst, int sync) {
+namespace {
+int partition_dispatch(fs_sorter* s, int dtype, const void* keys, const uint32_t* vals, bool with_vals, uint64_t n,
+                       uint64_t gpos_base, const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,
+                       void* const* bucket_dst, uint32_t* const* value_dst, int sync) {
   int rc = check_common(s, dtype, n);
   if (rc) return rc;
   if (!s->part.ready || s->part.dtype != dtype || s->part.nsplit != nsplit || s->part.keys != keys ||
@@ -1261,14 +1283,83 @@ int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n,
   s->part.ready = false;
   if (n == 0) return FS_OK;
   if (!bucket_dst) return fail(s, FS_E_INVALID, "bucket_dst is NULL");
-  for (int b = 0; b <= nsplit; ++b)
+  if (with_vals && !value_dst) return fail(s, FS_E_INVALID, "value_dst is NULL");
+  for (int b = 0; b <= nsplit; ++b) {
     if (!bucket_dst[b]) return fail(s, FS_E_INVALID, "bucket_dst[%d] is NULL", b);
+    if (with_vals && !value_dst[b]) return fail(s, FS_E_INVALID, "value_dst[%d] is NULL", b);
+  }
+  if (with_vals && !vals && gpos_base + n > (1ull << 32))
+    return fail(s, FS_E_INVALID, "global positions past 2^32 do not fit u32 indices");
   if ((rc = set_device(s))) return rc;
-#define FS_PD(K, XF) \
-  enqueue_partition_dispatch<K, XF>(s, keys, n, gpos_base, splitter_keys, splitter_gpos, nsplit, bucket_dst)
+  if (with_vals && vals && (rc = prepare_ptr(s, vals, (size_t)n * 4, "values"))) return rc;
+#define FS_PD(K, XF)                                                                                         \
+  enqueue_partition_dispatch<K, XF>(s, keys, vals, with_vals, n, gpos_base, splitter_keys, splitter_gpos, nsplit, \
+                                    bucket_dst, value_dst)
   FS_PARTITION_DTYPES(FS_PD)
 #undef FS_PD
   if (rc) return rc;
+  return finish(s, sync);
+}
+}  // namespace
+
+int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n, uint64_t gpos_base,
+                          const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,
+                          void* const* bucket_dst, int sync) {
+  return partition_dispatch(s, dtype, keys, nullptr, false, n, gpos_base, splitter_keys, splitter_gpos, nsplit,
+                            bucket_dst, nullptr, sync);
+}
+
+int fs_partition_dispatch_pairs(fs_sorter* s, int dtype, const void* keys, const uint32_t* vals, uint64_t n,
+                                uint64_t gpos_base, const void* splitter_keys, const uint64_t* splitter_gpos,
+                                int nsplit, void* const* bucket_dst, uint32_t* const* value_dst, int sync) {
+  return partition_dispatch(s, dtype, keys, vals, true, n, gpos_base, splitter_keys, splitter_gpos, nsplit,
+                            bucket_dst, value_dst, sync);
+}
+
+int fs_sort_pairs_copy(fs_sorter* s, int dtype, const void* keys_in, const uint32_t* vals_in, void* keys_out,
+                       uint32_t* vals_out, uint64_t n, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (n == 0) return FS_OK;
+  if (!keys_in || !keys_out || !vals_out) return fail(s, FS_E_INVALID, "keys_in, keys_out or vals_out is NULL");
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  auto overlap = [n](const void* a, size_t ea, const void* b, size_t eb) {
+    const char* x = static_cast<const char*>(a);
+    const char* y = static_cast<const char*>(b);
+    return x < y + n * eb && y < x + n * ea;
+  };
+  if (overlap(keys_in, kb, keys_out, kb) || overlap(keys_out, kb, vals_out, 4) ||
+      (vals_in && (overlap(vals_in, 4, vals_out, 4) || overlap(vals_in, 4, keys_out, kb))))
+    return fail(s, FS_E_INVALID, "inputs and outputs overlap");
+  if ((rc = prepare_ptr(s, keys_in, (size_t)n * kb, "keys_in"))) return rc;
+  if (vals_in && (rc = prepare_ptr(s, vals_in, (size_t)n * 4, "vals_in"))) return rc;
+  if ((rc = prepare_ptr(s, keys_out, (size_t)n * kb, "keys_out"))) return rc;
+  if ((rc = prepare_ptr(s, vals_out, (size_t)n * 4, "vals_out"))) return rc;
+  if (n == 1) {
+    FS_CUDA(s, cudaMemcpyAsync(keys_out, keys_in, kb, cudaMemcpyDeviceToDevice, s->stream));
+    if (vals_in)
+      FS_CUDA(s, cudaMemcpyAsync(vals_out, vals_in, 4, cudaMemcpyDeviceToDevice, s->stream));
+    else
+      FS_CUDA(s, cudaMemsetAsync(vals_out, 0, 4, s->stream));
+    s->last_launches = 0;
+    return finish(s, sync);
+  }
+  if ((rc = grow(s, &s->kother, &s->kother_bytes, (size_t)n * kb, false))) return rc;
+  if ((rc = grow(s, &s->vother, &s->vother_bytes, (size_t)n * 4, false))) return rc;
+  PlanArgs a{};
+  a.n = n;
+  a.kin = keys_in;
+  a.kfinal = keys_out;
+  a.kother = s->kother;
+  a.vin = vals_in;  // nullptr: input positions (argsort with the sorted keys)
+  a.vfinal = vals_out;
+  a.vother = static_cast<uint32_t*>(s->vother);
+  a.passes = kb;
+  a.has_vals = 1;
+  a.write_keys = 1;
+  a.key_bytes = kb;
+  if ((rc = dispatch(s, dtype, a))) return rc;
   return finish(s, sync);
 }
 

@@ -53,6 +53,8 @@ SIGNATURES = {
     "fs_partition": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _i32]),
     "fs_host_sort_keys_copy_async": (_i32, [_vp, _i32, _vp, _vp, _u64]),
     "fs_gather": (_i32, [_vp, _i32, _vp, _u64, _vp, _vp, _u64, _i32]),
+    "fs_sort_pairs_copy": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _u64, _i32]),
+    "fs_partition_dispatch_pairs": (_i32, [_vp, _i32, _vp, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _vp, _i32]),
     "fs_stream_create": (_i32, [_i32, _vp]),
     "fs_stream_synchronize": (_i32, [_vp]),
     "fs_stream_destroy": (_i32, [_vp]),

@@ -23,6 +23,13 @@ Per call, on every rank:
      the bucket sizes and one of the buckets;
   4. local sort of the received keys (the single-GPU radix sort).
 
+sort_pairs / argsort carry a u32 payload through the same steps: the
+dispatch stores each key's value (or its global position, for argsort) in a
+second region of the destination inbox at the key's slot, and the local step
+is a stable pairs sort.  Within a bucket the keys arrive in global-position
+order (source ranks in rank order, each in input order), so equal keys end in
+global input order: the result is the stable sort_by_key of the whole input.
+
 The local steps go through an ops object so the host logic can run on CPU
 ranks (gloo) in tests with a CPU stand-in; CudaOps is the product path.
 """
@@ -159,9 +166,13 @@ class CudaOps:
         self._inbox = 0
         self._cap = 0
 
-    def exchange(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray, group):
-        """Partition + all-to-all + local sort; returns (sorted piece, send
-        counts, receive counts).  Runs on the current torch stream."""
+    def exchange(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray, group,
+                 vals=None, payload: bool = False):
+        """Partition + all-to-all + local sort; returns (sorted piece, value
+        piece or None, send counts, receive counts).  With payload, a u32
+        value travels with every key: vals (int32 tensor), or each key's
+        global position when vals is None.  Runs on the current torch
+        stream."""
         torch, dist = self.torch, self.torch.distributed
         G, r = dist.get_world_size(group), dist.get_rank(group)
         dev, kb, m = keys.device, keys.element_size(), keys.numel()
@@ -172,10 +183,18 @@ class CudaOps:
         rows = [torch.empty_like(cnt) for _ in range(G)]
         dist.all_gather(rows, cnt, group=group)
         M = torch.stack(rows).cpu().numpy()  # M[s, b]: keys rank s sends to rank b
-        self._ensure_inbox(int(M.sum(axis=0).max()) * kb, group, dev)
+        most = int(M.sum(axis=0).max())
+        # inbox: [keys | values], the values region 256-byte aligned
+        voff = (most * kb + 255) // 256 * 256 if payload else 0
+        self._ensure_inbox(voff + most * 4 if payload else most * kb, group, dev)
         start = M[:r, :].sum(axis=0)  # where this rank's keys begin in every inbox
         dst = [self._peers[b] + int(start[b]) * kb for b in range(G)]
-        self.s.partition_dispatch(dt, keys.data_ptr(), m, gpos_base, skp, sgp, G - 1, dst, sync=True)
+        if payload:
+            vdst = [self._peers[b] + voff + int(start[b]) * 4 for b in range(G)]
+            self.s.partition_dispatch_pairs(dt, keys.data_ptr(), 0 if vals is None else vals.data_ptr(), m,
+                                            gpos_base, skp, sgp, G - 1, dst, vdst, sync=True)
+        else:
+            self.s.partition_dispatch(dt, keys.data_ptr(), m, gpos_base, skp, sgp, G - 1, dst, sync=True)
         # every rank enters this collective after its dispatch finished, so
         # once it completes every inbox is full
         done = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -185,9 +204,13 @@ class CudaOps:
         recv = [int(x) for x in M[:, r]]
         total = sum(recv)
         out = torch.empty(total, dtype=keys.dtype, device=dev)
-        if total:
+        vout = torch.empty(total, dtype=torch.int32, device=dev) if payload else None
+        if total and payload:
+            self.s.sort_pairs_device_copy(dt, self._inbox, self._inbox + voff, out.data_ptr(), vout.data_ptr(),
+                                          total, sync=True)
+        elif total:
             self.s.sort_device_copy(dt, self._inbox, out.data_ptr(), total, sync=True)
-        return out, send, recv
+        return out, vout, send, recv
 
     def partition(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray) -> Tuple[object, List[int]]:
         torch = self.torch
@@ -213,6 +236,16 @@ class CudaOps:
         if keys.numel():
             self.s.sort_device_copy(dt, keys.data_ptr(), out.data_ptr(), keys.numel(), sync=True)
         return out
+
+    def sort_pairs(self, dt, keys, vals):
+        """Stable pairs sort into new tensors; vals None: input positions."""
+        torch = self.torch
+        out = torch.empty_like(keys)
+        vout = torch.empty(keys.numel(), dtype=torch.int32, device=keys.device)
+        if keys.numel():
+            self.s.sort_pairs_device_copy(dt, keys.data_ptr(), 0 if vals is None else vals.data_ptr(),
+                                          out.data_ptr(), vout.data_ptr(), keys.numel(), sync=True)
+        return out, vout
 
 
 @dataclass
@@ -245,6 +278,25 @@ class SampleSorter:
         return self.dist.get_world_size(self.group), self.dist.get_rank(self.group)
 
     def sort(self, keys, gpos_base: Optional[int] = None):
+        """This rank's piece of the sorted keys."""
+        return self._run(keys, None, False, gpos_base)[0]
+
+    def sort_pairs(self, keys, values, gpos_base: Optional[int] = None):
+        """(keys piece, values piece) of the stable sort of (key, value)
+        pairs by key: equal keys keep their global input order.  values is an
+        int32 tensor holding u32 values, one per key."""
+        if values is None or values.numel() != keys.numel():
+            raise ValueError("sort_pairs needs one value per key")
+        return self._run(keys, values, True, gpos_base)
+
+    def argsort(self, keys, gpos_base: Optional[int] = None):
+        """This rank's piece of the stable global argsort: the global input
+        positions (u32, in an int32 tensor) of the keys this rank's piece of
+        the sorted sequence holds.  The whole input may hold at most 2^32
+        keys."""
+        return self._run(keys, None, True, gpos_base)[1]
+
+    def _run(self, keys, vals, payload: bool, gpos_base: Optional[int]):
         torch, dist, dt = self.torch, self.dist, self.dt
         G, r = self._world()
         m = keys.numel()
@@ -255,7 +307,12 @@ class SampleSorter:
             gpos_base = int(sum(int(t.item()) for t in sizes[:r]))
         if G == 1:
             self.last = SampleSortStats([m], [m])
-            return self.ops.sort(dt, keys)
+            if not payload:
+                return self.ops.sort(dt, keys), None
+            out, vout = self.ops.sort_pairs(dt, keys, vals)
+            if vals is None and gpos_base:
+                vout = (vout.to(torch.int64) + gpos_base).to(torch.int32)
+            return out, vout
 
         # 1. regular samples with their global positions -> splitters, on the
         # keys' device: gather, one stable sort of the G*S sample keys (ties
@@ -291,12 +348,18 @@ class SampleSorter:
 
         # 2-4 on GPUs: dispatch straight into the peers' inboxes, local sort
         if getattr(self.ops, "dispatch", False):
-            out, send, recv = self.ops.exchange(dt, keys, gpos_base, spl_raw, spl_gpos, self.group)
+            out, vout, send, recv = self.ops.exchange(dt, keys, gpos_base, spl_raw, spl_gpos, self.group,
+                                                      vals=vals, payload=payload)
             self.last = SampleSortStats(send, recv)
-            return out
+            return out, vout
 
-        # 2. stable partition into G buckets
-        part, send = self.ops.partition(dt, keys, gpos_base, spl_raw, spl_gpos)
+        # 2. stable partition into G buckets (values travel beside the keys)
+        if payload:
+            if vals is None:  # argsort: the global positions, as u32
+                vals = (torch.arange(m, dtype=torch.int64, device=dev) + gpos_base).to(torch.int32)
+            part, pvals, send = self.ops.partition_pairs(dt, keys, vals, gpos_base, spl_raw, spl_gpos)
+        else:
+            part, send = self.ops.partition(dt, keys, gpos_base, spl_raw, spl_gpos)
 
         # 3. exchange sizes, then the buckets
         sc = torch.tensor(send, dtype=torch.int64, device=dev)
@@ -306,10 +369,18 @@ class SampleSorter:
         inbox = torch.empty(sum(recv), dtype=keys.dtype, device=dev)
         dist.all_to_all_single(inbox, part, output_split_sizes=recv, input_split_sizes=send, group=self.group)
         del part
+        vinbox = None
+        if payload:
+            vinbox = torch.empty(sum(recv), dtype=torch.int32, device=dev)
+            dist.all_to_all_single(vinbox, pvals, output_split_sizes=recv, input_split_sizes=send,
+                                   group=self.group)
+            del pvals
 
         # 4. local sort of this rank's bucket
         self.last = SampleSortStats(send, recv)
-        return self.ops.sort(dt, inbox)
+        if payload:
+            return self.ops.sort_pairs(dt, inbox, vinbox)
+        return self.ops.sort(dt, inbox), None
 
     def close(self) -> None:
         """Collective: release the ops' exchange resources (CUDA IPC inboxes)."""

@@ -415,6 +415,16 @@ class GpuSorter:
                                                  ctypes.c_void_p(out_ptr), n, int(sync)))
         self._pending = self._pending or not sync
 
+    def sort_pairs_device_copy(self, dt, kin: int, vin: int, kout: int, vout: int, n: int,
+                               sync: bool = True) -> None:
+        """Out-of-place stable pairs sort of device memory; vin == 0 takes the
+        input positions as values.  The inputs are left untouched."""
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_sort_pairs_copy(self._h, _DT[name][0], ctypes.c_void_p(kin),
+                                                  ctypes.c_void_p(vin or None), ctypes.c_void_p(kout),
+                                                  ctypes.c_void_p(vout), n, int(sync)))
+        self._pending = self._pending or not sync
+
     def host_sort_copy_async_ptr(self, dt, host_in: int, host_out: int, n: int) -> None:
         """Enqueue host-memory out-of-place sort (H2D + sort + D2H) and return;
         consecutive calls overlap their copies.  synchronize() waits."""
@@ -470,6 +480,18 @@ class GpuSorter:
         self._call(_lib.load().fs_partition_dispatch(self._h, _DT[name][0], ctypes.c_void_p(in_ptr), n, gpos_base,
                                                      ctypes.c_void_p(spl_keys_ptr), ctypes.c_void_p(spl_gpos_ptr),
                                                      nsplit, tab, int(sync)))
+        self._pending = self._pending or not sync
+
+    def partition_dispatch_pairs(self, dt, in_ptr: int, vals_ptr: int, n: int, gpos_base: int, spl_keys_ptr: int,
+                                 spl_gpos_ptr: int, nsplit: int, dst_ptrs, vdst_ptrs, sync: bool = False) -> None:
+        """Dispatch step 2 with a u32 payload: value i goes to vdst_ptrs[b]
+        beside key i; vals_ptr == 0 sends global positions gpos_base + i."""
+        name = dtype_name(dt)
+        tab = (ctypes.c_void_p * (nsplit + 1))(*[ctypes.c_void_p(int(p)) for p in dst_ptrs])
+        vtab = (ctypes.c_void_p * (nsplit + 1))(*[ctypes.c_void_p(int(p)) for p in vdst_ptrs])
+        self._call(_lib.load().fs_partition_dispatch_pairs(
+            self._h, _DT[name][0], ctypes.c_void_p(in_ptr), ctypes.c_void_p(vals_ptr or None), n, gpos_base,
+            ctypes.c_void_p(spl_keys_ptr), ctypes.c_void_p(spl_gpos_ptr), nsplit, tab, vtab, int(sync)))
         self._pending = self._pending or not sync
 
     def gather_device(self, width: int, src_ptr: int, src_n: int, idx_ptr: int, dst_ptr: int, n: int,

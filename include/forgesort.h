@@ -129,6 +129,16 @@ int fs_argsort(fs_sorter* s, int dtype, const void* keys, uint32_t* idx_out,
 int fs_sort_keys_copy(fs_sorter* s, int dtype, const void* keys_in,
                       void* keys_out, uint64_t n, int sync);
 
+/* Out-of-place stable pairs sort: (keys_in, vals_in) sorted by key into
+ * (keys_out, vals_out); equal keys keep their input order.  vals_in == NULL
+ * takes the input positions as values (an argsort that also returns the
+ * sorted keys).  Device or managed pointers, no two arrays overlapping; the
+ * inputs are not modified.  The first pass reads the inputs and the last
+ * pass writes the outputs (no extra copy). */
+int fs_sort_pairs_copy(fs_sorter* s, int dtype, const void* keys_in,
+                       const uint32_t* vals_in, void* keys_out,
+                       uint32_t* vals_out, uint64_t n, int sync);
+
 /* ---- host-slice sorts (sort_u32(&mut [u32]) etc.) ------------------------ */
 
 /* Copy host keys to the device, sort, copy back; synchronous.  Pinned host
@@ -237,6 +247,19 @@ int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n,
                           uint64_t gpos_base, const void* splitter_keys,
                           const uint64_t* splitter_gpos, int nsplit,
                           void* const* bucket_dst, int sync);
+
+/* fs_partition_dispatch with a u32 payload, for a multi-GPU sort_pairs or
+ * argsort: value i travels with key i to value_dst[b] at the key's position
+ * in bucket_dst[b].  vals == NULL sends each key's global position
+ * gpos_base + i instead (gpos_base + n <= 2^32).  Same pairing rule with
+ * fs_partition_count; within a bucket the keys keep their input order, so a
+ * stable local sort of the received pairs gives the globally stable order. */
+int fs_partition_dispatch_pairs(fs_sorter* s, int dtype, const void* keys,
+                                const uint32_t* vals, uint64_t n,
+                                uint64_t gpos_base, const void* splitter_keys,
+                                const uint64_t* splitter_gpos, int nsplit,
+                                void* const* bucket_dst,
+                                uint32_t* const* value_dst, int sync);
 
 /* CUDA IPC for the dispatch inboxes (one process per GPU): export a handle to
  * device memory from cudaMalloc (fs_alloc with managed = 0), open a peer's
