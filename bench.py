@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--log2n", type=int, default=32, help="total keys = 2^log2n")
     p.add_argument("--dist", choices=["uniform", "skew"], default="uniform")
     p.add_argument("--dtype", choices=["u32", "u64"], default="u32")
+    p.add_argument("--op", choices=["keys", "argsort", "pairs"], default="keys",
+                   help="N > 1: keys-only sample sort (the headline), or the payload forms")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile-steps", type=int, default=3)
@@ -66,8 +68,10 @@ def dist_env():
 
 
 def config(args, world):
+    what = {"keys": "sort", "argsort": "argsort (u32 global positions) of", "pairs": "sort_pairs (u32 values) of"}
     return {
-        "workload": f"configs[4]: sort {args.dtype} keys, {'uniform' if args.dist == 'uniform' else '70% in one 2^20 range'}"
+        "workload": f"configs[4]: {what[getattr(args, 'op', 'keys')]} {args.dtype} keys, "
+                    f"{'uniform' if args.dist == 'uniform' else '70% in one 2^20 range'}"
                     f", total 2^{args.log2n} keys partitioned over N GPUs",
         "keys_total": 1 << args.log2n,
         "keys_per_gpu": (1 << args.log2n) // world,
@@ -408,11 +412,20 @@ def run_multi(args):
     if args.dist == "skew":
         gen = _lib.GEN_SKEW_U32
     assert L.fs_generate(gen, 42, rank * m, m, keys_in.data_ptr(), stream.cuda_stream) == 0
+    op = args.op
+    vals_in = None
+    if op == "pairs":  # values: a scrambled global position per key
+        vals_in = ((torch.arange(m, dtype=torch.int64, device=dev) + rank * m) * 2654435761 & 0xFFFFFFFF).to(torch.int32)
     stream.synchronize()
     ss = SampleSorter(CudaOps(sorter, torch), dtype=dt)
+    vb = 0 if op == "keys" else 4  # payload bytes per key
 
     def step():
-        return ss.sort(keys_in, gpos_base=rank * m)
+        if op == "keys":
+            return ss.sort(keys_in, gpos_base=rank * m)
+        if op == "argsort":
+            return ss.sort_with_positions(keys_in, gpos_base=rank * m)
+        return ss.sort_pairs(keys_in, vals_in, gpos_base=rank * m)
 
     def timed(fn, steps):
         tdist.barrier()
@@ -439,7 +452,15 @@ def run_multi(args):
     clocks = clk.summary()
 
     # correctness of the timed output: sorted pieces, ordered across ranks,
-    # all keys accounted for
+    # all keys accounted for; with a payload, the values of this rank's own
+    # keys match the input
+    if op != "keys":
+        out, vout = out
+        if op == "argsort":
+            pos = vout.to(torch.int64) & 0xFFFFFFFF
+            own = (pos >= rank * m) & (pos < (rank + 1) * m)
+            assert bool((keys_in[pos[own] - rank * m] == out[own]).all()), "positions do not match the keys"
+        del vout
     o = out.cpu().numpy().view("u4" if kb == 4 else "u8")
     assert (o[1:] >= o[:-1]).all(), "rank output not sorted"
     edge = torch.tensor([int(o[0]) if o.size else -1, int(o[-1]) if o.size else -1, o.size],
@@ -460,25 +481,26 @@ def run_multi(args):
     t = sorter.last_kernel_times()
     sorter.set_kernel_timing(False)
     P = kb
-    pass_ms = [t[3 + 2 * p] for p in range(1, P)]  # stable passes (pass 0 ranks unstably)
+    pass_ms = [t[3 + 2 * p] for p in range(1, P)]  # stable passes (pass 0 of keys-only ranks unstably)
     pass_avg = sum(pass_ms) / len(pass_ms)
     peak, peak_kind = measured_peak_hbm()
     piece = out.numel()
-    achieved = piece * 2 * kb / (pass_avg * 1e-3) / 1e9
+    achieved = piece * 2 * (kb + vb) / (pass_avg * 1e-3) / 1e9
     # phase-summed roofline of the whole job (slowest rank holds max_piece):
     # bucket count + dispatch pass (3K; the dispatch's stores are the
     # exchange), local sort (K(1+2P) + K(P-1) counts) over HBM, and (G-1)/G
     # of the keys over NVLink at the measured 770 GB/s per direction
     nvlink = 770.0
-    hbm_b = m * 3 * kb + max_piece * (kb * (1 + 2 * P) + kb * (P - 1))
-    t_roof = hbm_b / (peak * 1e9) + m * kb * (world - 1) / world / (nvlink * 1e9)
+    vread = 4 if op == "pairs" else 0  # argsort's positions are made in the dispatch
+    hbm_b = m * (3 * kb + vread + vb) + max_piece * (kb * (1 + 2 * P) + kb * (P - 1) + vb * 2 * P)
+    t_roof = hbm_b / (peak * 1e9) + m * (kb + vb) * (world - 1) / world / (nvlink * 1e9)
     roofline = {
         "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
-        "kernel": "k_scatter, stable ranking (local sort pass)", "alg_bytes_per_launch": piece * 2 * kb,
+        "kernel": "k_scatter, stable ranking (local sort pass)", "alg_bytes_per_launch": piece * 2 * (kb + vb),
         "pass_ms": round(pass_avg, 4),
         "job_roofline_ms": round(t_roof * 1e3, 3), "job_frac": round(t_roof * 1e3 / ms, 4),
-        "job_model": "HBM: bucket count K + dispatch pass 2K (its stores land in the peers' inboxes) + local sort K(1+2P)+K(P-1) per key; NVLink (G-1)/G*K at 770 GB/s",
+        "job_model": "HBM: bucket count K + dispatch pass 2K (its stores land in the peers' inboxes) + local sort K(1+2P)+K(P-1) per key, plus V per key for each payload read and write; NVLink (G-1)/G*(K+V) at 770 GB/s",
     }
     value = n_total / (ms * 1e-3) / 1e6
 
@@ -487,21 +509,39 @@ def run_multi(args):
         h_in = torch.empty(m, dtype=tdt, pin_memory=True)
         h_in.copy_(keys_in.cpu())
         h_out = torch.empty(max_piece + (1 << 20), dtype=tdt, pin_memory=True)
+        if op != "keys":
+            hv_out = torch.empty(max_piece + (1 << 20), dtype=torch.int32, pin_memory=True)
+        if op == "pairs":
+            hv_in = torch.empty(m, dtype=torch.int32, pin_memory=True)
+            hv_in.copy_(vals_in.cpu())
 
         def e2e_step():
             d_in = torch.empty(m, dtype=tdt, device=dev)
             d_in.copy_(h_in, non_blocking=True)
-            r = ss.sort(d_in, gpos_base=rank * m)
-            h_out[: r.numel()].copy_(r, non_blocking=True)
-            return r.numel()
+            if op == "keys":
+                r = ss.sort(d_in, gpos_base=rank * m)
+                h_out[: r.numel()].copy_(r, non_blocking=True)
+                return r.numel()
+            if op == "argsort":
+                v = ss.argsort(d_in, gpos_base=rank * m)
+            else:
+                dv = torch.empty(m, dtype=torch.int32, device=dev)
+                dv.copy_(hv_in, non_blocking=True)
+                r, v = ss.sort_pairs(d_in, dv, gpos_base=rank * m)
+                h_out[: r.numel()].copy_(r, non_blocking=True)
+            hv_out[: v.numel()].copy_(v, non_blocking=True)
+            return v.numel()
 
         with torch.cuda.stream(stream):
             for _ in range(min(args.warmup, 3)):
                 e2e_step()
             ems, got = timed(e2e_step, args.steps)
+        h2d = m * kb + (m * 4 if op == "pairs" else 0)
+        d2h = int(got) * ({"keys": kb, "argsort": 4, "pairs": kb + 4}[op])
+        api = {"keys": "SampleSorter.sort", "argsort": "SampleSorter.argsort", "pairs": "SampleSorter.sort_pairs"}[op]
         e2e = {"value": round(n_total / (ems * 1e-3) / 1e6, 2), "unit": UNIT,
-               "h2d_bytes_per_step": m * kb, "d2h_bytes_per_step": int(got) * kb,
-               "ms_per_step": round(ems, 3), "api": "SampleSorter.sort on pinned host shards (H2D, sort, D2H per rank)"}
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": round(ems, 3), "api": f"{api} on pinned host shards (H2D, sort, D2H per rank)"}
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -510,6 +550,7 @@ def run_multi(args):
         "roofline": roofline, "cpu_baseline": None, "e2e": e2e, "clocks": clocks,
         "gpu_launches": (5 + 3 + 3 * P) * args.steps,
         "balance": {"max_piece": max_piece, "mean_piece": n_total // world, "recv_counts_rank0": recv if rank == 0 else None},
+        "op": op,
         "impl": "ours",
     }
     if rank == 0:

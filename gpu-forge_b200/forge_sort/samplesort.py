@@ -296,6 +296,11 @@ class SampleSorter:
         keys."""
         return self._run(keys, None, True, gpos_base)[1]
 
+    def sort_with_positions(self, keys, gpos_base: Optional[int] = None):
+        """(keys piece, positions piece): argsort that also returns the
+        sorted keys the local step produces anyway."""
+        return self._run(keys, None, True, gpos_base)
+
     def _run(self, keys, vals, payload: bool, gpos_base: Optional[int]):
         torch, dist, dt = self.torch, self.dist, self.dt
         G, r = self._world()
