@@ -345,6 +345,34 @@ class MultiGpuSorter {
     return out_n;
   }
 
+  // The stable pairs form: vals[i] (device, shard_n[i] u32) travel with the
+  // keys into out_vals[i] (room for out_cap[i]); with `vals` empty, every
+  // key's global position is sent instead (an argsort).  Same sizing rule.
+  template <typename T>
+  std::vector<uint64_t> sort_pairs(const std::vector<T*>& shards, const std::vector<const uint32_t*>& vals,
+                                   const std::vector<uint64_t>& shard_n, const std::vector<T*>& out,
+                                   const std::vector<uint32_t*>& out_vals, const std::vector<uint64_t>& out_cap,
+                                   std::vector<uint64_t>* needed = nullptr) {
+    if (shards.size() != g_ || shard_n.size() != g_ || out.size() != g_ || out_cap.size() != g_ ||
+        out_vals.size() != g_ || (!vals.empty() && vals.size() != g_))
+      throw std::invalid_argument("one shard, value array and output per device");
+    std::vector<void*> sp(shards.begin(), shards.end()), op(out.begin(), out.end());
+    std::vector<uint64_t> out_n(g_);
+    const int rc = fs_mg_sort_pairs(h_, SortKey<T>::DTYPE, sp.data(), vals.empty() ? nullptr : vals.data(),
+                                    shard_n.data(), op.data(), out_vals.data(), out_cap.data(), out_n.data());
+    if (rc == FS_E_INVALID) {
+      bool over = false;
+      for (size_t i = 0; i < g_; ++i) over = over || out_n[i] > out_cap[i];
+      if (over) {
+        if (needed) *needed = out_n;
+        throw std::length_error(fs_mg_last_error(h_));
+      }
+      throw std::invalid_argument(fs_mg_last_error(h_));
+    }
+    if (rc != FS_OK) throw SortError::gpu_execution(fs_mg_last_error(h_));
+    return out_n;
+  }
+
  private:
   fs_mg* h_ = nullptr;
   size_t g_ = 0;

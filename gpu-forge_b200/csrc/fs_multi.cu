@@ -13,6 +13,11 @@
 //      straight into its destination device's inbox (peer access over
 //      NVLink, plain stores), at the offset the matrix gives;
 //   4. local sort of every inbox into the caller's output buffer.
+// fs_mg_sort_pairs carries a u32 per key (the caller's values, or each key's
+// global position for an argsort) in a second region of every inbox and
+// ends with a stable local pairs sort: keys reach an inbox in global-position
+// order (lower devices first, each in input order), so equal keys end in
+// global input order.
 #include "forgesort.h"
 #include "fs_device.cuh"
 
@@ -112,8 +117,9 @@ int each_device(fs_mg* mg, F&& f) {
 }
 
 template <typename K, int XF>
-int mg_sort(fs_mg* mg, int dtype, void* const* shards, const uint64_t* shard_n, void* const* out,
-            const uint64_t* out_cap, uint64_t* out_n) {
+int mg_sort(fs_mg* mg, int dtype, void* const* shards, const uint32_t* const* vals, bool payload,
+            const uint64_t* shard_n, void* const* out, uint32_t* const* out_vals, const uint64_t* out_cap,
+            uint64_t* out_n) {
   const int G = mg->g;
   const uint32_t S = MG_SAMPLES;
   uint64_t base[MG_MAX + 1] = {};
@@ -168,8 +174,10 @@ int mg_sort(fs_mg* mg, int dtype, void* const* shards, const uint64_t* shard_n, 
   if (!fits)
     return mg_fail(mg, FS_E_INVALID, "an output piece exceeds its capacity (out_n holds the sizes needed)");
 
-  // inboxes: grow-only, one capacity for all devices
-  const uint64_t need_bytes = need * sizeof(K);
+  // inboxes: grow-only, one capacity for all devices; with a payload the
+  // values follow the keys from a 256-byte boundary
+  const uint64_t voff = payload ? (need * sizeof(K) + 255) / 256 * 256 : 0;
+  const uint64_t need_bytes = payload ? voff + need * 4 : need * sizeof(K);
   if (need_bytes > mg->inbox_bytes) {
     const uint64_t cap = std::max<uint64_t>(need_bytes + need_bytes / 16, 1u << 20);
     for (int i = 0; i < G; ++i) {
@@ -186,14 +194,21 @@ int mg_sort(fs_mg* mg, int dtype, void* const* shards, const uint64_t* shard_n, 
   // 3. dispatch: device i's bucket b goes to inbox b after the keys of lower devices
   for (int i = 0; i < G; ++i) {
     void* dst[MG_MAX];
+    uint32_t* vdst[MG_MAX];
     for (int b = 0; b < G; ++b) {
       uint64_t start = 0;
       for (int s = 0; s < i; ++s) start += M[(size_t)s * G + b];
       dst[b] = static_cast<char*>(mg->inbox[b]) + start * sizeof(K);
+      vdst[b] = reinterpret_cast<uint32_t*>(static_cast<char*>(mg->inbox[b]) + voff + start * 4);
     }
     MG_CUDA(mg, cudaSetDevice(mg->dev[i]));
-    rc = fs_partition_dispatch(mg->s[i], dtype, shards[i], shard_n[i], base[i], mg->spl_keys[i],
-                               static_cast<const uint64_t*>(mg->spl_gpos[i]), nsplit, dst, 0);
+    if (payload)
+      rc = fs_partition_dispatch_pairs(mg->s[i], dtype, shards[i], vals ? vals[i] : nullptr, shard_n[i], base[i],
+                                       mg->spl_keys[i], static_cast<const uint64_t*>(mg->spl_gpos[i]), nsplit, dst,
+                                       vdst, 0);
+    else
+      rc = fs_partition_dispatch(mg->s[i], dtype, shards[i], shard_n[i], base[i], mg->spl_keys[i],
+                                 static_cast<const uint64_t*>(mg->spl_gpos[i]), nsplit, dst, 0);
     if (rc) return mg_from(mg, i, rc);
   }
   // every inbox is complete once every device's dispatch is
@@ -204,7 +219,13 @@ int mg_sort(fs_mg* mg, int dtype, void* const* shards, const uint64_t* shard_n, 
   for (int i = 0; i < G; ++i) {
     if (out_n[i] == 0) continue;
     MG_CUDA(mg, cudaSetDevice(mg->dev[i]));
-    if ((rc = mg_from(mg, i, fs_sort_keys_copy(mg->s[i], dtype, mg->inbox[i], out[i], out_n[i], 0)))) return rc;
+    if (payload)
+      rc = fs_sort_pairs_copy(mg->s[i], dtype, mg->inbox[i],
+                              reinterpret_cast<const uint32_t*>(static_cast<char*>(mg->inbox[i]) + voff), out[i],
+                              out_vals[i], out_n[i], 0);
+    else
+      rc = fs_sort_keys_copy(mg->s[i], dtype, mg->inbox[i], out[i], out_n[i], 0);
+    if ((rc = mg_from(mg, i, rc))) return rc;
   }
   for (int i = 0; i < G; ++i)
     if ((rc = mg_from(mg, i, fs_synchronize(mg->s[i])))) return rc;
@@ -283,26 +304,47 @@ int fs_mg_destroy(fs_mg* mg) {
 
 const char* fs_mg_last_error(const fs_mg* mg) { return mg ? mg->err.c_str() : ""; }
 
-int fs_mg_sort_keys(fs_mg* mg, int dtype, void* const* shards, const uint64_t* shard_n, void* const* out,
-                    const uint64_t* out_cap, uint64_t* out_n) {
+namespace {
+int mg_entry(fs_mg* mg, int dtype, void* const* shards, const uint32_t* const* vals, bool payload,
+             const uint64_t* shard_n, void* const* out, uint32_t* const* out_vals, const uint64_t* out_cap,
+             uint64_t* out_n) {
   if (!mg) return FS_E_INVALID;
   if (dtype < FS_U32 || dtype > FS_F64) return mg_fail(mg, FS_E_INVALID, "unknown dtype %d", dtype);
-  if (!shards || !shard_n || !out || !out_cap || !out_n) return mg_fail(mg, FS_E_INVALID, "NULL argument");
+  if (!shards || !shard_n || !out || !out_cap || !out_n || (payload && !out_vals))
+    return mg_fail(mg, FS_E_INVALID, "NULL argument");
   uint64_t total = 0;
   for (int i = 0; i < mg->g; ++i) {
     if (shard_n[i] && !shards[i]) return mg_fail(mg, FS_E_INVALID, "shard %d is NULL", i);
+    if (payload && vals && shard_n[i] && !vals[i]) return mg_fail(mg, FS_E_INVALID, "values of shard %d are NULL", i);
     total += shard_n[i];
   }
   for (int i = 0; i < mg->g; ++i) out_n[i] = 0;
   if (total == 0) return FS_OK;
+  if (payload && !vals && total > (1ull << 32))
+    return mg_fail(mg, FS_E_INVALID, "%llu keys: global positions past 2^32 do not fit u32",
+                   (unsigned long long)total);
+#define MG_CALL(K, XF) mg_sort<K, XF>(mg, dtype, shards, vals, payload, shard_n, out, out_vals, out_cap, out_n)
   switch (dtype) {
-    case FS_U32: return mg_sort<uint32_t, XF_NONE>(mg, dtype, shards, shard_n, out, out_cap, out_n);
-    case FS_I32: return mg_sort<uint32_t, XF_SIGN>(mg, dtype, shards, shard_n, out, out_cap, out_n);
-    case FS_F32: return mg_sort<uint32_t, XF_FLOAT>(mg, dtype, shards, shard_n, out, out_cap, out_n);
-    case FS_U64: return mg_sort<uint64_t, XF_NONE>(mg, dtype, shards, shard_n, out, out_cap, out_n);
-    case FS_I64: return mg_sort<uint64_t, XF_SIGN>(mg, dtype, shards, shard_n, out, out_cap, out_n);
-    default: return mg_sort<uint64_t, XF_FLOAT>(mg, dtype, shards, shard_n, out, out_cap, out_n);
+    case FS_U32: return MG_CALL(uint32_t, XF_NONE);
+    case FS_I32: return MG_CALL(uint32_t, XF_SIGN);
+    case FS_F32: return MG_CALL(uint32_t, XF_FLOAT);
+    case FS_U64: return MG_CALL(uint64_t, XF_NONE);
+    case FS_I64: return MG_CALL(uint64_t, XF_SIGN);
+    default: return MG_CALL(uint64_t, XF_FLOAT);
   }
+#undef MG_CALL
+}
+}  // namespace
+
+int fs_mg_sort_keys(fs_mg* mg, int dtype, void* const* shards, const uint64_t* shard_n, void* const* out,
+                    const uint64_t* out_cap, uint64_t* out_n) {
+  return mg_entry(mg, dtype, shards, nullptr, false, shard_n, out, nullptr, out_cap, out_n);
+}
+
+int fs_mg_sort_pairs(fs_mg* mg, int dtype, void* const* shards, const uint32_t* const* vals,
+                     const uint64_t* shard_n, void* const* out, uint32_t* const* out_vals, const uint64_t* out_cap,
+                     uint64_t* out_n) {
+  return mg_entry(mg, dtype, shards, vals, true, shard_n, out, out_vals, out_cap, out_n);
 }
 
 }  // extern "C"

@@ -62,6 +62,7 @@ SIGNATURES = {
     "fs_mg_destroy": (_i32, [_vp]),
     "fs_mg_last_error": (ctypes.c_char_p, [_vp]),
     "fs_mg_sort_keys": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "fs_mg_sort_pairs": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "fs_partition_count": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp]),
     "fs_partition_dispatch": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _i32]),
     "fs_ipc_export": (_i32, [_vp, _vp, _vp]),

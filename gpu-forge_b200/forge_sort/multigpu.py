@@ -39,19 +39,20 @@ class MultiGpuSorter:
         except Exception:
             pass
 
-    def sort(self, dt, shards: List, headroom: float = 1.125) -> List:
-        """Sort the concatenation of `shards` (1-D torch tensors holding raw
-        key bits, shard i on devices[i]); returns the sorted pieces."""
-        import torch
-        name = dtype_name(dt)
+    def _check(self, name, shards, what="shard", size=None):
         G = len(self.devices)
         if len(shards) != G:
-            raise ValueError(f"{len(shards)} shards for {G} devices")
+            raise ValueError(f"{len(shards)} {what}s for {G} devices")
         for i, t in enumerate(shards):
             if t.device.type != "cuda" or t.device.index != self.devices[i] or not t.is_contiguous():
-                raise ValueError(f"shard {i} must be a contiguous tensor on cuda:{self.devices[i]}")
-            if t.element_size() != _DT[name][2]:
-                raise TypeError(f"shard {i} has {t.element_size()}-byte elements, {name} needs {_DT[name][2]}")
+                raise ValueError(f"{what} {i} must be a contiguous tensor on cuda:{self.devices[i]}")
+            want = size if size is not None else _DT[name][2]
+            if t.element_size() != want:
+                raise TypeError(f"{what} {i} has {t.element_size()}-byte elements, {want} needed")
+
+    def _run(self, name, shards, vals, payload: bool, headroom: float):
+        import torch
+        G = len(self.devices)
         total = sum(t.numel() for t in shards)
         cap = [int(total / G * headroom) + 1024] * G
         L = _lib.load()
@@ -59,16 +60,51 @@ class MultiGpuSorter:
         PV = ctypes.c_void_p * G
         for _attempt in range(2):
             outs = [torch.empty(cap[i], dtype=shards[i].dtype, device=shards[i].device) for i in range(G)]
+            vouts = [torch.empty(cap[i], dtype=torch.int32, device=shards[i].device) for i in range(G)] \
+                if payload else None
             for t in shards:
                 torch.cuda.current_stream(t.device).synchronize()  # shards ready
             out_n = U64()
-            rc = L.fs_mg_sort_keys(self._h, _DT[name][0], PV(*[t.data_ptr() for t in shards]),
-                                   U64(*[t.numel() for t in shards]), PV(*[t.data_ptr() for t in outs]),
-                                   U64(*cap), out_n)
+            sp, sn = PV(*[t.data_ptr() for t in shards]), U64(*[t.numel() for t in shards])
+            op = PV(*[t.data_ptr() for t in outs])
+            if payload:
+                vp = PV(*[v.data_ptr() for v in vals]) if vals is not None else None
+                rc = L.fs_mg_sort_pairs(self._h, _DT[name][0], sp, vp, sn, op, PV(*[v.data_ptr() for v in vouts]),
+                                        U64(*cap), out_n)
+            else:
+                rc = L.fs_mg_sort_keys(self._h, _DT[name][0], sp, sn, op, U64(*cap), out_n)
             if rc == _lib.OK:
-                return [outs[i][: out_n[i]] for i in range(G)]
+                keys = [outs[i][: out_n[i]] for i in range(G)]
+                return (keys, [vouts[i][: out_n[i]] for i in range(G)]) if payload else keys
             if rc == _lib.E_INVALID and any(out_n[i] > cap[i] for i in range(G)):
                 cap = [max(cap[i], int(out_n[i])) for i in range(G)]  # resize and retry once
                 continue
             raise from_status(rc, L.fs_mg_last_error(self._h).decode())
         raise RuntimeError("MultiGpuSorter: output sizing failed")
+
+    def sort(self, dt, shards: List, headroom: float = 1.125) -> List:
+        """Sort the concatenation of `shards` (1-D torch tensors holding raw
+        key bits, shard i on devices[i]); returns the sorted pieces."""
+        name = dtype_name(dt)
+        self._check(name, shards)
+        return self._run(name, shards, None, False, headroom)
+
+    def sort_pairs(self, dt, shards: List, values: List, headroom: float = 1.125):
+        """Stable sort of (key, value) pairs by key across the devices:
+        values[i] is an int32 tensor of u32 values beside shards[i].  Returns
+        (key pieces, value pieces); equal keys keep their global input
+        order."""
+        name = dtype_name(dt)
+        self._check(name, shards)
+        self._check(name, values, "value", 4)
+        if any(v.numel() != t.numel() for v, t in zip(values, shards)):
+            raise ValueError("one value per key")
+        return self._run(name, shards, values, True, headroom)
+
+    def argsort(self, dt, shards: List, headroom: float = 1.125):
+        """Stable argsort across the devices: (key pieces, position pieces),
+        positions into the concatenated shards as u32 in int32 tensors (at
+        most 2^32 keys in total)."""
+        name = dtype_name(dt)
+        self._check(name, shards)
+        return self._run(name, shards, None, True, headroom)

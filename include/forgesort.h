@@ -297,6 +297,18 @@ int fs_mg_sort_keys(fs_mg* mg, int dtype, void* const* shards,
                     const uint64_t* shard_n, void* const* out,
                     const uint64_t* out_cap, uint64_t* out_n);
 
+/* fs_mg_sort_keys with a u32 payload: a stable multi-GPU sort_pairs, or an
+ * argsort.  vals[i] (device memory of devices[i], shard_n[i] values) travels
+ * with shard i's keys; vals == NULL sends each key's global position instead
+ * (position = its index in the concatenated shards; at most 2^32 keys in
+ * total).  out_vals[i] (device memory of devices[i], room for out_cap[i]
+ * values) receives piece i's values.  Equal keys keep their global input
+ * order.  Same sizing rule as fs_mg_sort_keys. */
+int fs_mg_sort_pairs(fs_mg* mg, int dtype, void* const* shards,
+                     const uint32_t* const* vals, const uint64_t* shard_n,
+                     void* const* out, uint32_t* const* out_vals,
+                     const uint64_t* out_cap, uint64_t* out_n);
+
 /* ---- allocation-free form ------------------------------------------------ */
 
 /* Sort n keys in place at `keys` (device memory of the current device),

@@ -65,3 +65,43 @@ def test_multi_gpu_sorter_one_process_matches_oracle(world):
                 assert max(p.numel() for p in pieces) < 1.1 * mean + 1024  # regular-sampling balance
     finally:
         mg.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_multi_gpu_sorter_argsort_and_pairs_stable(world):
+    """fs_mg_sort_pairs: values (or global positions) travel with the keys;
+    the pieces concatenated equal the oracle's stable order of the whole
+    input, Zipf duplicates split across devices included."""
+    import numpy as np
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs, {torch.cuda.device_count()} visible")
+    import forge_sort
+    from oracle import oracle as orc
+    from tests._mgpu_worker import scrambled_values, shard_bounds
+    mg = forge_sort.MultiGpuSorter(list(range(world)))
+    try:
+        for gen, dt, n, mode in [("zipf_u32", "u32", 2_000_003, None), ("f64_logu", "f64", 1 << 20, "one_empty"),
+                                 ("i32", "i32", 1_000_003, "ragged")]:
+            full = orc.gen(gen, n, seed=42)
+            cuts = shard_bounds(n, world, mode)
+            iv = np.int32 if full.itemsize == 4 else np.int64
+            shards = [torch.from_numpy(np.ascontiguousarray(full[cuts[i]:cuts[i + 1]]).view(iv)).to(f"cuda:{i}")
+                      for i in range(world)]
+            order = orc.argsort(full, dt)
+            bits = orc.BITS_DTYPE[dt]
+            keys, pos = mg.argsort(dt, shards)
+            assert np.array_equal(np.concatenate([k.cpu().numpy() for k in keys]).view(bits),
+                                  np.ascontiguousarray(full[order]).view(bits)), gen
+            assert np.array_equal(np.concatenate([p.cpu().numpy() for p in pos]).view(np.uint32),
+                                  order.astype(np.uint32)), gen
+            vals = [torch.from_numpy(scrambled_values(int(cuts[i]), int(cuts[i + 1])).view(np.int32)).to(f"cuda:{i}")
+                    for i in range(world)]
+            keys, vout = mg.sort_pairs(dt, shards, vals)
+            assert np.array_equal(np.concatenate([k.cpu().numpy() for k in keys]).view(bits),
+                                  np.ascontiguousarray(full[order]).view(bits)), gen
+            assert np.array_equal(np.concatenate([v.cpu().numpy() for v in vout]).view(np.uint32),
+                                  scrambled_values(0, n)[order]), gen
+    finally:
+        mg.close()
