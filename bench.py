@@ -548,7 +548,7 @@ def run_multi(args):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": dt, "data": "synthetic", "config": config(args, world),
         "roofline": roofline, "cpu_baseline": None, "e2e": e2e, "clocks": clocks,
-        "gpu_launches": (5 + 3 + 3 * P) * args.steps,
+        "gpu_launches": (5 + 2 + 3 * P) * args.steps,  # count + dispatch chain, local sort 2 + 3P
         "balance": {"max_piece": max_piece, "mean_piece": n_total // world, "recv_counts_rank0": recv if rank == 0 else None},
         "op": op,
         "impl": "ours",

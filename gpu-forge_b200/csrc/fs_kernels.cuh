@@ -62,6 +62,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Programmatic dependent launch: a kernel of the sort's chain may be
+// scheduled while its predecessor on the stream is still draining, and
+// waits here -- its first statement, on every path -- until the predecessor
+// has completed and its memory operations are visible.  Launched without
+// the attribute, the wait returns at once.
+__device__ __forceinline__ void chain_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // global -> shared bulk copy; both addresses 16-byte aligned, bytes % 16 == 0
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -234,6 +241,7 @@ template <typename K, int XF, int BLOCK, bool VEC>
 __global__ void __launch_bounds__(BLOCK)
     k_first_count(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
                   uint32_t* __restrict__ counts /* [count][RADIX] */) {
+  chain_wait();
   constexpr int WARPS = BLOCK / 32;
   __shared__ uint32_t hw[WARPS][RADIX];
   __shared__ uint32_t tot[RADIX];
@@ -379,6 +387,7 @@ __global__ void __launch_bounds__(BLOCK)
 // the caller wants it.  Replaces sort_msd_prep (shaders/sort.metal:153-181).
 // --------------------------------------------------------------------------
 __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanArgs a) {
+  chain_wait();
   const int d = threadIdx.x;
   __shared__ int s_exec[MAX_PASSES];
   const unsigned long long c0 = ctl->hist[0][d];
@@ -473,6 +482,7 @@ template <typename K, int XF, int BLOCK>
 __global__ void __launch_bounds__(BLOCK)
     k_count(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
             uint32_t* __restrict__ counts /* [count][RADIX] */) {
+  chain_wait();
   const uint32_t flags = ctl->pass[pass].flags;
   if (!(flags & PD_EXEC) || pass == 0) return;
   const K* keys = static_cast<const K*>(ctl->pass[pass].kin);
@@ -529,6 +539,7 @@ constexpr int SCAN_WARPS = 32;
 __global__ void __launch_bounds__(SCAN_WARPS * 32)
     k_slice_scan(SortCtl* __restrict__ ctl, const int pass, const Slices sl,
                  const uint32_t* __restrict__ counts, uint32_t* __restrict__ offsets, const int relative) {
+  chain_wait();
   const uint32_t flags = ctl->pass[pass].flags;
   if (!(flags & PD_EXEC)) return;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -883,6 +894,7 @@ __global__ void __launch_bounds__(BLOCK, MINB)
   __shared__ K s_spk[D::STAGE ? (R < 8 ? 8 : R) : 1];  // the splitter search pads to 8
   __shared__ uint64_t s_spg[D::STAGE ? (R < 8 ? 8 : R) : 1];
 
+  chain_wait();
   const PassDesc pd = ctl->pass[pass];
   if (!(pd.flags & PD_EXEC)) return;
   if (MODE == SCATTER_UNSTABLE && !(pd.flags & PD_UNSTABLE)) return;
@@ -977,58 +989,99 @@ __global__ void __launch_bounds__(BLOCK, MINB)
 }
 
 // --------------------------------------------------------------------------
-// Small sorts (n <= SMALL_N): one CTA sorts everything in shared memory with
-// a bitonic network over (ordered key, input position), so equal keys keep
-// their input order (stable, as the radix passes are).  One launch instead of
-// fifteen, for the short arrays of e.g. gpu-search's argsort_u64
-// (gpu-search/src/search/content.rs:849-884).  Payloads are staged too, so
-// in-place calls are safe.
+// Small sorts (n <= SMALL_N_MAX): one CTA sorts everything in shared memory
+// with a bitonic network, one launch instead of a radix pass chain, for the
+// short arrays of e.g. gpu-search's argsort_u64
+// (gpu-search/src/search/content.rs:849-884).  With a payload (argsort,
+// pairs) the network orders (ordered key, input position), so equal keys keep
+// their input order, as the radix passes do; keys alone need no position
+// (equal keys are equal bits).  Inputs are staged first, so in-place calls
+// are safe.
+//
+// The block has max(32, npad/4) threads (npad = n rounded up to a power of
+// two, at most 1024 threads); every thread does PP = npad / (2 * threads)
+// compare-exchanges per stage.  Warp w owns elements [w*E, (w+1)*E), E =
+// 64 * PP: a stage with distance j <= E/2 only touches the warp's own
+// elements, so it follows the previous warp-local stage after __syncwarp;
+// only the stages with larger j (15 of the 78 at npad = 4096) and their
+// neighbours need a block barrier.
 // --------------------------------------------------------------------------
-constexpr uint32_t SMALL_N = 4096;
-constexpr int SMALL_BLOCK = 1024;
-template <typename K, int XF>
-__global__ void __launch_bounds__(SMALL_BLOCK)
+// Measured on B200 (one sort per launch, device time): the single CTA beats
+// the radix chain up to 8192 keys without a payload (u32: 55 vs 63 us at
+// 8192) and up to 4096 with one (argsort u32 at 4096: 42 vs 55 us; at 8192:
+// 86 vs 56 us).
+constexpr uint32_t SMALL_N_MAX = 8192;
+constexpr uint32_t SMALL_N_PAYLOAD_MAX = 4096;
+constexpr int SMALL_BLOCK_MAX = 1024;
+
+template <typename K, bool VALS>
+__device__ __forceinline__ void small_cx(K* sk, uint32_t* si, uint32_t i, uint32_t l, bool up) {
+  const K a = sk[i], b = sk[l];
+  bool swap;
+  uint32_t ia = 0, ib = 0;
+  if constexpr (VALS) {
+    ia = si[i];
+    ib = si[l];
+    swap = (a > b || (a == b && ia > ib)) == up;
+  } else {
+    swap = (a > b) == up;
+  }
+  if (swap) {
+    sk[i] = b;
+    sk[l] = a;
+    if constexpr (VALS) {
+      si[i] = ib;
+      si[l] = ia;
+    }
+  }
+}
+
+template <typename K, int XF, bool VALS>
+__global__ void __launch_bounds__(SMALL_BLOCK_MAX)
     k_small_sort(const K* __restrict__ kin, K* __restrict__ kout, const uint32_t* __restrict__ vin,
-                 uint32_t* __restrict__ vout, const uint32_t n, const uint32_t npad, const int has_vals,
-                 const int write_keys) {
+                 uint32_t* __restrict__ vout, const uint32_t n, const uint32_t npad, const int write_keys) {
   extern __shared__ __align__(16) unsigned char sm[];
   K* sk = reinterpret_cast<K*>(sm);
-  uint32_t* si = reinterpret_cast<uint32_t*>(sm + (size_t)npad * sizeof(K));
-  uint32_t* sv = si + npad;
-  const bool synth = has_vals && vin == nullptr;
-  for (uint32_t i = threadIdx.x; i < npad; i += SMALL_BLOCK) {
+  uint32_t* si = reinterpret_cast<uint32_t*>(sm + (size_t)npad * sizeof(K));  // input positions (VALS)
+  uint32_t* sv = si + npad;                                                    // payload (VALS)
+  const uint32_t B = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t pp = npad / (2 * B) > 0 ? npad / (2 * B) : 1;  // pairs per thread
+  const uint32_t half = npad / 2;
+  const uint32_t local_j = 32 * pp;  // j <= local_j: the stage stays inside each warp's elements
+  for (uint32_t i = tid; i < npad; i += B) {
     if (i < n) {
       sk[i] = to_ordered<K, XF>(kin[i]);
-      si[i] = i;
-      if (has_vals) sv[i] = synth ? i : vin[i];
-    } else {  // padding sorts after every real key: largest key, largest position
+      if constexpr (VALS) {
+        si[i] = i;
+        sv[i] = vin ? vin[i] : i;
+      }
+    } else {  // padding sorts after every real key: largest key (and position)
       sk[i] = ~K(0);
-      si[i] = 0xffffffffu;
+      if constexpr (VALS) si[i] = 0xffffffffu;
+    }
+  }
+  uint32_t prev_j = npad;  // the loads above are block-strided: start with a barrier
+  for (uint32_t k = 2; k <= npad; k <<= 1) {
+    for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+      if (j > local_j || prev_j > local_j)
+        __syncthreads();
+      else
+        __syncwarp();
+      const uint32_t lj = 31 - __clz(j);
+      for (uint32_t r = 0; r < pp; ++r) {
+        const uint32_t q = warp * 32 * pp + r * 32 + lane;  // this warp's pairs
+        if (q < half) {
+          const uint32_t i = ((q >> lj) << (lj + 1)) | (q & (j - 1));  // q with a 0 bit inserted at lj
+          small_cx<K, VALS>(sk, si, i, i | j, (i & k) == 0);
+        }
+      }
+      prev_j = j;
     }
   }
   __syncthreads();
-  for (uint32_t k = 2; k <= npad; k <<= 1) {
-    for (uint32_t j = k >> 1; j > 0; j >>= 1) {
-      for (uint32_t i = threadIdx.x; i < npad; i += SMALL_BLOCK) {
-        const uint32_t l = i ^ j;
-        if (l > i) {
-          const K a = sk[i], b = sk[l];
-          const uint32_t ia = si[i], ib = si[l];
-          const bool greater = a > b || (a == b && ia > ib);
-          if (greater == ((i & k) == 0)) {
-            sk[i] = b;
-            sk[l] = a;
-            si[i] = ib;
-            si[l] = ia;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  for (uint32_t i = threadIdx.x; i < n; i += SMALL_BLOCK) {
+  for (uint32_t i = tid; i < n; i += B) {
     if (write_keys) kout[i] = from_ordered<K, XF>(sk[i]);
-    if (has_vals) vout[i] = sv[si[i]];
+    if constexpr (VALS) vout[i] = sv[si[i]];
   }
 }
 
@@ -1086,6 +1139,7 @@ __global__ void __launch_bounds__(256)
 template <typename K>
 __global__ void __launch_bounds__(256)
     k_finalize(SortCtl* __restrict__ ctl, const uint64_t n, int* __restrict__ host_err) {
+  chain_wait();
   const FinalDesc f = ctl->fin;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   const uint64_t i0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;

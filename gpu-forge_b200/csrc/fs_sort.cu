@@ -40,7 +40,8 @@ struct fs_sorter {
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
   void* dst_tab = nullptr;  // sample-sort dispatch: 256 destination pointers
-  bool no_small = false;  // FORGESORT_SMALL_SORT=0: small sorts take the radix passes
+  uint32_t small_max = SMALL_N_MAX;  // single-CTA sorts up to this n (FORGESORT_SMALL_SORT);
+                                     // with a payload up to min(small_max, SMALL_N_PAYLOAD_MAX)
   // fs_host_sort_keys_copy_async: two device buffers used in turn, and copy
   // streams of their own so one call's copies overlap the next call's work
   struct PipeSlot {
@@ -312,6 +313,37 @@ int scatter_occupancy(const Exec& e) {
   return bps;
 }
 
+// Kernels of one sort follow each other on the sorter's stream.  Launched
+// with programmatic stream serialization, each is scheduled while its
+// predecessor drains instead of after it has finished; every such kernel
+// opens with chain_wait(), which holds it until the predecessor's writes are
+// visible, so results are unchanged.  FORGESORT_CHAIN_LAUNCH=0 launches
+// them plainly.
+bool chain_launch_on() {
+  static const bool on = [] {
+    const char* t = getenv("FORGESORT_CHAIN_LAUNCH");
+    return !(t && atoi(t) == 0);
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+int chain_launch(const Exec& e, void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = e.stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = chain_launch_on() ? 1 : 0;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (err != cudaSuccess) return cuda_fail(e.s, err, "cudaLaunchKernelEx");
+  return FS_OK;
+}
+
 template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
   using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS>;
@@ -319,9 +351,8 @@ int launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const 
   if (bps < 0) return -bps;
   const uint64_t cap = (uint64_t)bps * e.sm_count;
   const unsigned grid = (unsigned)(sl.count < cap ? sl.count : cap);
-  k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D><<<grid, C::BLOCK, Ly::BYTES, e.stream>>>(
-      e.ctl, pass, n, sl, e.offsets, e.timeout_ns, dfn, gpos_base);
-  return FS_OK;
+  return chain_launch(e, k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D>, grid, C::BLOCK, Ly::BYTES,
+                      e.ctl, pass, n, sl, static_cast<const uint32_t*>(e.offsets), e.timeout_ns, dfn, gpos_base);
 }
 
 // Cut n keys into contiguous slices of whole `unit`-key blocks (a multiple of
@@ -361,31 +392,34 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
   // 2. plan
   PlanArgs pa = a;
   pa.trivial_from_bits = 1;
+  int rc;
   t_begin(e);
-  k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, pa);
+  if ((rc = chain_launch(e, k_plan, 1, RADIX, 0, e.ctl, pa))) return rc;
   t_end(e);
   // 3. passes: count (pass 0 was counted above), slice scan, scatter
   int nl = 2;
   for (int p = 0; p < P; ++p) {
     t_begin(e);
-    k_count<K, XF, HIST_BLOCK><<<sg, HIST_BLOCK, 0, e.stream>>>(e.ctl, p, n, sl, e.counts);
-    k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, p, sl, e.counts, e.offsets, 0);
+    if (p > 0) {
+      if ((rc = chain_launch(e, k_count<K, XF, HIST_BLOCK>, sg, HIST_BLOCK, 0, e.ctl, p, n, sl, e.counts))) return rc;
+      ++nl;
+    }
+    if ((rc = chain_launch(e, k_slice_scan, SCAN_GROUPS, SCAN_WARPS * 32, 0, e.ctl, p, sl,
+                           static_cast<const uint32_t*>(e.counts), e.offsets, 0)))
+      return rc;
     t_end(e);
     t_begin(e);
     const RadixDigit dg{p * RADIX_BITS};
-    int rc;
     if (a.has_vals) {
       rc = launch_scatter<K, true, XF, StableCfg<K, true>, SCATTER_ANY>(e, p, n, sl, dg, 0ull);
-      nl += 3;
     } else if (a.unstable_first && p == 0) {
       // pass 0, when it runs, is the first executed pass: it may rank
       // unstably.  (If it is trivial, the stable pass 1 kernel ranks pass 1.)
       rc = launch_scatter<K, false, XF, UnstableCfg<K>, SCATTER_UNSTABLE>(e, p, n, sl, dg, 0ull);
-      nl += 3;
     } else {
       rc = launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_ANY>(e, p, n, sl, dg, 0ull);
-      nl += 3;
     }
+    nl += 2;  // scan, scatter
     t_end(e);
     if (rc) return rc;
   }
@@ -393,7 +427,8 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
   uint64_t fb = (n + 255) / 256;
   const uint64_t fcap = (uint64_t)e.sm_count * 4;
   t_begin(e);
-  k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, e.stream>>>(e.ctl, n, e.err_out);
+  if ((rc = chain_launch(e, k_finalize<K>, (unsigned)(fb < fcap ? fb : fcap), 256, 0, e.ctl, n, e.err_out)))
+    return rc;
   t_end(e);
   if (launches) *launches = nl + 1;
   FS_CUDA(e.s, cudaGetLastError());
@@ -446,25 +481,33 @@ Exec exec_of(fs_sorter* s) {
 }
 
 // Small sorts: one CTA, everything in shared memory (k_small_sort).
-template <typename K, int XF>
-int enqueue_small(fs_sorter* s, const PlanArgs& a) {
+template <typename K, int XF, bool VALS>
+int launch_small(fs_sorter* s, const PlanArgs& a) {
   const uint32_t n = (uint32_t)a.n;
   uint32_t npad = 2;
   while (npad < n) npad <<= 1;
-  const size_t smem = (size_t)npad * (sizeof(K) + 8);
-  auto kern = k_small_sort<K, XF>;
+  const size_t smem = (size_t)npad * (sizeof(K) + (VALS ? 8 : 0));
+  uint32_t block = npad / 4;
+  if (block < 32) block = 32;
+  if (block > (uint32_t)SMALL_BLOCK_MAX) block = SMALL_BLOCK_MAX;
+  auto kern = k_small_sort<K, XF, VALS>;
   static std::atomic<unsigned> configured{0};  // opt-in shared memory, once per device
   const unsigned bit = 1u << (s->device & 31);
   if (!(configured.load() & bit)) {
     FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)(SMALL_N * (sizeof(K) + 8))));
+                                    (int)(SMALL_N_MAX * (sizeof(K) + (VALS ? 8 : 0)))));
     configured.fetch_or(bit);
   }
-  kern<<<1, SMALL_BLOCK, smem, s->stream>>>(static_cast<const K*>(a.kin), static_cast<K*>(a.kfinal), a.vin, a.vfinal,
-                                            n, npad, a.has_vals, a.write_keys);
+  kern<<<1, block, smem, s->stream>>>(static_cast<const K*>(a.kin), static_cast<K*>(a.kfinal), a.vin, a.vfinal, n,
+                                      npad, a.write_keys);
   s->last_launches = 1;
   FS_CUDA(s, cudaGetLastError());
   return FS_OK;
+}
+
+template <typename K, int XF>
+int enqueue_small(fs_sorter* s, const PlanArgs& a) {
+  return a.has_vals ? launch_small<K, XF, true>(s, a) : launch_small<K, XF, false>(s, a);
 }
 
 int dispatch_small(fs_sorter* s, int dtype, const PlanArgs& a) {
@@ -482,7 +525,8 @@ int dispatch_small(fs_sorter* s, int dtype, const PlanArgs& a) {
 // The sorter's path: size the slices, grow its scratch, enqueue.
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
-  if (a.n <= SMALL_N && !s->no_small) return dispatch_small(s, dtype, a);
+  const uint32_t small_cap = a.has_vals && s->small_max > SMALL_N_PAYLOAD_MAX ? SMALL_N_PAYLOAD_MAX : s->small_max;
+  if (a.n <= small_cap) return dispatch_small(s, dtype, a);
   Exec e = exec_of(s);
   const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);
   int rc = ensure_slice_buffers(s, sl);
@@ -745,7 +789,10 @@ int fs_create(int device, void* stream, fs_sorter** out) {
   *s->host_err = 0;
   e = cudaHostGetDevicePointer((void**)&s->host_err_dev, s->host_err, 0);
   if (e != cudaSuccess) return bail(cuda_fail(s, e, "cudaHostGetDevicePointer"));
-  if (const char* t = getenv("FORGESORT_SMALL_SORT")) s->no_small = atoi(t) == 0;
+  if (const char* t = getenv("FORGESORT_SMALL_SORT")) {  // 0: off; N: up to N keys (at most SMALL_N_MAX)
+    const long long v = atoll(t);
+    s->small_max = v <= 0 ? 0u : (uint32_t)(v < (long long)SMALL_N_MAX ? v : SMALL_N_MAX);
+  }
   if (const char* t = getenv("FORGESORT_WAIT_TIMEOUT_MS")) {
     const long long ms = atoll(t);
     if (ms > 0) s->timeout_ns = (uint64_t)ms * 1000000ull;

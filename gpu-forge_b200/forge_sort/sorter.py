@@ -56,8 +56,15 @@ def dtype_name(dt) -> str:
         raise TypeError(f"not a SortKey type: {dt!r} (u32, i32, f32, u64, i64, f64)") from None
 
 
+_CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream's handle
+
+
 def _stream_handle(stream) -> Optional[int]:
-    """Accept None, an int cudaStream_t, or an object with .cuda_stream."""
+    """Accept None (the sorter's own stream), an int cudaStream_t (0 also
+    means the sorter's own stream, as NULL does in the C ABI), or an object
+    with .cuda_stream such as a torch.cuda.Stream.  torch's default stream
+    reports handle 0; it is the legacy default stream, so it is passed as
+    cudaStreamLegacy and the work really runs on it."""
     if stream is None:
         return None
     if isinstance(stream, int):
@@ -65,7 +72,7 @@ def _stream_handle(stream) -> Optional[int]:
     h = getattr(stream, "cuda_stream", None)
     if h is None:
         raise TypeError("stream must be None, an int cudaStream_t, or have .cuda_stream")
-    return int(h) or None
+    return int(h) or _CUDA_STREAM_LEGACY
 
 
 def _check_array(a, name: str, want: str) -> np.ndarray:

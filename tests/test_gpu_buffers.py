@@ -114,25 +114,31 @@ def test_device_pointer_checks(sorter):
 def test_launch_count(sorter):
     x = orc.gen("u32", 100_000, seed=1)
     sorter.sort_u32(x.copy())
-    # first count, plan, per pass (count, scan, scatter -- pass 0 ranks
-    # unstably, the others stably), finalize
-    assert sorter.last_launch_count() == 3 + 3 * 4
+    # first count, plan, per pass (count -- pass 0 is counted by the first
+    # count --, scan, scatter -- pass 0 ranks unstably, the others stably),
+    # finalize
+    assert sorter.last_launch_count() == 2 + 3 * 4
     y = orc.gen("u64", 100_000, seed=1)
     sorter.sort_u64(y.copy())
-    assert sorter.last_launch_count() == 3 + 3 * 8
+    assert sorter.last_launch_count() == 2 + 3 * 8
     k, v = orc.gen("u32", 10_000, seed=2), np.arange(10_000, dtype=np.uint32)
     sorter.sort_pairs_u32(k, v)  # payload: every pass ranks stably, one scatter each
-    assert sorter.last_launch_count() == 3 + 3 * 4
-    # up to 4096 keys: one single-CTA launch
+    assert sorter.last_launch_count() == 2 + 3 * 4
+    # up to 4096 keys with a payload, 8192 without: one single-CTA launch
     for dt in ("u32", "f64"):
         getattr(sorter, f"argsort_{dt}")(orc.gen("u32" if dt == "u32" else "f64_logu", 4096, seed=3))
         assert sorter.last_launch_count() == 1
+        getattr(sorter, f"sort_{dt}")(orc.gen("u32" if dt == "u32" else "f64_logu", 8192, seed=3))
+        assert sorter.last_launch_count() == 1
+    sorter.argsort_u32(orc.gen("u32", 4097, seed=3))
+    assert sorter.last_launch_count() == 2 + 3 * 4
 
 
 @pytest.mark.parametrize("dt,dist", [("u32", "u32"), ("i32", "i32"), ("f32", "f32_mix"),
                                      ("u64", "u64"), ("i64", "i64"), ("f64", "f64_logu")])
 def test_small_sort_matches_radix_path(sorter, monkeypatch, dt, dist):
-    """The single-CTA path (n <= 4096) and the radix passes
+    """The single-CTA path (n <= 8192 keys alone, <= 4096 with a payload;
+    6000 and 8192 below cover both sides) and the radix passes
     (FORGESORT_SMALL_SORT=0) give the same keys, the same stable argsort and
     the same pairs, on inputs full of ties, and sort device memory in place."""
     import torch
@@ -140,7 +146,7 @@ def test_small_sort_matches_radix_path(sorter, monkeypatch, dt, dist):
     monkeypatch.setenv("FORGESORT_SMALL_SORT", "0")
     radix = GpuSorter()
     rng = np.random.default_rng(17)
-    for n in (1, 2, 3, 255, 1000, 2049, 4096):
+    for n in (1, 2, 3, 255, 1000, 2049, 4096, 6000, 8192):
         x = orc.gen(dist, n, seed=n)
         x[rng.integers(0, n, n // 2)] = x[0]  # ties
         for srt in (sorter, radix):
