@@ -93,3 +93,22 @@ def test_null_arguments_are_rejected_without_a_device():
     assert L.fs_sort_keys(None, 0, None, 10, 1) == _lib.E_INVALID
     assert L.fs_destroy(None) == _lib.OK
     assert L.fs_scratch_bytes(None) == 0
+
+
+def test_stream_handles():
+    """None and 0 select the sorter's own stream (NULL in the C ABI); a
+    stream object reporting handle 0 (torch's default stream) is the legacy
+    default stream, cudaStreamLegacy = 1; other handles pass through."""
+    from forge_sort.sorter import _stream_handle
+
+    class S:
+        def __init__(self, h):
+            self.cuda_stream = h
+
+    assert _stream_handle(None) is None
+    assert _stream_handle(0) is None
+    assert _stream_handle(0x1234) == 0x1234
+    assert _stream_handle(S(0)) == 1
+    assert _stream_handle(S(0x5678)) == 0x5678
+    with pytest.raises(TypeError):
+        _stream_handle(object())
