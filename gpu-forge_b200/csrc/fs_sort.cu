@@ -300,17 +300,20 @@ template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int scatter_occupancy(const Exec& e) {
   using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS>;
   auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D>;
-  static int configured_mask = 0;  // bit per device (the attribute is per context)
-  static int bps = 0;
-  if (!(configured_mask & (1 << (e.device & 31)))) {
+  // sorters on several host threads may get here at once: the attribute
+  // call is idempotent, the cache words are atomic
+  static std::atomic<unsigned> configured_mask{0};  // bit per device (the attribute is per context)
+  static std::atomic<int> bps{0};
+  const unsigned bit = 1u << (e.device & 31);
+  if (!(configured_mask.load() & bit)) {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES);
     if (err != cudaSuccess) return -cuda_fail(e.s, err, "cudaFuncSetAttribute");
     const int b = blocks_per_sm(e.s, kern, C::BLOCK, Ly::BYTES);
     if (b < 0) return b;
-    bps = b;
-    configured_mask |= 1 << (e.device & 31);
+    bps.store(b);
+    configured_mask.fetch_or(bit);
   }
-  return bps;
+  return bps.load();
 }
 
 // Kernels of one sort follow each other on the sorter's stream.  Launched
