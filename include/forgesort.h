@@ -67,6 +67,16 @@ typedef struct fs_sorter fs_sorter;
  * NULL to create a private non-blocking stream (the analogue of new()).
  * Replaces src/lib.rs:596-686. */
 int fs_create(int device, void* stream, fs_sorter** out);
+/* Environment read by fs_create (all optional):
+ *   FORGESORT_WAIT_TIMEOUT_MS  bound on every device-side wait (default 2000);
+ *                              a wait that runs out fails the call with
+ *                              FS_E_TIMEOUT instead of hanging
+ *   FORGESORT_SMALL_SORT       largest n sorted by one CTA in shared memory
+ *                              (default and maximum 8192 keys alone, 4096 with
+ *                              a payload; 0: always the radix passes)
+ * and once per process:
+ *   FORGESORT_CHAIN_LAUNCH     0: launch a sort's kernels without programmatic
+ *                              stream serialization (default: chained) */
 int fs_destroy(fs_sorter* s);
 
 /* Text of the last failure on `s` (never NULL; "" when none).  With s == NULL,
