@@ -117,7 +117,9 @@ class Buffer:
 class ForgeContext:
     """One CUDA device and one stream, shared by the sorters and gathers made
     with_context(ctx.device(), ctx.queue()).  Raises forge_sort's
-    DeviceNotFound when there is no CUDA device (the reference panics)."""
+    DeviceNotFound when there is no CUDA device (the reference panics).
+    close() destroys the stream and frees the buffers from alloc_buffer:
+    sorters and gathers bound to queue() must not be used after it."""
 
     def __init__(self, device: int = 0):
         L = _lib.load()
@@ -267,7 +269,8 @@ class Pipeline:
         raise NotImplementedError("filter stages need forge-filter, which this build does not include")
 
     def sort(self, gpu_sorter: GpuSorter, buf: SortBuffer) -> None:
-        """Enqueue an in-place sort of a SortBuffer<u32> (pipeline.rs:98-105)."""
+        """Enqueue an in-place sort of a SortBuffer<u32> (pipeline.rs:98-105).
+        The sorter is rebound to the context's stream (encode_sort)."""
         try:
             gpu_sorter.encode_sort(self._ctx.queue(), buf)
         except SortError as e:
