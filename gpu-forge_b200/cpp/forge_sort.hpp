@@ -345,6 +345,18 @@ class MultiGpuSorter {
     return out_n;
   }
 
+  // The per-type names of the boundary.
+  std::vector<uint64_t> sort_u32(const std::vector<uint32_t*>& shards, const std::vector<uint64_t>& shard_n,
+                                 const std::vector<uint32_t*>& out, const std::vector<uint64_t>& out_cap,
+                                 std::vector<uint64_t>* needed = nullptr) {
+    return sort<uint32_t>(shards, shard_n, out, out_cap, needed);
+  }
+  std::vector<uint64_t> sort_u64(const std::vector<uint64_t*>& shards, const std::vector<uint64_t>& shard_n,
+                                 const std::vector<uint64_t*>& out, const std::vector<uint64_t>& out_cap,
+                                 std::vector<uint64_t>* needed = nullptr) {
+    return sort<uint64_t>(shards, shard_n, out, out_cap, needed);
+  }
+
   // The stable pairs form: vals[i] (device, shard_n[i] u32) travel with the
   // keys into out_vals[i] (room for out_cap[i]); with `vals` empty, every
   // key's global position is sent instead (an argsort).  Same sizing rule.

@@ -28,6 +28,10 @@ class MultiGpuSorter:
         self._h = h
         self.devices = [int(d) for d in devices]
 
+    @classmethod
+    def new(cls, devices: Sequence[int]) -> "MultiGpuSorter":
+        return cls(devices)
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             _lib.load().fs_mg_destroy(self._h)
@@ -108,3 +112,10 @@ class MultiGpuSorter:
         name = dtype_name(dt)
         self._check(name, shards)
         return self._run(name, shards, None, True, headroom)
+
+    # the per-type names of the boundary (MultiGpuSorter::sort_u32 / sort_u64)
+    def sort_u32(self, shards: List, headroom: float = 1.125) -> List:
+        return self.sort("u32", shards, headroom)
+
+    def sort_u64(self, shards: List, headroom: float = 1.125) -> List:
+        return self.sort("u64", shards, headroom)

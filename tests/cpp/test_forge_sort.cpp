@@ -158,6 +158,9 @@ CPU_TEST(test_no_device_multi_and_context) {
     std::vector<uint32_t*> k(2, nullptr), vo(2, nullptr);
     mg.sort_pairs<uint32_t>(k, {}, z, k, vo, z);
     mg.sort<uint32_t>(k, z, k, z);
+    mg.sort_u32(k, z, k, z);
+    std::vector<uint64_t*> k64(2, nullptr);
+    mg.sort_u64(k64, z, k64, z);
     CHECK(false && "a multi-GPU sorter was created without a device");
   } catch (const SortError& e) {
     CHECK(e.kind() == SortError::Kind::DeviceNotFound);
