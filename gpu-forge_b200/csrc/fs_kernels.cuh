@@ -13,6 +13,9 @@
 //                    payload carried alongside; next tile bulk-prefetched
 // then:
 //   k_finalize       copy-back / iota when the plan needs it; error hand-off
+// (2 + 3P launches in a row on one stream, each after the first chained to
+// its predecessor: chain_wait below.)  Up to a few thousand keys,
+// k_small_sort does the whole sort in one CTA instead.
 //
 // The array is cut into contiguous slices (12 per SM, whole tiles each) that
 // the scatter CTAs take in turn; no CTA ever waits on another: the offsets a
