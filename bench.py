@@ -216,7 +216,12 @@ def run_reference(args):
         "metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt_s * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dt,
-        "data": "synthetic", "config": config(args, world),
+        "data": "synthetic",
+        # same workload and metric as our arm; each step sorts a bounded
+        # 2^26-key sample of it (the full 2^32 keys would take minutes a step)
+        "config": {**config(args, world), "keys_per_step": sample_n,
+                   "parallelism": f"CPU, {threads} host threads (__gnu_parallel::sort)",
+                   "sample": f"first 2^26 keys of the 2^{args.log2n}-key input, sorted each step"},
         "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"each step sorts 2^26 keys of the same stream with __gnu_parallel::sort "
                                    "(C++ restatement of the reference's CPU path; Rust toolchain absent)"},

@@ -91,6 +91,7 @@ enum PassFlags : uint32_t {
   PD_WRITE_KEYS = 1u << 4,  // write keys (argsort's last pass does not)
   PD_FIRST = 1u << 5,       // first executed pass (reads the caller's keys)
   PD_UNSTABLE = 1u << 6,    // keys-only first pass: order among equal digits is free
+  PD_TEST_WITHHOLD = 1u << 7,  // failure-path test: CTA 0 never issues its first bulk copy
 };
 
 struct PassDesc {
@@ -164,6 +165,8 @@ struct PlanArgs {
   int trivial_from_bits;           // 1: a pass is trivial when kor/kandn show its
                                    // digit never varies; 0: when hist[0] has one
                                    // digit holding all n keys (single-pass plans)
+  int test_withhold;               // failure-path test (fs_test_inject): mark the
+                                   // first executed pass PD_TEST_WITHHOLD
 };
 
 }  // namespace fs

@@ -427,6 +427,7 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
       if (i == 1) f |= PD_XF_IN | PD_FIRST;
       if (i == 1 && p == 0 && !a.has_vals && a.unstable_first) f |= PD_UNSTABLE;
       if (i == 1 && a.has_vals && a.vin == nullptr) f |= PD_SYNTH_IDX;
+      if (i == 1 && a.test_withhold) f |= PD_TEST_WITHHOLD;
       if (i == m) f |= PD_XF_OUT;
       if (a.write_keys || i < m) f |= PD_WRITE_KEYS;
       pd.kin = kprev;
@@ -911,8 +912,15 @@ __global__ void __launch_bounds__(BLOCK, MINB)
   // thread 0: start the copy of the tile at key `t0` of a slice ending at
   // `hi` into slot s (full tiles only)
   uint32_t armed = 0;  // thread 0: bit s = copy into slot s in flight
+  // failure-path test: CTA 0 leaves its first copy un-issued (barrier never
+  // armed, nothing in flight), so its bounded wait runs out
+  bool withhold = (pd.flags & PD_TEST_WITHHOLD) != 0 && blockIdx.x == 0;
   auto issue = [&](uint64_t t0, uint64_t hi, int s) {
     if (bulk_ok && t0 + Ly::TILE <= hi) {
+      if (withhold) {
+        withhold = false;
+        return;
+      }
       unsigned char* dst = dsm + (size_t)s * Ly::SLOT;
       fence_proxy_async_smem();  // earlier generic reads of the slot precede the async write
       mbar_arrive_expect_tx(&s_bar[s], (uint32_t)(Ly::KEYS + (copy_vals ? Ly::VALB : 0)));

@@ -5,6 +5,7 @@
 //   first count -> plan -> P x (count, slice scan, scatter) -> finalize
 // on that stream (P = key bytes), with no host round trip in between.
 #include "forgesort.h"
+#include "forgesort_bench.h"
 #include "fs_kernels.cuh"
 
 #include <cstdarg>
@@ -68,6 +69,8 @@ struct fs_sorter {
   static constexpr int MAX_TIMED = 24;
   cudaEvent_t ev[2 * MAX_TIMED] = {};
   int ev_used = 0;
+  int test_withhold = 0;    // fs_test_inject(FS_TEST_WITHHOLD_COPY): next radix sort
+  int test_fail_alloc = 0;  // fs_test_inject(FS_TEST_FAIL_ALLOC): countdown to a failed growth
   std::unordered_map<void*, size_t> allocs;  // fs_alloc'd pointers -> bytes
   std::unordered_map<void*, int> managed;
   std::string err;
@@ -170,6 +173,18 @@ constexpr int HIST_BLOCK = 512;  // histogram / count kernels: more loads in fli
 
 int key_bytes_of(int dtype) { return dtype >= FS_U64 ? 8 : 4; }
 
+// Device ordinals the per-device caches below cover (fs_create refuses more).
+constexpr int MAX_DEVICES = 64;
+
+// Bound on every device-side wait: FORGESORT_WAIT_TIMEOUT_MS, default 2 s.
+uint64_t wait_timeout_ns_env() {
+  if (const char* t = getenv("FORGESORT_WAIT_TIMEOUT_MS")) {
+    const long long ms = atoll(t);
+    if (ms > 0) return (uint64_t)ms * 1000000ull;
+  }
+  return 2000000000ull;
+}
+
 int grow(fs_sorter* s, void** p, size_t* cap, size_t need, bool zero) {
   if (*cap >= need) return FS_OK;
   if (*p) {
@@ -178,6 +193,9 @@ int grow(fs_sorter* s, void** p, size_t* cap, size_t need, bool zero) {
     *p = nullptr;
     *cap = 0;
   }
+  if (s && s->test_fail_alloc > 0 && --s->test_fail_alloc == 0)
+    return fail(s, FS_E_OOM, "device allocation of %zu bytes failed: out of memory (injected by fs_test_inject)",
+                need);
   cudaError_t e = cudaMalloc(p, need);
   if (e != cudaSuccess) {
     *p = nullptr;
@@ -302,16 +320,17 @@ int scatter_occupancy(const Exec& e) {
   auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D>;
   // sorters on several host threads may get here at once: the attribute
   // call is idempotent, the cache words are atomic
-  static std::atomic<unsigned> configured_mask{0};  // bit per device (the attribute is per context)
+  static std::atomic<bool> configured[MAX_DEVICES];  // per device (the attribute is per context)
   static std::atomic<int> bps{0};
-  const unsigned bit = 1u << (e.device & 31);
-  if (!(configured_mask.load() & bit)) {
+  if (e.device < 0 || e.device >= MAX_DEVICES)
+    return -fail(e.s, FS_E_INVALID, "device %d outside [0, %d)", e.device, MAX_DEVICES);
+  if (!configured[e.device].load()) {
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES);
     if (err != cudaSuccess) return -cuda_fail(e.s, err, "cudaFuncSetAttribute");
     const int b = blocks_per_sm(e.s, kern, C::BLOCK, Ly::BYTES);
     if (b < 0) return b;
     bps.store(b);
-    configured_mask.fetch_or(bit);
+    configured[e.device].store(true);
   }
   return bps.load();
 }
@@ -494,12 +513,13 @@ int launch_small(fs_sorter* s, const PlanArgs& a) {
   if (block < 32) block = 32;
   if (block > (uint32_t)SMALL_BLOCK_MAX) block = SMALL_BLOCK_MAX;
   auto kern = k_small_sort<K, XF, VALS>;
-  static std::atomic<unsigned> configured{0};  // opt-in shared memory, once per device
-  const unsigned bit = 1u << (s->device & 31);
-  if (!(configured.load() & bit)) {
+  static std::atomic<bool> configured[MAX_DEVICES];  // opt-in shared memory, once per device
+  if (s->device < 0 || s->device >= MAX_DEVICES)
+    return fail(s, FS_E_INVALID, "device %d outside [0, %d)", s->device, MAX_DEVICES);
+  if (!configured[s->device].load()) {
     FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)(SMALL_N_MAX * (sizeof(K) + (VALS ? 8 : 0)))));
-    configured.fetch_or(bit);
+    configured[s->device].store(true);
   }
   kern<<<1, block, smem, s->stream>>>(static_cast<const K*>(a.kin), static_cast<K*>(a.kfinal), a.vin, a.vfinal, n,
                                       npad, a.write_keys);
@@ -536,7 +556,10 @@ int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   if (rc) return rc;
   e.counts = static_cast<uint32_t*>(s->counts);
   e.offsets = static_cast<uint32_t*>(s->offsets);
-  return dispatch_enqueue(e, dtype, a, sl, &s->last_launches);
+  PlanArgs pa = a;
+  pa.test_withhold = s->test_withhold;
+  s->test_withhold = 0;  // one-shot
+  return dispatch_enqueue(e, dtype, pa, sl, &s->last_launches);
 }
 
 // ---- sample-sort partition --------------------------------------------------
@@ -728,11 +751,11 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_BYTES];
 
 // Device address of g_noalloc_scratch per device.  In host code the array's
 // name is only a host-side stand-in: kernels must be given this address.
-unsigned char* g_na_base[64] = {};
+unsigned char* g_na_base[MAX_DEVICES] = {};
 std::mutex g_na_mu;
 
 int noalloc_base(int device, unsigned char** out) {
-  if (device < 0 || device >= 64) return fail(nullptr, FS_E_INVALID, "device %d out of range", device);
+  if (device < 0 || device >= MAX_DEVICES) return fail(nullptr, FS_E_INVALID, "device %d out of range", device);
   std::lock_guard<std::mutex> lk(g_na_mu);
   if (!g_na_base[device]) {
     void* p = nullptr;
@@ -765,6 +788,7 @@ int fs_create(int device, void* stream, fs_sorter** out) {
     return fail(nullptr, FS_E_DEVICE_NOT_FOUND, "no CUDA device");
   }
   if (device < 0 || device >= count) return fail(nullptr, FS_E_DEVICE_NOT_FOUND, "no CUDA device %d", device);
+  if (device >= MAX_DEVICES) return fail(nullptr, FS_E_INVALID, "device %d outside [0, %d)", device, MAX_DEVICES);
   fs_sorter* s = new fs_sorter();
   s->device = device;
   auto bail = [&](int rc) {
@@ -796,10 +820,7 @@ int fs_create(int device, void* stream, fs_sorter** out) {
     const long long v = atoll(t);
     s->small_max = v <= 0 ? 0u : (uint32_t)(v < (long long)SMALL_N_MAX ? v : SMALL_N_MAX);
   }
-  if (const char* t = getenv("FORGESORT_WAIT_TIMEOUT_MS")) {
-    const long long ms = atoll(t);
-    if (ms > 0) s->timeout_ns = (uint64_t)ms * 1000000ull;
-  }
+  s->timeout_ns = wait_timeout_ns_env();
   *out = s;
   return FS_OK;
 }
@@ -1190,7 +1211,7 @@ int fs_last_kernel_times(fs_sorter* s, float* ms, int cap) {
 int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream) {
   if (dtype < FS_U32 || dtype > FS_F64) return fail(nullptr, FS_E_INVALID, "unknown dtype %d", dtype);
   const int kb = key_bytes_of(dtype);
-  if (n * (uint64_t)kb > NA_MAX_KEY_BYTES)
+  if (n > NA_MAX_KEY_BYTES / (uint64_t)kb)  // (n * kb could wrap for huge n)
     return fail(nullptr, FS_E_INVALID,
                 "n = %llu keys exceeds the allocation-free limit of %llu bytes of keys (%llu keys of %d bytes)",
                 (unsigned long long)n, (unsigned long long)NA_MAX_KEY_BYTES,
@@ -1214,7 +1235,7 @@ int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream) {
   e.stream = static_cast<cudaStream_t>(stream);
   ce = cudaDeviceGetAttribute(&e.sm_count, cudaDevAttrMultiProcessorCount, device);
   if (ce != cudaSuccess) return cuda_fail(nullptr, ce, "cudaDeviceGetAttribute");
-  e.timeout_ns = 2000000000ull;
+  e.timeout_ns = wait_timeout_ns_env();
   e.ctl = reinterpret_cast<SortCtl*>(base + NA_OFF_CTL);
   e.err_out = reinterpret_cast<int*>(base + NA_OFF_ERR);
   e.counts = reinterpret_cast<uint32_t*>(base + NA_OFF_COUNTS);
@@ -1524,6 +1545,33 @@ int fs_ipc_close(fs_sorter* s, void* ptr) {
   if (rc) return rc;
   FS_CUDA(s, cudaIpcCloseMemHandle(ptr));
   return FS_OK;
+}
+
+int fs_set_wait_timeout_ms(fs_sorter* s, uint64_t ms) {
+  if (!s) return FS_E_INVALID;
+  if (ms == 0 || ms > 3600000ull) return fail(s, FS_E_INVALID, "wait timeout %llu ms outside [1, 3600000]",
+                                             (unsigned long long)ms);
+  s->timeout_ns = ms * 1000000ull;
+  return FS_OK;
+}
+
+int fs_test_inject(fs_sorter* s, int kind, int arg) {
+  if (!s) return FS_E_INVALID;
+  switch (kind) {
+    case 0:
+      s->test_withhold = 0;
+      s->test_fail_alloc = 0;
+      return FS_OK;
+    case FS_TEST_WITHHOLD_COPY:
+      s->test_withhold = 1;
+      return FS_OK;
+    case FS_TEST_FAIL_ALLOC:
+      if (arg < 1) return fail(s, FS_E_INVALID, "FS_TEST_FAIL_ALLOC needs arg >= 1, got %d", arg);
+      s->test_fail_alloc = arg;
+      return FS_OK;
+    default:
+      return fail(s, FS_E_INVALID, "unknown injection kind %d", kind);
+  }
 }
 
 uint64_t fs_scratch_bytes(const fs_sorter* s) {

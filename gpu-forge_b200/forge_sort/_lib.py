@@ -76,7 +76,10 @@ SIGNATURES = {
 # include/forgesort_bench.h
 BENCH_SIGNATURES = {
     "fs_generate": (_i32, [_i32, _u64, _u64, _u64, _vp, _vp]),
+    "fs_set_wait_timeout_ms": (_i32, [_vp, _u64]),
+    "fs_test_inject": (_i32, [_vp, _i32, _i32]),
 }
+TEST_WITHHOLD_COPY, TEST_FAIL_ALLOC = 1, 2
 GEN_U32, GEN_U64, GEN_SKEW_U32 = 0, 1, 2
 
 _lib = None

@@ -40,11 +40,24 @@ from typing import List, Optional, Tuple
 
 import numpy as np
 
+from .errors import GpuExecution
 from .sorter import GpuSorter, dtype_name
 
 _BITS = {"u32": np.uint32, "i32": np.uint32, "f32": np.uint32,
          "u64": np.uint64, "i64": np.uint64, "f64": np.uint64}
 _WIDTH = {"u32": 32, "i32": 32, "f32": 32, "u64": 64, "i64": 64, "f64": 64}
+
+
+def collective(dist, what: str, fn, *args, **kw):
+    """Run one torch.distributed collective; a failure there -- a peer rank
+    that raised, stalled past the process group's timeout, or exited --
+    becomes SortError::GpuExecution naming the step, so every surviving rank
+    fails with an error instead of hanging or leaking a backend exception."""
+    try:
+        return fn(*args, **kw)
+    except RuntimeError as e:  # DistBackendError, gloo / NCCL timeouts and closed connections
+        rank = dist.get_rank() if dist.is_initialized() else -1
+        raise GpuExecution(f"sample sort: collective '{what}' failed on rank {rank}: {e}") from e
 
 
 def ordered_bits(raw: np.ndarray, dt: str) -> np.ndarray:
@@ -147,7 +160,7 @@ class CudaOps:
         self._cap = cap
         mine = torch.tensor(list(self.s.ipc_export(self._inbox)), dtype=torch.uint8, device=dev)
         handles = [torch.empty_like(mine) for _ in range(G)]
-        dist.all_gather(handles, mine, group=group)
+        collective(dist, "inbox handles", dist.all_gather, handles, mine, group=group)
         self._peers = [self._inbox if b == r else self.s.ipc_open(bytes(handles[b].cpu().tolist()))
                        for b in range(G)]
 
@@ -161,7 +174,7 @@ class CudaOps:
             if b != r:
                 self.s.ipc_close(p)
         self._peers = []
-        dist.barrier(group=group)  # no rank frees an inbox a peer still maps
+        collective(dist, "inbox release", dist.barrier, group=group)  # no rank frees an inbox a peer still maps
         self.s.free_device(self._inbox)
         self._inbox = 0
         self._cap = 0
@@ -181,7 +194,7 @@ class CudaOps:
         send = self.s.partition_count(dt, keys.data_ptr(), m, gpos_base, skp, sgp, G - 1)
         cnt = torch.tensor(send, dtype=torch.int64, device=dev)
         rows = [torch.empty_like(cnt) for _ in range(G)]
-        dist.all_gather(rows, cnt, group=group)
+        collective(dist, "bucket counts", dist.all_gather, rows, cnt, group=group)
         M = torch.stack(rows).cpu().numpy()  # M[s, b]: keys rank s sends to rank b
         most = int(M.sum(axis=0).max())
         # inbox: [keys | values], the values region 256-byte aligned
@@ -198,7 +211,7 @@ class CudaOps:
         # every rank enters this collective after its dispatch finished, so
         # once it completes every inbox is full
         done = torch.zeros(1, dtype=torch.int32, device=dev)
-        dist.all_reduce(done, group=group)
+        collective(dist, "dispatch done", dist.all_reduce, done, group=group)
         torch.cuda.current_stream(dev).synchronize()
         del sk, sg
         recv = [int(x) for x in M[:, r]]
@@ -308,7 +321,8 @@ class SampleSorter:
         dev = keys.device
         if gpos_base is None:
             sizes = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(G)]
-            dist.all_gather(sizes, torch.tensor([m], dtype=torch.int64, device=dev), group=self.group)
+            collective(dist, "shard sizes", dist.all_gather, sizes, torch.tensor([m], dtype=torch.int64, device=dev),
+                       group=self.group)
             gpos_base = int(sum(int(t.item()) for t in sizes[:r]))
         if G == 1:
             self.last = SampleSortStats([m], [m])
@@ -342,7 +356,7 @@ class SampleSorter:
             raw64 = torch.zeros(S, dtype=torch.int64, device=dev)
         mine = torch.stack([skey, gpos, raw64], dim=1).contiguous()
         gathered = [torch.empty_like(mine) for _ in range(G)]
-        dist.all_gather(gathered, mine, group=self.group)
+        collective(dist, "samples", dist.all_gather, gathered, mine, group=self.group)
         allv = torch.cat(gathered)
         order = torch.sort(allv[:, 0], stable=True).indices
         sel = allv[order[torch.arange(1, G, device=allv.device) * S]].cpu().numpy()
@@ -369,16 +383,17 @@ class SampleSorter:
         # 3. exchange sizes, then the buckets
         sc = torch.tensor(send, dtype=torch.int64, device=dev)
         rc = torch.empty(G, dtype=torch.int64, device=dev)
-        dist.all_to_all_single(rc, sc, group=self.group)
+        collective(dist, "bucket sizes", dist.all_to_all_single, rc, sc, group=self.group)
         recv = [int(x) for x in rc.cpu().tolist()]
         inbox = torch.empty(sum(recv), dtype=keys.dtype, device=dev)
-        dist.all_to_all_single(inbox, part, output_split_sizes=recv, input_split_sizes=send, group=self.group)
+        collective(dist, "key exchange", dist.all_to_all_single, inbox, part, output_split_sizes=recv,
+                   input_split_sizes=send, group=self.group)
         del part
         vinbox = None
         if payload:
             vinbox = torch.empty(sum(recv), dtype=torch.int32, device=dev)
-            dist.all_to_all_single(vinbox, pvals, output_split_sizes=recv, input_split_sizes=send,
-                                   group=self.group)
+            collective(dist, "value exchange", dist.all_to_all_single, vinbox, pvals, output_split_sizes=recv,
+                       input_split_sizes=send, group=self.group)
             del pvals
 
         # 4. local sort of this rank's bucket

@@ -252,6 +252,14 @@ class GpuSorter:
     def last_launch_count(self) -> int:
         return int(_lib.load().fs_last_launch_count(self._h))
 
+    def set_wait_timeout_ms(self, ms: int) -> None:
+        """Bound on every device-side wait of this sorter (default 2000 ms)."""
+        self._call(_lib.load().fs_set_wait_timeout_ms(self._h, int(ms)))
+
+    def _test_inject(self, kind: int, arg: int = 0) -> None:
+        """Failure-path test hook (fs_test_inject): arm one injected failure."""
+        self._call(_lib.load().fs_test_inject(self._h, int(kind), int(arg)))
+
     # -- zero-copy buffers (src/lib.rs:694-738, 1000-1117, 2301-2590) -----------
     def alloc_sort_buffer(self, dt, capacity: int) -> SortBuffer:
         name = dtype_name(dt)

@@ -337,11 +337,17 @@ int fs_mg_sort_pairs(fs_mg* mg, int dtype, void* const* shards,
  * FS_E_INVALID with the limit in fs_last_error(NULL).  Every GPU that loads
  * the library holds that array (about 4.6 MB) until the process exits.
  *
- * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture.  All
- * calls share the one array: calls that overlap on the GPU (other streams or
- * host threads, same device) race and corrupt each other's results, so
- * serialise them.  Errors: text in fs_last_error(NULL). */
+ * The call is synchronous: it returns after the sort has finished on
+ * `stream` (it waits for the stream to read back the device error word).
+ * Device waits are bounded by FORGESORT_WAIT_TIMEOUT_MS (default 2 s), as
+ * for sorters.  The first call on a device looks up the array's device
+ * address (with that device current) and caches it for the process; make
+ * that first call before any stream capture, and do not keep using the
+ * library across a cudaDeviceReset of that device.  All calls share the one
+ * array, which keeps the previous call's contents (each call clears what
+ * must start at zero): calls that overlap on the GPU (other streams or host
+ * threads, same device) race and corrupt each other's results, so serialise
+ * them.  Errors: text in fs_last_error(NULL). */
 int fs_sort_keys_noalloc(int dtype, void* keys, uint64_t n, void* stream);
 
 /* ---- introspection ------------------------------------------------------- */

@@ -19,6 +19,8 @@
 extern "C" {
 #endif
 
+typedef struct fs_sorter fs_sorter; /* declared in forgesort.h */
+
 typedef enum fs_gen_dist {
   FS_GEN_U32 = 0,      /* high 32 bits of each state                         */
   FS_GEN_U64 = 1,      /* the full state                                     */
@@ -31,6 +33,35 @@ typedef enum fs_gen_dist {
  * legacy default stream) of the current device.  Returns an fs_status. */
 int fs_generate(int dist, uint64_t seed, uint64_t start, uint64_t n, void* out,
                 void* stream);
+
+/* ---- failure-path hooks (tests) -------------------------------------------
+ * The reference maps a failed command buffer to SortError::GpuExecution
+ * (forge-sort src/lib.rs:396-406) and panics when a buffer allocation fails
+ * (src/metal_helpers.rs:194-202).  These hooks make the corresponding paths
+ * of this library run without faulting or hanging a GPU, so tests can check
+ * that the call fails with the right status and that the sorter works again
+ * afterwards. */
+
+/* Bound on every device-side wait of this sorter (the mbarrier waits of the
+ * scatter's bulk copies), in milliseconds (> 0).  fs_create takes it from
+ * FORGESORT_WAIT_TIMEOUT_MS (default 2000). */
+int fs_set_wait_timeout_ms(fs_sorter* s, uint64_t ms);
+
+typedef enum fs_test_inject_kind {
+  /* The next radix-path sort (n above the single-CTA limit, 16-byte aligned
+   * keys) leaves the first bulk copy of CTA 0's first scatter tile un-issued:
+   * that CTA's bounded wait runs out, the kernels stop early and the call
+   * returns FS_E_TIMEOUT.  Nothing is left in flight.  One-shot. */
+  FS_TEST_WITHHOLD_COPY = 1,
+  /* The arg-th next growth of the sorter's device scratch (arg >= 1) fails
+   * as if cudaMalloc had run out of memory: the call returns FS_E_OOM and
+   * the scratch slot is left empty (the next call grows it again). */
+  FS_TEST_FAIL_ALLOC = 2
+} fs_test_inject_kind;
+
+/* Arm one injected failure (kind above) on sorter `s`; arg as the kind says.
+ * kind 0 disarms both. */
+int fs_test_inject(fs_sorter* s, int kind, int arg);
 
 #ifdef __cplusplus
 }

@@ -149,6 +149,36 @@ void argsort_t(const K* k, uint32_t* idx, uint64_t n, int mode) {
   std::stable_sort(idx, idx + n, [&](uint32_t a, uint32_t b) { return o[a] < o[b]; });
 }
 
+// Parallel stable argsort: sorting (ordered key, index) tuples with the
+// index as the tie-break gives exactly the permutation of a stable
+// sort_by_key, in any sort algorithm, so __gnu_parallel::sort may be used.
+// 32-bit keys pack the tuple into one u64.  Lets full-size (2^24..2^28)
+// argsort / pairs cases be checked bit-exactly in seconds.
+template <typename K>
+void par_argsort_t(const K* k, uint32_t* idx, uint64_t n, int mode, int threads) {
+  if (threads > 0) omp_set_num_threads(threads);
+  if constexpr (sizeof(K) == 4) {
+    std::vector<uint64_t> t(n);
+#pragma omp parallel for schedule(static)
+    for (uint64_t i = 0; i < n; ++i) t[i] = ((uint64_t)to_ordered(k[i], mode) << 32) | i;
+    __gnu_parallel::sort(t.begin(), t.end());
+#pragma omp parallel for schedule(static)
+    for (uint64_t i = 0; i < n; ++i) idx[i] = (uint32_t)t[i];
+  } else {
+    struct KI {
+      uint64_t k;
+      uint32_t i;
+      bool operator<(const KI& o) const { return k < o.k || (k == o.k && i < o.i); }
+    };
+    std::vector<KI> t(n);
+#pragma omp parallel for schedule(static)
+    for (uint64_t i = 0; i < n; ++i) t[i] = KI{to_ordered(k[i], mode), (uint32_t)i};
+    __gnu_parallel::sort(t.begin(), t.end());
+#pragma omp parallel for schedule(static)
+    for (uint64_t i = 0; i < n; ++i) idx[i] = t[i].i;
+  }
+}
+
 // LSD radix sort: P passes of 8-bit counting sort on the ordered image,
 // payload carried.  Stable by construction.
 template <typename K>
@@ -322,6 +352,36 @@ void orc_sort_pairs(int dtype, void* keys, uint32_t* vals, uint64_t n) {
   } else {
     uint32_t* k = static_cast<uint32_t*>(keys);
     std::vector<uint32_t> kk(k, k + n);
+    for (uint64_t i = 0; i < n; ++i) {
+      k[i] = kk[idx[i]];
+      vals[i] = v[idx[i]];
+    }
+  }
+}
+
+void orc_par_argsort(int dtype, const void* keys, uint32_t* idx, uint64_t n, int threads) {
+  if (wide(dtype))
+    par_argsort_t(static_cast<const uint64_t*>(keys), idx, n, mode_of(dtype), threads);
+  else
+    par_argsort_t(static_cast<const uint32_t*>(keys), idx, n, mode_of(dtype), threads);
+}
+
+// Stable pairs sort through the parallel argsort, then a parallel gather.
+void orc_par_sort_pairs(int dtype, void* keys, uint32_t* vals, uint64_t n, int threads) {
+  std::vector<uint32_t> idx(n), v(vals, vals + n);
+  orc_par_argsort(dtype, keys, idx.data(), n, threads);
+  if (wide(dtype)) {
+    uint64_t* k = static_cast<uint64_t*>(keys);
+    std::vector<uint64_t> kk(k, k + n);
+#pragma omp parallel for schedule(static)
+    for (uint64_t i = 0; i < n; ++i) {
+      k[i] = kk[idx[i]];
+      vals[i] = v[idx[i]];
+    }
+  } else {
+    uint32_t* k = static_cast<uint32_t*>(keys);
+    std::vector<uint32_t> kk(k, k + n);
+#pragma omp parallel for schedule(static)
     for (uint64_t i = 0; i < n; ++i) {
       k[i] = kk[idx[i]];
       vals[i] = v[idx[i]];

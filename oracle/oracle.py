@@ -61,6 +61,8 @@ def lib():
         L.orc_argsort.argtypes = [i32, vp, vp, u64]
         L.orc_sort_pairs.argtypes = [i32, vp, vp, u64]
         L.orc_radix_sort.argtypes = [i32, vp, vp, u64]
+        L.orc_par_argsort.argtypes = [i32, vp, vp, u64, i32]
+        L.orc_par_sort_pairs.argtypes = [i32, vp, vp, u64, i32]
         L.orc_max_threads.restype = i32
         for f, t in (("orc_to_ordered32", ctypes.c_uint32), ("orc_from_ordered32", ctypes.c_uint32),
                      ("orc_to_ordered64", u64), ("orc_from_ordered64", u64)):
@@ -152,6 +154,23 @@ def sort_pairs(keys: np.ndarray, vals: np.ndarray, dt: str):
     k = np.array(keys, dtype=NP_DTYPE[dt], copy=True, order="C")
     v = np.array(vals, dtype=np.uint32, copy=True, order="C")
     lib().orc_sort_pairs(DTYPES[dt], _ptr(k), _ptr(v), k.size)
+    return k, v
+
+
+def par_argsort(a: np.ndarray, dt: str, threads: int = 0) -> np.ndarray:
+    """argsort() on every host thread: sorts (ordered key, index) tuples, so
+    the result is the same stable permutation."""
+    a = np.ascontiguousarray(a, dtype=NP_DTYPE[dt])
+    idx = np.empty(a.size, np.uint32)
+    lib().orc_par_argsort(DTYPES[dt], _ptr(a), _ptr(idx), a.size, threads)
+    return idx
+
+
+def par_sort_pairs(keys: np.ndarray, vals: np.ndarray, dt: str, threads: int = 0):
+    """sort_pairs() on every host thread (same stable result)."""
+    k = np.array(keys, dtype=NP_DTYPE[dt], copy=True, order="C")
+    v = np.array(vals, dtype=np.uint32, copy=True, order="C")
+    lib().orc_par_sort_pairs(DTYPES[dt], _ptr(k), _ptr(v), k.size, threads)
     return k, v
 
 

@@ -60,6 +60,11 @@ def test_radix_restatement_agrees_with_comparison_sort(dt, dist):
     k2, v2 = orc.radix_sort_pairs(x, v, dt)
     assert np.array_equal(v1, v2)
     assert np.array_equal(orc.argsort(x, dt), v1)
+    # the parallel stable forms (full-size GPU checks use them) agree too
+    assert np.array_equal(orc.par_argsort(x, dt), v1)
+    k3, v3 = orc.par_sort_pairs(x, v, dt)
+    assert np.array_equal(v3, v1)
+    assert np.array_equal(k3.view(orc.BITS_DTYPE[dt]), k1.view(orc.BITS_DTYPE[dt]))
 
 
 @pytest.mark.parametrize("dt,dist", [("f32", "f32_mix"), ("f64", "f64_logu"), ("i32", "i32"), ("i64", "i64")])
