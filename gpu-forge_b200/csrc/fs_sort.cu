@@ -6,6 +6,7 @@
 // on that stream (P = key bytes), with no host round trip in between.
 #include "forgesort.h"
 #include "forgesort_bench.h"
+#include "fs_hoststage.h"
 #include "fs_kernels.cuh"
 
 #include <cstdarg>
@@ -69,6 +70,7 @@ struct fs_sorter {
   static constexpr int MAX_TIMED = 24;
   cudaEvent_t ev[2 * MAX_TIMED] = {};
   int ev_used = 0;
+  HostStage stage;  // page-locked chunk ring for pageable host-slice copies
   int test_withhold = 0;    // fs_test_inject(FS_TEST_WITHHOLD_COPY): next radix sort
   int test_fail_alloc = 0;  // fs_test_inject(FS_TEST_FAIL_ALLOC): countdown to a failed growth
   std::unordered_map<void*, size_t> allocs;  // fs_alloc'd pointers -> bytes
@@ -254,6 +256,31 @@ int device_view(fs_sorter* s, const void* p, size_t bytes, const char* what, voi
   }
   *out = const_cast<void*>(p);
   return prepare_ptr(s, p, bytes, what);
+}
+
+// Host-slice copies.  Page-locked host memory is copied directly; pageable
+// memory of at least STAGE_MIN bytes goes through the sorter's chunk ring
+// (fs_hoststage.h), below that the driver's own path is as fast.
+constexpr size_t STAGE_MIN = 1u << 20;
+
+int host_to_device(fs_sorter* s, void* dev, const void* host, size_t bytes) {
+  if (bytes < STAGE_MIN || is_pinned_host(host)) {
+    FS_CUDA(s, cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, s->stream));
+    return FS_OK;
+  }
+  FS_CUDA(s, s->stage.to_device(dev, host, bytes, s->stream));
+  return FS_OK;
+}
+
+// Enqueued after the sort; for pageable memory this waits until the bytes
+// have landed (the caller synchronises the stream next anyway).
+int device_to_host(fs_sorter* s, void* host, const void* dev, size_t bytes) {
+  if (bytes < STAGE_MIN || is_pinned_host(host)) {
+    FS_CUDA(s, cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, s->stream));
+    return FS_OK;
+  }
+  FS_CUDA(s, s->stage.to_host(host, dev, bytes, s->stream));
+  return FS_OK;
 }
 
 int copy_back(fs_sorter* s, void* host, const void* dev, size_t bytes) {
@@ -845,6 +872,7 @@ int fs_destroy(fs_sorter* s) {
   if (s->h2d) cudaStreamSynchronize(s->h2d), cudaStreamDestroy(s->h2d);
   if (s->d2h) cudaStreamSynchronize(s->d2h), cudaStreamDestroy(s->d2h);
   if (s->pipe_start) cudaEventDestroy(s->pipe_start);
+  s->stage.release();
   void* bufs[] = {s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->dst_tab, s->ctl};
   for (void* b : bufs)
     if (b) cudaFree(b);
@@ -1085,9 +1113,9 @@ int fs_host_sort_keys(fs_sorter* s, int dtype, void* host_keys, uint64_t n) {
   if ((rc = set_device(s))) return rc;
   const size_t bytes = (size_t)n * key_bytes_of(dtype);
   if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, bytes, false))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_keys, bytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = host_to_device(s, s->dkeys, host_keys, bytes))) return rc;
   if ((rc = fs_sort_keys(s, dtype, s->dkeys, n, 0))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(host_keys, s->dkeys, bytes, cudaMemcpyDeviceToHost, s->stream));
+  if ((rc = device_to_host(s, host_keys, s->dkeys, bytes))) return rc;
   return finish(s, 1);
 }
 
@@ -1106,11 +1134,11 @@ int fs_host_sort_pairs(fs_sorter* s, int dtype, void* host_keys, uint64_t n_keys
   const size_t kbytes = (size_t)n * key_bytes_of(dtype), vbytes = (size_t)n * 4;
   if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, kbytes, false))) return rc;
   if ((rc = grow(s, &s->dvals, &s->dvals_bytes, vbytes, false))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_keys, kbytes, cudaMemcpyHostToDevice, s->stream));
-  FS_CUDA(s, cudaMemcpyAsync(s->dvals, host_vals, vbytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = host_to_device(s, s->dkeys, host_keys, kbytes))) return rc;
+  if ((rc = host_to_device(s, s->dvals, host_vals, vbytes))) return rc;
   if ((rc = fs_sort_pairs(s, dtype, s->dkeys, static_cast<uint32_t*>(s->dvals), n, 0))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(host_keys, s->dkeys, kbytes, cudaMemcpyDeviceToHost, s->stream));
-  FS_CUDA(s, cudaMemcpyAsync(host_vals, s->dvals, vbytes, cudaMemcpyDeviceToHost, s->stream));
+  if ((rc = device_to_host(s, host_keys, s->dkeys, kbytes))) return rc;
+  if ((rc = device_to_host(s, host_vals, s->dvals, vbytes))) return rc;
   return finish(s, 1);
 }
 
@@ -1127,9 +1155,9 @@ int fs_host_argsort(fs_sorter* s, int dtype, const void* host_keys, uint32_t* ho
   const size_t kbytes = (size_t)n * key_bytes_of(dtype), vbytes = (size_t)n * 4;
   if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, kbytes, false))) return rc;
   if ((rc = grow(s, &s->dvals, &s->dvals_bytes, vbytes, false))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_keys, kbytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = host_to_device(s, s->dkeys, host_keys, kbytes))) return rc;
   if ((rc = fs_argsort(s, dtype, s->dkeys, static_cast<uint32_t*>(s->dvals), n, 0))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(host_idx_out, s->dvals, vbytes, cudaMemcpyDeviceToHost, s->stream));
+  if ((rc = device_to_host(s, host_idx_out, s->dvals, vbytes))) return rc;
   return finish(s, 1);
 }
 
@@ -1177,9 +1205,9 @@ int fs_host_sort_keys_copy(fs_sorter* s, int dtype, const void* host_in, void* h
   }
   if ((rc = set_device(s))) return rc;
   if ((rc = grow(s, &s->dkeys, &s->dkeys_bytes, bytes, false))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(s->dkeys, host_in, bytes, cudaMemcpyHostToDevice, s->stream));
+  if ((rc = host_to_device(s, s->dkeys, host_in, bytes))) return rc;
   if ((rc = fs_sort_keys(s, dtype, s->dkeys, n, 0))) return rc;
-  FS_CUDA(s, cudaMemcpyAsync(host_out, s->dkeys, bytes, cudaMemcpyDeviceToHost, s->stream));
+  if ((rc = device_to_host(s, host_out, s->dkeys, bytes))) return rc;
   return finish(s, 1);
 }
 
