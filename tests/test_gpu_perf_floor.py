@@ -82,17 +82,17 @@ def test_host_slice_floor(sorter, name, dt, floor):
 
 
 # device-resident: (op, dtype, floor Mk/s on one B200)
-DEVICE_CASES = [
-    ("keys", "u32", 25000.0),
-    ("keys", "i32", 25000.0),
-    ("keys", "f32", 25000.0),
-    ("keys", "u64", 8000.0),
-    ("keys", "i64", 8000.0),
-    ("keys", "f64", 8000.0),
-    ("argsort", "u32", 15000.0),
-    ("argsort", "f32", 15000.0),
-    ("pairs", "u32", 15000.0),
-    ("pairs", "u64", 6000.0),
+DEVICE_CASES = [  # measured on one B200 (16M keys): keys u32 42.3, u64 16.1, argsort 30.3, pairs u32 29.5 / u64 9.9 Gk/s
+    ("keys", "u32", 28000.0),
+    ("keys", "i32", 28000.0),
+    ("keys", "f32", 28000.0),
+    ("keys", "u64", 10500.0),
+    ("keys", "i64", 10500.0),
+    ("keys", "f64", 10500.0),
+    ("argsort", "u32", 20000.0),
+    ("argsort", "f32", 20000.0),
+    ("pairs", "u32", 19500.0),
+    ("pairs", "u64", 6500.0),
 ]
 
 
