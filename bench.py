@@ -426,11 +426,14 @@ def run_multi(args):
     vb = 0 if op == "keys" else 4  # payload bytes per key
 
     def step():
+        # sync=False: a step's local sort stays in flight; the next step's one
+        # host wait (for the all-gathered bucket counts) follows it on the
+        # stream, and ss.synchronize() after the timed loop reports errors
         if op == "keys":
-            return ss.sort(keys_in, gpos_base=rank * m)
+            return ss.sort(keys_in, gpos_base=rank * m, sync=False)
         if op == "argsort":
-            return ss.sort_with_positions(keys_in, gpos_base=rank * m)
-        return ss.sort_pairs(keys_in, vals_in, gpos_base=rank * m)
+            return ss.sort_with_positions(keys_in, gpos_base=rank * m, sync=False)
+        return ss.sort_pairs(keys_in, vals_in, gpos_base=rank * m, sync=False)
 
     def timed(fn, steps):
         tdist.barrier()
@@ -442,6 +445,7 @@ def run_multi(args):
             out = fn()
         e1.record(stream)
         e1.synchronize()
+        ss.synchronize()  # device-side errors of the last step
         torch.cuda.synchronize()
         t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)  # the job is as slow as its slowest rank

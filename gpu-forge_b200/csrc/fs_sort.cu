@@ -633,9 +633,12 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
 // ---- sample-sort dispatch -----------------------------------------------------
 // Count: per-slice bucket counts (kept in the sorter's scratch for the
 // dispatch that follows) and the bucket totals, copied to the host.
+// host_counts: copy the bucket sizes to host memory and wait; dev_counts
+// (host_counts == nullptr): copy them to device memory, stream-ordered.
 template <typename K, int XF>
 int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t gpos_base, const void* spl_keys,
-                            const uint64_t* spl_gpos, int nsplit, unsigned long long* host_counts) {
+                            const uint64_t* spl_gpos, int nsplit, unsigned long long* host_counts,
+                            unsigned long long* dev_counts = nullptr) {
   using D = SplitterDigit<K, XF>;
   const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
   Exec e = exec_of(s);
@@ -650,6 +653,12 @@ int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t
       static_cast<const K*>(keys), n, e.ctl, sl, e.counts, dfn, gpos_base);
   t_end(e);
   FS_CUDA(s, cudaGetLastError());
+  if (!host_counts) {
+    FS_CUDA(s, cudaMemcpyAsync(dev_counts, &e.ctl->hist[0][0], (size_t)(nsplit + 1) * sizeof(unsigned long long),
+                               cudaMemcpyDeviceToDevice, e.stream));
+    s->last_launches = 1;
+    return FS_OK;
+  }
   FS_CUDA(s, cudaMemcpyAsync(host_counts, &e.ctl->hist[0][0], (size_t)(nsplit + 1) * sizeof(unsigned long long),
                              cudaMemcpyDeviceToHost, e.stream));
   FS_CUDA(s, cudaStreamSynchronize(e.stream));
@@ -660,6 +669,27 @@ int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t
 // Dispatch: one stable pass that stores every key at its rank within its
 // bucket, straight into that bucket's destination (dst[b], this rank's region
 // of rank b's inbox: plain stores over NVLink when it is another GPU's).
+// Destinations of a dispatch computed on the device from the all-gathered
+// send matrix M (G x G, row s = the bucket sizes rank s sends): this rank's
+// keys of bucket b start after the keys that lower ranks send to rank b.
+struct DispatchBases {
+  uintptr_t key[RADIX];  // rank b's inbox (keys), this process's mapping
+  uintptr_t val[RADIX];  // rank b's inbox (values), payload dispatches only
+};
+
+__global__ void __launch_bounds__(RADIX)
+    k_dispatch_table(const unsigned long long* __restrict__ M, const int G, const int rank, const int kb,
+                     const DispatchBases bases, const int payload, void** __restrict__ tab) {
+  const int b = threadIdx.x;
+  if (b >= G) return;
+  unsigned long long before = 0;
+  for (int r = 0; r < rank; ++r) before += M[(size_t)r * G + b];
+  tab[b] = reinterpret_cast<void*>(bases.key[b] + before * (unsigned long long)kb);
+  if (payload) tab[RADIX + b] = reinterpret_cast<void*>(bases.val[b] + before * 4ull);
+}
+
+// dst_host / vdst_host: destinations from the host (copied into the table);
+// nullptr: the table was already written on the device (k_dispatch_table).
 template <typename K, int XF, int NB, bool VALS>
 int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t* vals, uint64_t n,
                                   uint64_t gpos_base, const void* spl_keys, const uint64_t* spl_gpos, int nsplit,
@@ -673,8 +703,10 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t
   if (!s->dst_tab) FS_CUDA(s, cudaMalloc(&s->dst_tab, 2 * RADIX * sizeof(void*)));
   void** tab = static_cast<void**>(s->dst_tab);
   // pageable sources: the copies are staged before cudaMemcpyAsync returns
-  FS_CUDA(s, cudaMemcpyAsync(tab, dst_host, (size_t)(nsplit + 1) * sizeof(void*), cudaMemcpyHostToDevice, s->stream));
-  if (VALS)
+  if (dst_host)
+    FS_CUDA(s, cudaMemcpyAsync(tab, dst_host, (size_t)(nsplit + 1) * sizeof(void*), cudaMemcpyHostToDevice,
+                               s->stream));
+  if (VALS && vdst_host)
     FS_CUDA(s, cudaMemcpyAsync(tab + RADIX, vdst_host, (size_t)(nsplit + 1) * sizeof(void*), cudaMemcpyHostToDevice,
                                s->stream));
   dfn.dst = reinterpret_cast<K* const*>(tab);
@@ -686,7 +718,7 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t
   PlanArgs a{};
   a.n = n;
   a.kin = keys;
-  a.kfinal = dst_host[0];  // not written: dispatch stores through dst[]
+  a.kfinal = nullptr;  // not written: dispatch stores through dst[]
   a.kother = nullptr;
   a.passes = 1;
   a.write_keys = 1;
@@ -695,7 +727,7 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t
   if (VALS) {
     a.has_vals = 1;
     a.vin = vals;  // nullptr: each key's global position, gpos_base + i
-    a.vfinal = vdst_host[0];  // not written either: dispatch stores through vdst[]
+    a.vfinal = nullptr;  // not written either: dispatch stores through vdst[]
   }
   s->ev_used = 0;
   t_begin(e);
@@ -1370,10 +1402,42 @@ int fs_partition_count(fs_sorter* s, int dtype, const void* keys, uint64_t n, ui
   return finish(s, 1);
 }
 
+int fs_partition_count_async(fs_sorter* s, int dtype, const void* keys, uint64_t n, uint64_t gpos_base,
+                             const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,
+                             uint64_t* bucket_counts_dev) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  if (nsplit < 0 || nsplit > RADIX - 1) return fail(s, FS_E_INVALID, "nsplit = %d outside [0, 255]", nsplit);
+  if (!bucket_counts_dev) return fail(s, FS_E_INVALID, "bucket_counts_dev is NULL");
+  s->part.ready = false;
+  if ((rc = set_device(s))) return rc;
+  const int kb = key_bytes_of(dtype);
+  if ((rc = prepare_ptr(s, bucket_counts_dev, (size_t)(nsplit + 1) * 8, "bucket_counts_dev"))) return rc;
+  if (n == 0) {
+    FS_CUDA(s, cudaMemsetAsync(bucket_counts_dev, 0, (size_t)(nsplit + 1) * 8, s->stream));
+    s->part = {true, dtype, nsplit, keys, 0};
+    return finish(s, 0);
+  }
+  if ((rc = prepare_ptr(s, keys, (size_t)n * kb, "keys"))) return rc;
+  if (nsplit > 0) {
+    if ((rc = prepare_ptr(s, splitter_keys, (size_t)nsplit * kb, "splitter_keys"))) return rc;
+    if ((rc = prepare_ptr(s, splitter_gpos, (size_t)nsplit * 8, "splitter_gpos"))) return rc;
+  }
+  auto* dc = reinterpret_cast<unsigned long long*>(bucket_counts_dev);
+#define FS_PC(K, XF) \
+  enqueue_partition_count<K, XF>(s, keys, n, gpos_base, splitter_keys, splitter_gpos, nsplit, nullptr, dc)
+  FS_PARTITION_DTYPES(FS_PC)
+#undef FS_PC
+  if (rc) return rc;
+  s->part = {true, dtype, nsplit, keys, n};
+  return finish(s, 0);
+}
+
 namespace {
 int partition_dispatch(fs_sorter* s, int dtype, const void* keys, const uint32_t* vals, bool with_vals, uint64_t n,
                        uint64_t gpos_base, const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,
-                       void* const* bucket_dst, uint32_t* const* value_dst, int sync) {
+                       void* const* bucket_dst, uint32_t* const* value_dst, int sync,
+                       const uint64_t* send_matrix = nullptr, int rank = 0) {
   int rc = check_common(s, dtype, n);
   if (rc) return rc;
   if (!s->part.ready || s->part.dtype != dtype || s->part.nsplit != nsplit || s->part.keys != keys ||
@@ -1389,17 +1453,46 @@ int partition_dispatch(fs_sorter* s, int dtype, const void* keys, const uint32_t
   }
   if (with_vals && !vals && gpos_base + n > (1ull << 32))
     return fail(s, FS_E_INVALID, "global positions past 2^32 do not fit u32 indices");
+  if (send_matrix && (rank < 0 || rank > nsplit))
+    return fail(s, FS_E_INVALID, "rank %d outside [0, %d]", rank, nsplit);
   if ((rc = set_device(s))) return rc;
   if (with_vals && vals && (rc = prepare_ptr(s, vals, (size_t)n * 4, "values"))) return rc;
+  void* const* kd = bucket_dst;
+  uint32_t* const* vd = value_dst;
+  if (send_matrix) {  // destinations = inbox bases + what lower ranks send, computed on the device
+    const int G = nsplit + 1;
+    if ((rc = prepare_ptr(s, send_matrix, (size_t)G * G * 8, "send_matrix"))) return rc;
+    if (!s->dst_tab) FS_CUDA(s, cudaMalloc(&s->dst_tab, 2 * RADIX * sizeof(void*)));
+    DispatchBases bases{};
+    for (int b = 0; b < G; ++b) {
+      bases.key[b] = reinterpret_cast<uintptr_t>(bucket_dst[b]);
+      bases.val[b] = with_vals ? reinterpret_cast<uintptr_t>(value_dst[b]) : 0;
+    }
+    k_dispatch_table<<<1, RADIX, 0, s->stream>>>(reinterpret_cast<const unsigned long long*>(send_matrix), G, rank,
+                                                 key_bytes_of(dtype), bases, with_vals ? 1 : 0,
+                                                 static_cast<void**>(s->dst_tab));
+    FS_CUDA(s, cudaGetLastError());
+    kd = nullptr;  // the table is ready on the device
+    vd = nullptr;
+  }
 #define FS_PD(K, XF)                                                                                         \
   enqueue_partition_dispatch<K, XF>(s, keys, vals, with_vals, n, gpos_base, splitter_keys, splitter_gpos, nsplit, \
-                                    bucket_dst, value_dst)
+                                    kd, vd)
   FS_PARTITION_DTYPES(FS_PD)
 #undef FS_PD
   if (rc) return rc;
   return finish(s, sync);
 }
 }  // namespace
+
+int fs_partition_dispatch_matrix(fs_sorter* s, int dtype, const void* keys, const uint32_t* vals, int payload,
+                                 uint64_t n, uint64_t gpos_base, const void* splitter_keys,
+                                 const uint64_t* splitter_gpos, int nsplit, const uint64_t* send_matrix, int rank,
+                                 void* const* inbox_keys, uint32_t* const* inbox_vals, int sync) {
+  if (!send_matrix) return s ? fail(s, FS_E_INVALID, "send_matrix is NULL") : FS_E_INVALID;
+  return partition_dispatch(s, dtype, keys, vals, payload != 0, n, gpos_base, splitter_keys, splitter_gpos, nsplit,
+                            inbox_keys, inbox_vals, sync, send_matrix, rank);
+}
 
 int fs_partition_dispatch(fs_sorter* s, int dtype, const void* keys, uint64_t n, uint64_t gpos_base,
                           const void* splitter_keys, const uint64_t* splitter_gpos, int nsplit,

@@ -65,6 +65,9 @@ SIGNATURES = {
     "fs_mg_sort_pairs": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "fs_partition_count": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp]),
     "fs_partition_dispatch": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp, _i32]),
+    "fs_partition_count_async": (_i32, [_vp, _i32, _vp, _u64, _u64, _vp, _vp, _i32, _vp]),
+    "fs_partition_dispatch_matrix": (_i32, [_vp, _i32, _vp, _vp, _i32, _u64, _u64, _vp, _vp, _i32, _vp, _i32, _vp,
+                                            _vp, _i32]),
     "fs_ipc_export": (_i32, [_vp, _vp, _vp]),
     "fs_ipc_open": (_i32, [_vp, _vp, _pp]),
     "fs_ipc_close": (_i32, [_vp, _vp]),

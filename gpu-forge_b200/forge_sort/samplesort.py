@@ -179,51 +179,69 @@ class CudaOps:
         self._inbox = 0
         self._cap = 0
 
-    def exchange(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray, group,
-                 vals=None, payload: bool = False):
+    def _same_stream(self, dev) -> bool:
+        from .sorter import _stream_handle
+        return self.s.stream_handle == _stream_handle(self.torch.cuda.current_stream(dev))
+
+    def exchange(self, dt, keys, gpos_base, spl_keys, spl_gpos, group, vals=None, payload: bool = False,
+                 sync: bool = True):
         """Partition + all-to-all + local sort; returns (sorted piece, value
-        piece or None, send counts, receive counts).  With payload, a u32
-        value travels with every key: vals (int32 tensor), or each key's
-        global position when vals is None.  Runs on the current torch
-        stream."""
+        piece or None, send counts, receive counts).  spl_keys / spl_gpos:
+        the G-1 splitters (raw key bits, global positions) as device tensors
+        in (key, position) order.  With payload, a u32 value travels with
+        every key: vals (int32 tensor), or each key's global position when
+        vals is None.
+
+        Runs on the current torch stream.  When that is the sorter's stream,
+        the host waits once per call -- for the all-gathered bucket counts,
+        which size the receive buffers -- and everything else is
+        stream-ordered: count, count all-gather, dispatch (destinations
+        computed on the device), the all-reduce that tells every rank its
+        inbox is complete, and the local sort.  sync=False leaves the local
+        sort in flight (errors surface at the next call or synchronize())."""
         torch, dist = self.torch, self.torch.distributed
         G, r = dist.get_world_size(group), dist.get_rank(group)
         dev, kb, m = keys.device, keys.element_size(), keys.numel()
-        torch.cuda.current_stream(dev).synchronize()  # keys are ready whatever stream wrote them
-        sk, sg, skp, sgp = self._splitters(dt, dev, spl_raw, spl_gpos)
-        send = self.s.partition_count(dt, keys.data_ptr(), m, gpos_base, skp, sgp, G - 1)
-        cnt = torch.tensor(send, dtype=torch.int64, device=dev)
-        rows = [torch.empty_like(cnt) for _ in range(G)]
-        collective(dist, "bucket counts", dist.all_gather, rows, cnt, group=group)
-        M = torch.stack(rows).cpu().numpy()  # M[s, b]: keys rank s sends to rank b
+        same = self._same_stream(dev)
+        if not same:
+            torch.cuda.current_stream(dev).synchronize()  # keys are ready whatever stream wrote them
+        counts = torch.empty(G, dtype=torch.int64, device=dev)
+        self.s.partition_count_async(dt, keys.data_ptr(), m, gpos_base, spl_keys.data_ptr(), spl_gpos.data_ptr(),
+                                     G - 1, counts.data_ptr())
+        if not same:
+            self.s.synchronize()
+        rows = [torch.empty_like(counts) for _ in range(G)]
+        collective(dist, "bucket counts", dist.all_gather, rows, counts, group=group)
+        Mdev = torch.stack(rows)  # Mdev[s, b]: keys rank s sends to rank b
+        M = Mdev.cpu().numpy()  # the one host wait of the step
+        self.s.synchronize()  # the stream is drained this far: surfaces earlier device errors at no cost
         most = int(M.sum(axis=0).max())
         # inbox: [keys | values], the values region 256-byte aligned
         voff = (most * kb + 255) // 256 * 256 if payload else 0
         self._ensure_inbox(voff + most * 4 if payload else most * kb, group, dev)
-        start = M[:r, :].sum(axis=0)  # where this rank's keys begin in every inbox
-        dst = [self._peers[b] + int(start[b]) * kb for b in range(G)]
-        if payload:
-            vdst = [self._peers[b] + voff + int(start[b]) * 4 for b in range(G)]
-            self.s.partition_dispatch_pairs(dt, keys.data_ptr(), 0 if vals is None else vals.data_ptr(), m,
-                                            gpos_base, skp, sgp, G - 1, dst, vdst, sync=True)
-        else:
-            self.s.partition_dispatch(dt, keys.data_ptr(), m, gpos_base, skp, sgp, G - 1, dst, sync=True)
-        # every rank enters this collective after its dispatch finished, so
-        # once it completes every inbox is full
+        vbase = [p + voff for p in self._peers] if payload else None
+        self.s.partition_dispatch_matrix(dt, keys.data_ptr(), m, gpos_base, spl_keys.data_ptr(),
+                                         spl_gpos.data_ptr(), G - 1, Mdev.data_ptr(), r, self._peers, vbase,
+                                         vals_ptr=0 if (vals is None or not payload) else vals.data_ptr(),
+                                         payload=payload, sync=not same)
+        # every rank enters this collective after its dispatch (stream order),
+        # so once it completes every inbox is full
         done = torch.zeros(1, dtype=torch.int32, device=dev)
         collective(dist, "dispatch done", dist.all_reduce, done, group=group)
-        torch.cuda.current_stream(dev).synchronize()
-        del sk, sg
+        if not same:
+            torch.cuda.current_stream(dev).synchronize()
         recv = [int(x) for x in M[:, r]]
         total = sum(recv)
         out = torch.empty(total, dtype=keys.dtype, device=dev)
         vout = torch.empty(total, dtype=torch.int32, device=dev) if payload else None
+        local_sync = sync or not same
         if total and payload:
             self.s.sort_pairs_device_copy(dt, self._inbox, self._inbox + voff, out.data_ptr(), vout.data_ptr(),
-                                          total, sync=True)
+                                          total, sync=local_sync)
         elif total:
-            self.s.sort_device_copy(dt, self._inbox, out.data_ptr(), total, sync=True)
-        return out, vout, send, recv
+            self.s.sort_device_copy(dt, self._inbox, out.data_ptr(), total, sync=local_sync)
+        del Mdev, rows, counts
+        return out, vout, [int(x) for x in M[r, :]], recv
 
     def partition(self, dt, keys, gpos_base, spl_raw: np.ndarray, spl_gpos: np.ndarray) -> Tuple[object, List[int]]:
         torch = self.torch
@@ -290,31 +308,38 @@ class SampleSorter:
     def _world(self):
         return self.dist.get_world_size(self.group), self.dist.get_rank(self.group)
 
-    def sort(self, keys, gpos_base: Optional[int] = None):
-        """This rank's piece of the sorted keys."""
-        return self._run(keys, None, False, gpos_base)[0]
+    def sort(self, keys, gpos_base: Optional[int] = None, sync: bool = True):
+        """This rank's piece of the sorted keys.  sync=False returns with the
+        local sort still in flight on the current stream (call synchronize()
+        before relying on device-side error reporting)."""
+        return self._run(keys, None, False, gpos_base, sync)[0]
 
-    def sort_pairs(self, keys, values, gpos_base: Optional[int] = None):
+    def sort_pairs(self, keys, values, gpos_base: Optional[int] = None, sync: bool = True):
         """(keys piece, values piece) of the stable sort of (key, value)
         pairs by key: equal keys keep their global input order.  values is an
         int32 tensor holding u32 values, one per key."""
         if values is None or values.numel() != keys.numel():
             raise ValueError("sort_pairs needs one value per key")
-        return self._run(keys, values, True, gpos_base)
+        return self._run(keys, values, True, gpos_base, sync)
 
-    def argsort(self, keys, gpos_base: Optional[int] = None):
+    def argsort(self, keys, gpos_base: Optional[int] = None, sync: bool = True):
         """This rank's piece of the stable global argsort: the global input
         positions (u32, in an int32 tensor) of the keys this rank's piece of
         the sorted sequence holds.  The whole input may hold at most 2^32
         keys."""
-        return self._run(keys, None, True, gpos_base)[1]
+        return self._run(keys, None, True, gpos_base, sync)[1]
 
-    def sort_with_positions(self, keys, gpos_base: Optional[int] = None):
+    def sort_with_positions(self, keys, gpos_base: Optional[int] = None, sync: bool = True):
         """(keys piece, positions piece): argsort that also returns the
         sorted keys the local step produces anyway."""
-        return self._run(keys, None, True, gpos_base)
+        return self._run(keys, None, True, gpos_base, sync)
 
-    def _run(self, keys, vals, payload: bool, gpos_base: Optional[int]):
+    def synchronize(self) -> None:
+        """Wait for the last call's device work and report device-side errors."""
+        if hasattr(self.ops, "s"):
+            self.ops.s.synchronize()
+
+    def _run(self, keys, vals, payload: bool, gpos_base: Optional[int], sync: bool = True):
         torch, dist, dt = self.torch, self.dist, self.dt
         G, r = self._world()
         m = keys.numel()
@@ -358,19 +383,30 @@ class SampleSorter:
         gathered = [torch.empty_like(mine) for _ in range(G)]
         collective(dist, "samples", dist.all_gather, gathered, mine, group=self.group)
         allv = torch.cat(gathered)
+        # a stable sort by key keeps equal keys in gathered order, which is
+        # (rank, sample) = global-position order: the picks come out in
+        # (key, global position) order, as the partition searches them
         order = torch.sort(allv[:, 0], stable=True).indices
-        sel = allv[order[torch.arange(1, G, device=allv.device) * S]].cpu().numpy()
-        # splitters ascending by (key, global position), as the partition searches them
+        sel = allv[order[torch.arange(1, G, device=allv.device) * S]]
+
+        # 2-4 on GPUs: dispatch straight into the peers' inboxes, local sort;
+        # the splitters never leave the device
+        if getattr(self.ops, "dispatch", False):
+            spl_gpos_dev = sel[:, 1].contiguous()
+            if wide:
+                spl_keys_dev = sel[:, 2].contiguous()
+            else:  # low 32 bits as int32 (two's complement)
+                low = sel[:, 2]
+                spl_keys_dev = torch.where(low >= 2 ** 31, low - 2 ** 32, low).to(torch.int32).contiguous()
+            out, vout, send, recv = self.ops.exchange(dt, keys, gpos_base, spl_keys_dev, spl_gpos_dev, self.group,
+                                                      vals=vals, payload=payload, sync=sync)
+            self.last = SampleSortStats(send, recv)
+            return out, vout
+
+        sel = sel.cpu().numpy()
         sel = sel[np.lexsort((sel[:, 1].view(np.uint64), sel[:, 0]))]
         spl_raw = sel[:, 2].view(np.uint64).astype(_BITS[dt])
         spl_gpos = sel[:, 1].view(np.uint64)
-
-        # 2-4 on GPUs: dispatch straight into the peers' inboxes, local sort
-        if getattr(self.ops, "dispatch", False):
-            out, vout, send, recv = self.ops.exchange(dt, keys, gpos_base, spl_raw, spl_gpos, self.group,
-                                                      vals=vals, payload=payload)
-            self.last = SampleSortStats(send, recv)
-            return out, vout
 
         # 2. stable partition into G buckets (values travel beside the keys)
         if payload:

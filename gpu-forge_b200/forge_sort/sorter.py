@@ -201,6 +201,7 @@ class GpuSorter:
             raise from_status(rc, L.fs_last_error(None).decode())
         self._h = h
         self.device = int(device)
+        self.stream_handle = _stream_handle(stream)  # None: the sorter's own stream
         self._pending = False
 
     @classmethod
@@ -245,6 +246,7 @@ class GpuSorter:
 
     def set_stream(self, stream) -> None:
         self._call(_lib.load().fs_set_stream(self._h, _stream_handle(stream)))
+        self.stream_handle = _stream_handle(stream)
 
     def scratch_bytes(self) -> int:
         return int(_lib.load().fs_scratch_bytes(self._h))
@@ -485,6 +487,33 @@ class GpuSorter:
                                                   ctypes.c_void_p(spl_keys_ptr), ctypes.c_void_p(spl_gpos_ptr),
                                                   nsplit, out))
         return [int(x) for x in out]
+
+    def partition_count_async(self, dt, in_ptr: int, n: int, gpos_base: int, spl_keys_ptr: int,
+                              spl_gpos_ptr: int, nsplit: int, counts_dev_ptr: int) -> None:
+        """Dispatch step 1 without a host round trip: the nsplit+1 bucket
+        sizes go to device memory (u64), stream-ordered."""
+        name = dtype_name(dt)
+        self._call(_lib.load().fs_partition_count_async(
+            self._h, _DT[name][0], ctypes.c_void_p(in_ptr), n, gpos_base, ctypes.c_void_p(spl_keys_ptr),
+            ctypes.c_void_p(spl_gpos_ptr), nsplit, ctypes.c_void_p(counts_dev_ptr)))
+        self._pending = True
+
+    def partition_dispatch_matrix(self, dt, in_ptr: int, n: int, gpos_base: int, spl_keys_ptr: int,
+                                  spl_gpos_ptr: int, nsplit: int, send_matrix_ptr: int, rank: int, inbox_keys,
+                                  inbox_vals=None, vals_ptr: int = 0, payload: bool = False,
+                                  sync: bool = False) -> None:
+        """Dispatch step 2 with the destinations computed on the device from
+        the all-gathered send matrix (device, (nsplit+1)^2 u64) and this
+        rank's index; inbox_keys / inbox_vals are the peers' inbox bases."""
+        name = dtype_name(dt)
+        G = nsplit + 1
+        kt = (ctypes.c_void_p * G)(*[ctypes.c_void_p(int(p)) for p in inbox_keys])
+        vt = (ctypes.c_void_p * G)(*[ctypes.c_void_p(int(p)) for p in inbox_vals]) if payload else None
+        self._call(_lib.load().fs_partition_dispatch_matrix(
+            self._h, _DT[name][0], ctypes.c_void_p(in_ptr), ctypes.c_void_p(vals_ptr or None), int(payload), n,
+            gpos_base, ctypes.c_void_p(spl_keys_ptr), ctypes.c_void_p(spl_gpos_ptr), nsplit,
+            ctypes.c_void_p(send_matrix_ptr), int(rank), kt, vt, int(sync)))
+        self._pending = self._pending or not sync
 
     def partition_dispatch(self, dt, in_ptr: int, n: int, gpos_base: int, spl_keys_ptr: int, spl_gpos_ptr: int,
                            nsplit: int, dst_ptrs, sync: bool = False) -> None:

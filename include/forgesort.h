@@ -271,6 +271,33 @@ int fs_partition_dispatch_pairs(fs_sorter* s, int dtype, const void* keys,
                                 void* const* bucket_dst,
                                 uint32_t* const* value_dst, int sync);
 
+/* The same two steps without host round trips, for a sample-sort step that
+ * waits on the host once (to size the receive buffers).
+ * fs_partition_count_async: as fs_partition_count, but the bucket sizes go
+ * to device memory bucket_counts_dev (nsplit+1 u64), stream-ordered, and the
+ * call returns at once.
+ * fs_partition_dispatch_matrix: as fs_partition_dispatch(_pairs), with the
+ * destinations computed on the device: send_matrix (device, G x G u64,
+ * G = nsplit+1, row r = the bucket sizes rank r counted, e.g. the counts
+ * all-gathered in rank order) and this rank's index `rank` give
+ * bucket_dst[b] = inbox_keys[b] + (keys that ranks below `rank` send to
+ * rank b), and likewise inbox_vals[b] for the values (payload != 0; vals
+ * NULL sends global positions).  inbox_keys / inbox_vals: host arrays of G
+ * device pointers (peers' inboxes, fs_ipc_open).  Must follow
+ * fs_partition_count_async or fs_partition_count of the same keys. */
+int fs_partition_count_async(fs_sorter* s, int dtype, const void* keys,
+                             uint64_t n, uint64_t gpos_base,
+                             const void* splitter_keys,
+                             const uint64_t* splitter_gpos, int nsplit,
+                             uint64_t* bucket_counts_dev);
+int fs_partition_dispatch_matrix(fs_sorter* s, int dtype, const void* keys,
+                                 const uint32_t* vals, int payload, uint64_t n,
+                                 uint64_t gpos_base, const void* splitter_keys,
+                                 const uint64_t* splitter_gpos, int nsplit,
+                                 const uint64_t* send_matrix, int rank,
+                                 void* const* inbox_keys,
+                                 uint32_t* const* inbox_vals, int sync);
+
 /* CUDA IPC for the dispatch inboxes (one process per GPU): export a handle to
  * device memory from cudaMalloc (fs_alloc with managed = 0), open a peer's
  * handle into this process (peer access enabled lazily), close it again

@@ -174,3 +174,69 @@ def test_single_rank_argsort_and_pairs(sorter):
         assert np.array_equal(v2.cpu().numpy().view(np.uint32), v[order])
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dt,dist,nspl,payload,with_vals", [("u32", "u32", 7, False, False),
+                                                             ("f32", "f32_mix", 3, True, True),
+                                                             ("u64", "u64", 1, True, False),
+                                                             ("i64", "i64", 5, False, False)])
+def test_async_count_and_matrix_dispatch(sorter, dt, dist, nspl, payload, with_vals):
+    """fs_partition_count_async + fs_partition_dispatch_matrix, the host-wait-
+    free form of the sample sort's exchange, as rank r of G ranks on one GPU:
+    the counts land in device memory, and bucket b's keys (and values) land in
+    inbox b after what the lower ranks send there (rows of the send matrix
+    other than r are made up); nothing else in the inboxes is touched."""
+    import torch
+    from forge_sort.samplesort import choose_splitters, ordered_bits
+    G = nspl + 1
+    rank = G // 2
+    n, base = 250_003, 3_000_000
+    x = orc.gen(dist, n, seed=11 + nspl)
+    bits = orc.BITS_DTYPE[dt]
+    iv = np.int32 if bits is np.uint32 else np.int64
+    xb = np.ascontiguousarray(x).view(bits)
+    per = 64
+    pos = ((np.arange(per * G) + 0.5) * (n / (per * G))).astype(np.int64)
+    samp_raw, samp_gpos = xb[pos], (pos + base).astype(np.uint64)
+    picks = choose_splitters(ordered_bits(samp_raw, dt), samp_gpos, G, per)
+    spl_raw, spl_gpos = samp_raw[picks], samp_gpos[picks]
+    keys = torch.from_numpy(xb.view(iv).copy()).cuda()
+    vals_h = orc.gen("u32", n, seed=5)
+    vals = torch.from_numpy(vals_h.view(np.int32).copy()).cuda()
+    sk = torch.from_numpy(spl_raw.view(iv).copy()).cuda()
+    sg = torch.from_numpy(spl_gpos.view(np.int64).copy()).cuda()
+    counts = torch.zeros(G, dtype=torch.int64, device="cuda")
+    sorter.partition_count_async(dt, keys.data_ptr(), n, base, sk.data_ptr(), sg.data_ptr(), nspl, counts.data_ptr())
+    want_k, wcounts = ref_partition(xb, dt, base, spl_raw, spl_gpos)
+    assert counts.cpu().numpy().tolist() == wcounts.tolist()
+    rng = np.random.default_rng(nspl)
+    M = rng.integers(0, 5000, (G, G)).astype(np.int64)
+    M[rank] = wcounts
+    Mdev = torch.from_numpy(M).cuda()
+    col = M.sum(axis=0)
+    kb = keys.element_size()
+    inbox_k = [torch.full((int(col[b]) + 16,), -1, dtype=keys.dtype, device="cuda") for b in range(G)]
+    inbox_v = [torch.full((int(col[b]) + 16,), -1, dtype=torch.int32, device="cuda") for b in range(G)]
+    sorter.partition_dispatch_matrix(dt, keys.data_ptr(), n, base, sk.data_ptr(), sg.data_ptr(), nspl,
+                                     Mdev.data_ptr(), rank, [t.data_ptr() for t in inbox_k],
+                                     [t.data_ptr() for t in inbox_v] if payload else None,
+                                     vals_ptr=vals.data_ptr() if with_vals else 0, payload=payload, sync=True)
+    o = ordered_bits(xb, dt)
+    g = np.arange(n, dtype=np.uint64) + np.uint64(base)
+    so = ordered_bits(spl_raw, dt)
+    bk = np.zeros(n, np.int64)
+    for j in range(nspl):
+        bk += ((o > so[j]) | ((o == so[j]) & (g >= spl_gpos[j]))).astype(np.int64)
+    order = np.argsort(bk, kind="stable")
+    want_v = vals_h[order] if with_vals else (order + base).astype(np.uint32)
+    starts = np.concatenate([[0], np.cumsum(wcounts)[:-1]])
+    for b in range(G):
+        lo = int(M[:rank, b].sum())
+        c = int(wcounts[b])
+        got = inbox_k[b].cpu().numpy().view(bits)
+        assert np.array_equal(got[lo:lo + c], want_k[starts[b]:starts[b] + c]), b
+        assert bool((inbox_k[b][:lo] == -1).all()) and bool((inbox_k[b][lo + c:] == -1).all()), b
+        if payload:
+            gv = inbox_v[b].cpu().numpy().view(np.uint32)
+            assert np.array_equal(gv[lo:lo + c], want_v[starts[b]:starts[b] + c]), b
+            assert bool((inbox_v[b][:lo] == -1).all()) and bool((inbox_v[b][lo + c:] == -1).all()), b
