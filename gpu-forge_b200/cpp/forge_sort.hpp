@@ -8,9 +8,9 @@
 //   Result<T, SortError>      -> T, or throws forge_sort::SortError
 //   &mut [T] / &[T]           -> std::span<T> / std::span<const T>
 //   Vec<u32>                  -> std::vector<uint32_t>
-//   SortBuffer<T>             -> SortBuffer<T> (page-locked host memory: host
-//                                slices at full speed; a sort copies it
-//                                through HBM at PCIe rate)
+//   SortBuffer<T>             -> SortBuffer<T> (device memory + page-locked host
+//                                mirror kept coherent lazily: sorts stay in
+//                                HBM, host views copy back only what changed)
 //   MTLDevice + command queue -> CUDA device ordinal + cudaStream_t (void*)
 //   metal_buffer()            -> device_ptr()
 // Sealed SortKey (lib.rs:15-88) -> SortKey<T>, defined for the six key types
@@ -108,6 +108,11 @@ FORGE_SORT_KEY(double, FS_F64, 8, true, true, 1, 2)
 class GpuSorter;
 
 // ---- SortBuffer<T> (lib.rs:160-281) -----------------------------------------
+// Device memory plus a page-locked host mirror, kept coherent lazily by the
+// library (fs_buffer_*): sorts stay in HBM; as_slice() copies back only what
+// they changed; as_mut_slice() marks the device copy stale.  A span from
+// as_mut_slice() is one host write session: take it again to write after a
+// sort (Rust's borrow of &mut self ends the same way).
 template <typename T>
 class SortBuffer {
   static_assert(sizeof(SortKey<T>) > 0, "SortBuffer<T> needs a SortKey type");
@@ -117,8 +122,7 @@ class SortBuffer {
   SortBuffer& operator=(SortBuffer&& o) noexcept {
     if (this != &o) {
       release();
-      owner_ = std::exchange(o.owner_, nullptr);
-      ptr_ = std::exchange(o.ptr_, nullptr);
+      b_ = std::exchange(o.b_, nullptr);
       len_ = std::exchange(o.len_, 0);
       cap_ = std::exchange(o.cap_, 0);
     }
@@ -133,9 +137,15 @@ class SortBuffer {
   std::size_t capacity() const { return cap_; }
 
   // Writable view of all capacity() elements: write, then set_len().
-  std::span<T> as_mut_slice() { return {static_cast<T*>(ptr_), cap_}; }
+  std::span<T> as_mut_slice() {
+    detail::check(fs_buffer_host_write(b_), nullptr);
+    return {host(), cap_};
+  }
   // The first len() elements (the sorted result after a sort).
-  std::span<const T> as_slice() const { return {static_cast<const T*>(ptr_), len_}; }
+  std::span<const T> as_slice() const {
+    detail::check(fs_buffer_host_read(b_), nullptr);
+    return {host(), len_};
+  }
 
   void set_len(std::size_t len) {
     if (len > cap_)
@@ -146,42 +156,47 @@ class SortBuffer {
     if (data.size() > cap_)
       throw std::length_error("data len " + std::to_string(data.size()) + " exceeds capacity " +
                               std::to_string(cap_));
-    if (!data.empty()) std::memcpy(ptr_, data.data(), data.size_bytes());
+    detail::check(fs_buffer_host_write(b_), nullptr);
+    if (!data.empty()) std::memcpy(host(), data.data(), data.size_bytes());
     len_ = data.size();
   }
   void copy_to_slice(std::span<T> dest) const {
     const std::size_t n = len_ < dest.size() ? len_ : dest.size();
-    if (n) std::memcpy(dest.data(), ptr_, n * sizeof(T));
+    detail::check(fs_buffer_host_read(b_), nullptr);
+    if (n) std::memcpy(dest.data(), host(), n * sizeof(T));
   }
 
-  // Device address of element 0 (replaces metal_buffer()).
-  void* device_ptr() const { return ptr_; }
+  // Device address of element 0 (replaces metal_buffer()) for other device
+  // code: the device copy is made current for len() elements and counted as
+  // written, so a later host read waits for the device.
+  void* device_ptr() const {
+    detail::check(fs_buffer_device_use(b_, len_ * sizeof(T)), nullptr);
+    return fs_buffer_device(b_);
+  }
+  // The library's buffer object (what the sorts take).
+  fs_buffer* handle() const { return b_; }
 
-  // Wrap an allocation the caller owns (page-locked host, managed or device memory of at least
-  // capacity * sizeof(T) bytes); the SortBuffer will not free it.
-  static SortBuffer from_raw_parts(void* ptr, std::size_t len, std::size_t capacity) {
+  // Re-wrap a buffer object given up by into_raw_parts (owned again).
+  static SortBuffer from_raw_parts(fs_buffer* b, std::size_t len, std::size_t capacity) {
     if (len > capacity)
       throw std::length_error("len " + std::to_string(len) + " exceeds capacity " + std::to_string(capacity));
-    return SortBuffer(nullptr, ptr, len, capacity);
+    if (capacity * sizeof(T) > fs_buffer_bytes(b)) throw std::length_error("capacity exceeds the buffer's size");
+    return SortBuffer(b, len, capacity);
   }
-  // Give up ownership: (pointer, len, capacity).  The caller frees the
-  // pointer with fs_free on the sorter that allocated it.
-  std::tuple<void*, std::size_t, std::size_t> into_raw_parts() && {
-    owner_ = nullptr;
-    return {std::exchange(ptr_, nullptr), std::exchange(len_, 0), std::exchange(cap_, 0)};
+  // Give up ownership: (buffer object, len, capacity); fs_buffer_destroy frees it.
+  std::tuple<fs_buffer*, std::size_t, std::size_t> into_raw_parts() && {
+    return {std::exchange(b_, nullptr), std::exchange(len_, 0), std::exchange(cap_, 0)};
   }
 
  private:
   friend class GpuSorter;
-  SortBuffer(fs_sorter* owner, void* ptr, std::size_t len, std::size_t cap)
-      : owner_(owner), ptr_(ptr), len_(len), cap_(cap) {}
+  SortBuffer(fs_buffer* b, std::size_t len, std::size_t cap) : b_(b), len_(len), cap_(cap) {}
+  T* host() const { return static_cast<T*>(fs_buffer_host(b_)); }
   void release() noexcept {
-    if (owner_ && ptr_) fs_free(owner_, ptr_);
-    owner_ = nullptr;
-    ptr_ = nullptr;
+    if (b_) fs_buffer_destroy(b_);
+    b_ = nullptr;
   }
-  fs_sorter* owner_ = nullptr;  // frees ptr_ when set
-  void* ptr_ = nullptr;
+  fs_buffer* b_ = nullptr;
   std::size_t len_ = 0, cap_ = 0;
 };
 
@@ -213,9 +228,9 @@ class GpuSorter {
   // -- zero-copy buffers (lib.rs:694-738, 1000-1117, 2301-2590) ----------------
   template <typename T>
   SortBuffer<T> alloc_sort_buffer(std::size_t capacity) {
-    void* p = nullptr;
-    detail::check(fs_alloc(h_, capacity * sizeof(T), 1, &p), h_);
-    return SortBuffer<T>(h_, p, 0, capacity);
+    fs_buffer* b = nullptr;
+    detail::check(fs_buffer_create(h_, (capacity ? capacity : 1) * sizeof(T), &b), h_);
+    return SortBuffer<T>(b, 0, capacity);
   }
   void sort_buffer(const SortBuffer<uint32_t>& b) { sort_buf(b); }
   void sort_i32_buffer(const SortBuffer<int32_t>& b) { sort_buf(b); }
@@ -230,7 +245,7 @@ class GpuSorter {
   void encode_sort(void* stream, const SortBuffer<uint32_t>& b) {
     if (b.len() <= 1) return;
     if (stream) detail::check(fs_set_stream(h_, stream), h_);
-    detail::check(fs_sort_keys(h_, FS_U32, b.device_ptr(), b.len(), 0), h_);
+    detail::check(fs_sort_buffer(h_, FS_U32, b.handle(), b.len(), 0), h_);
   }
 
   // -- host slices, in place (lib.rs:791-998, 2238-2485) ----------------------
@@ -276,7 +291,7 @@ class GpuSorter {
   template <typename T>
   void sort_buf(const SortBuffer<T>& b) {
     if (b.len() <= 1) return;
-    detail::check(fs_sort_keys(h_, SortKey<T>::DTYPE, b.device_ptr(), b.len(), 1), h_);
+    detail::check(fs_sort_buffer(h_, SortKey<T>::DTYPE, b.handle(), b.len(), 1), h_);
   }
   template <typename T>
   void sort_host(std::span<T> d) {

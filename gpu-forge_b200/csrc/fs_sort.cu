@@ -78,6 +78,22 @@ struct fs_sorter {
   std::string err;
 };
 
+// A SortBuffer: device memory plus a page-locked host mirror, kept coherent
+// lazily.  Sorts run on the device copy and copy nothing back; the host side
+// is brought up to date only when the host reads it, and the device side
+// only for the bytes a sort (or a device user) needs after the host wrote.
+struct fs_buffer {
+  int device = 0;
+  void* dev = nullptr;
+  void* host = nullptr;
+  uint64_t bytes = 0;
+  uint64_t dev_valid = 0;   // leading bytes the device copy holds as the host last wrote them
+  uint64_t dev_newer = 0;   // leading bytes device work may have changed since the host last read
+  cudaEvent_t done = nullptr;  // recorded after the last sort that touched the buffer
+  bool pending = false;        // `done` marks work not yet waited for
+  bool any_stream = false;     // handed out for device use on a stream not known here
+};
+
 namespace {
 
 thread_local std::string g_create_err;
@@ -1693,6 +1709,157 @@ int fs_test_inject(fs_sorter* s, int kind, int arg) {
     default:
       return fail(s, FS_E_INVALID, "unknown injection kind %d", kind);
   }
+}
+
+// ---- SortBuffer objects ------------------------------------------------------
+// Buffer-only calls report errors through fs_last_error(NULL): a buffer may
+// outlive the sorter that created it.
+namespace {
+// Wait for the device work that may have written the buffer.
+int buffer_wait(fs_buffer* b) {
+  if (b->any_stream) {
+    FS_CUDA(nullptr, cudaDeviceSynchronize());
+  } else if (b->pending) {
+    FS_CUDA(nullptr, cudaEventSynchronize(b->done));
+  }
+  b->pending = false;
+  return FS_OK;
+}
+
+// Bring the leading `need` bytes of the device copy up to date with the host
+// mirror, enqueued on `st`.
+int buffer_to_device(fs_sorter* s, fs_buffer* b, uint64_t need, cudaStream_t st) {
+  if (b->dev_valid >= need) return FS_OK;
+  FS_CUDA(s, cudaMemcpyAsync(static_cast<char*>(b->dev) + b->dev_valid, static_cast<char*>(b->host) + b->dev_valid,
+                             need - b->dev_valid, cudaMemcpyHostToDevice, st));
+  b->dev_valid = need;
+  return FS_OK;
+}
+
+int check_buffer(fs_sorter* s, const fs_buffer* b, uint64_t need, const char* what) {
+  if (!b) return fail(s, FS_E_INVALID, "%s is NULL", what);
+  if (b->device != s->device)
+    return fail(s, FS_E_INVALID, "%s lives on device %d, the sorter on device %d", what, b->device, s->device);
+  if (need > b->bytes)
+    return fail(s, FS_E_INVALID, "%s holds %llu bytes, %llu needed", what, (unsigned long long)b->bytes,
+                (unsigned long long)need);
+  return FS_OK;
+}
+
+// After a sort enqueued on s's stream wrote the leading `need` bytes.
+int buffer_sorted(fs_sorter* s, fs_buffer* b, uint64_t need) {
+  if (need > b->dev_newer) b->dev_newer = need;
+  FS_CUDA(s, cudaEventRecord(b->done, s->stream));
+  b->pending = true;
+  b->any_stream = false;
+  return FS_OK;
+}
+}  // namespace
+
+int fs_buffer_create(fs_sorter* s, uint64_t bytes, fs_buffer** out) {
+  if (!s || !out) return s ? fail(s, FS_E_INVALID, "out is NULL") : FS_E_INVALID;
+  *out = nullptr;
+  int rc = set_device(s);
+  if (rc) return rc;
+  const uint64_t b = bytes ? bytes : 16;
+  fs_buffer* buf = new fs_buffer();
+  buf->device = s->device;
+  buf->bytes = b;
+  cudaError_t e = cudaMalloc(&buf->dev, b);
+  if (e == cudaSuccess) e = cudaHostAlloc(&buf->host, b, cudaHostAllocPortable);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&buf->done, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (buf->host) cudaFreeHost(buf->host);
+    if (buf->dev) cudaFree(buf->dev);
+    delete buf;
+    return fail(s, e == cudaErrorMemoryAllocation ? FS_E_OOM : FS_E_GPU_EXECUTION, "SortBuffer of %llu bytes: %s",
+                (unsigned long long)b, cudaGetErrorString(e));
+  }
+  *out = buf;
+  return FS_OK;
+}
+
+int fs_buffer_destroy(fs_buffer* b) {
+  if (!b) return FS_OK;
+  cudaSetDevice(b->device);
+  buffer_wait(b);
+  cudaFree(b->dev);
+  cudaFreeHost(b->host);
+  cudaEventDestroy(b->done);
+  cudaGetLastError();
+  delete b;
+  return FS_OK;
+}
+
+void* fs_buffer_host(const fs_buffer* b) { return b ? b->host : nullptr; }
+void* fs_buffer_device(const fs_buffer* b) { return b ? b->dev : nullptr; }
+uint64_t fs_buffer_bytes(const fs_buffer* b) { return b ? b->bytes : 0; }
+
+int fs_buffer_host_read(fs_buffer* b) {
+  if (!b) return fail(nullptr, FS_E_INVALID, "buffer is NULL");
+  FS_CUDA(nullptr, cudaSetDevice(b->device));
+  int rc = buffer_wait(b);
+  if (rc) return rc;
+  if (b->dev_newer) FS_CUDA(nullptr, cudaMemcpy(b->host, b->dev, b->dev_newer, cudaMemcpyDeviceToHost));
+  b->dev_newer = 0;
+  return FS_OK;
+}
+
+int fs_buffer_host_write(fs_buffer* b) {
+  const int rc = fs_buffer_host_read(b);
+  if (rc) return rc;
+  b->dev_valid = 0;  // the host may change any byte: the device copy is stale
+  return FS_OK;
+}
+
+int fs_buffer_device_use(fs_buffer* b, uint64_t bytes) {
+  if (!b) return fail(nullptr, FS_E_INVALID, "buffer is NULL");
+  if (bytes > b->bytes)
+    return fail(nullptr, FS_E_INVALID, "SortBuffer holds %llu bytes, %llu requested", (unsigned long long)b->bytes,
+                (unsigned long long)bytes);
+  FS_CUDA(nullptr, cudaSetDevice(b->device));
+  // no wait: a sort still in flight only touches bytes the device already
+  // holds, and the copy below fills bytes past them
+  if (b->dev_valid < bytes) {
+    FS_CUDA(nullptr, cudaMemcpy(static_cast<char*>(b->dev) + b->dev_valid, static_cast<char*>(b->host) + b->dev_valid,
+                                bytes - b->dev_valid, cudaMemcpyHostToDevice));
+    b->dev_valid = bytes;
+  }
+  if (bytes > b->dev_newer) b->dev_newer = bytes;  // device code may write through the pointer
+  b->any_stream = true;
+  return FS_OK;
+}
+
+int fs_sort_buffer(fs_sorter* s, int dtype, fs_buffer* keys, uint64_t n, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  const uint64_t need = n * (uint64_t)key_bytes_of(dtype);
+  if ((rc = check_buffer(s, keys, need, "keys"))) return rc;
+  if (n <= 1) return FS_OK;
+  if ((rc = set_device(s))) return rc;
+  if (keys->any_stream && (rc = buffer_wait(keys))) return fail(s, rc, "%s", fs_last_error(nullptr));
+  if ((rc = buffer_to_device(s, keys, need, s->stream))) return rc;
+  if ((rc = fs_sort_keys(s, dtype, keys->dev, n, sync))) return rc;
+  return buffer_sorted(s, keys, need);
+}
+
+int fs_sort_pairs_buffer(fs_sorter* s, int dtype, fs_buffer* keys, fs_buffer* vals, uint64_t n, int sync) {
+  int rc = check_common(s, dtype, n);
+  if (rc) return rc;
+  const uint64_t kneed = n * (uint64_t)key_bytes_of(dtype), vneed = n * 4;
+  if ((rc = check_buffer(s, keys, kneed, "keys"))) return rc;
+  if ((rc = check_buffer(s, vals, vneed, "values"))) return rc;
+  if (keys == vals) return fail(s, FS_E_INVALID, "keys and values are the same SortBuffer");
+  if (n <= 1) return FS_OK;
+  if ((rc = set_device(s))) return rc;
+  for (fs_buffer* b : {keys, vals})
+    if (b->any_stream && (rc = buffer_wait(b))) return fail(s, rc, "%s", fs_last_error(nullptr));
+  if ((rc = buffer_to_device(s, keys, kneed, s->stream))) return rc;
+  if ((rc = buffer_to_device(s, vals, vneed, s->stream))) return rc;
+  if ((rc = fs_sort_pairs(s, dtype, keys->dev, static_cast<uint32_t*>(vals->dev), n, sync))) return rc;
+  if ((rc = buffer_sorted(s, keys, kneed))) return rc;
+  return buffer_sorted(s, vals, vneed);
 }
 
 uint64_t fs_scratch_bytes(const fs_sorter* s) {

@@ -72,6 +72,16 @@ SIGNATURES = {
     "fs_ipc_open": (_i32, [_vp, _vp, _pp]),
     "fs_ipc_close": (_i32, [_vp, _vp]),
     "fs_sort_keys_noalloc": (_i32, [_i32, _vp, _u64, _vp]),
+    "fs_buffer_create": (_i32, [_vp, _u64, _pp]),
+    "fs_buffer_destroy": (_i32, [_vp]),
+    "fs_buffer_host": (_vp, [_vp]),
+    "fs_buffer_device": (_vp, [_vp]),
+    "fs_buffer_bytes": (_u64, [_vp]),
+    "fs_buffer_host_read": (_i32, [_vp]),
+    "fs_buffer_host_write": (_i32, [_vp]),
+    "fs_buffer_device_use": (_i32, [_vp, _u64]),
+    "fs_sort_buffer": (_i32, [_vp, _i32, _vp, _u64, _i32]),
+    "fs_sort_pairs_buffer": (_i32, [_vp, _i32, _vp, _vp, _u64, _i32]),
     "fs_scratch_bytes": (_u64, [_vp]),
     "fs_last_launch_count": (_i32, [_vp]),
     "fs_abi_version": (_i32, []),

@@ -7,9 +7,9 @@ variants); every call goes through libforgesort.so (include/forgesort.h).
 Type mapping from the Rust API:
   &mut [u32] / &[f32] ...   -> 1-D C-contiguous numpy arrays of that dtype
   Vec<u32> (argsort result) -> numpy uint32 array
-  SortBuffer<T>             -> SortBuffer (page-locked host memory; as_slice()
-                               is a numpy view the host reads in place, and
-                               sorting copies it through HBM at PCIe rate)
+  SortBuffer<T>             -> SortBuffer (device memory + page-locked host
+                               mirror kept coherent lazily: sorts stay in HBM,
+                               as_slice() copies back only what they changed)
   MTLDevice / command queue -> CUDA device ordinal / cudaStream_t handle
   Result<_, SortError>      -> return value, or raises SortError
 """
@@ -88,20 +88,37 @@ def _check_array(a, name: str, want: str) -> np.ndarray:
 
 
 class SortBuffer:
-    """A device buffer the host can also read and write (reference
-    SortBuffer<T>, src/lib.rs:160-281).  Backed by page-locked host memory, so
-    as_slice()/as_mut_slice() are numpy views the host reads and writes at
-    full speed; sorting copies the buffer into HBM, sorts and copies it back
-    (the discrete-GPU form of the reference's unified-memory zero-copy)."""
+    """A buffer the host and the GPU share (reference SortBuffer<T>,
+    src/lib.rs:160-281): device memory plus a page-locked host mirror, kept
+    coherent lazily by the library (fs_buffer_*).  Sorting a buffer sorts the
+    device copy in place and copies nothing back, so repeated sorts of a
+    buffer the host does not touch run at device speed.  as_slice() /
+    copy_to_slice() bring the host mirror up to date first; as_mut_slice() /
+    copy_from_slice() mark the device copy stale, so the next sort copies over
+    what the host wrote.  A view returned by as_mut_slice() is a host write
+    session: call as_mut_slice() again before writing after a sort (in Rust
+    the borrow checker enforces this)."""
 
-    def __init__(self, sorter: "GpuSorter", dt: str, ptr: int, length: int, capacity: int,
+    def __init__(self, sorter: "GpuSorter", dt: str, handle: int, length: int, capacity: int,
                  owned: bool = True):
         self._sorter = sorter
         self.dtype = dt
-        self._ptr = ptr
+        self._h = handle
         self._len = length
         self._cap = capacity
         self._owned = owned
+        L = _lib.load()
+        self._host = int(L.fs_buffer_host(ctypes.c_void_p(handle)) or 0)
+        self._dev = int(L.fs_buffer_device(ctypes.c_void_p(handle)) or 0)
+
+    @property
+    def handle(self) -> int:
+        """The library's buffer object (fs_buffer*)."""
+        return self._h
+
+    def _check(self, rc: int) -> None:
+        if rc != _lib.OK:
+            raise from_status(rc, _lib.load().fs_last_error(None).decode())
 
     # -- reference accessors --------------------------------------------------
     def len(self) -> int:
@@ -120,17 +137,25 @@ class SortBuffer:
         npdt = np.dtype(_DT[self.dtype][1])
         if count == 0:
             return np.empty(0, npdt)
-        raw = (ctypes.c_uint8 * (count * npdt.itemsize)).from_address(self._ptr)
+        raw = (ctypes.c_uint8 * (count * npdt.itemsize)).from_address(self._host)
         return np.frombuffer(raw, dtype=npdt, count=count)
+
+    def _host_read(self) -> None:
+        self._sorter._host_access()
+        self._check(_lib.load().fs_buffer_host_read(ctypes.c_void_p(self._h)))
+
+    def _host_write(self) -> None:
+        self._sorter._host_access()
+        self._check(_lib.load().fs_buffer_host_write(ctypes.c_void_p(self._h)))
 
     def as_mut_slice(self) -> np.ndarray:
         """Writable view of all `capacity` elements (write, then set_len)."""
-        self._sorter._host_access()
+        self._host_write()
         return self._view(self._cap)
 
     def as_slice(self) -> np.ndarray:
         """View of the first len() elements (sorted results after a sort)."""
-        self._sorter._host_access()
+        self._host_read()
         v = self._view(self._len)
         v.flags.writeable = False
         return v
@@ -144,43 +169,51 @@ class SortBuffer:
         data = np.ascontiguousarray(data, dtype=_DT[self.dtype][1])
         if data.size > self._cap:
             raise AssertionError(f"data len {data.size} exceeds capacity {self._cap}")
-        self._sorter._host_access()
+        self._host_write()
         self._view(data.size)[:] = data
         self._len = data.size
 
     def copy_to_slice(self, dest: np.ndarray) -> None:
         n = min(self._len, dest.size)
-        self._sorter._host_access()
+        self._host_read()
         dest[:n] = self._view(n)
 
     def device_ptr(self) -> int:
-        """Device address of element 0 (replaces metal_buffer())."""
-        return self._ptr
+        """Device address of element 0 (replaces metal_buffer()), for other
+        device code: the device copy is made current for len() elements and
+        counted as written, so a later host read waits for the device."""
+        self._sorter._host_access()
+        self._check(_lib.load().fs_buffer_device_use(ctypes.c_void_p(self._h), self._len * _DT[self.dtype][2]))
+        return self._dev
 
     metal_buffer = device_ptr  # deprecated alias of the reference's accessor
 
     @classmethod
-    def from_raw_parts(cls, sorter: "GpuSorter", dt, ptr: int, length: int, capacity: int):
-        """Wrap an existing page-locked host, managed or device allocation (not owned)."""
+    def from_raw_parts(cls, sorter: "GpuSorter", dt, handle: int, length: int, capacity: int):
+        """Re-wrap a buffer object given up by into_raw_parts (owned again)."""
         if length > capacity:
             raise AssertionError(f"len {length} exceeds capacity {capacity}")
-        return cls(sorter, dtype_name(dt), ptr, length, capacity, owned=False)
+        name = dtype_name(dt)
+        if capacity * _DT[name][2] > int(_lib.load().fs_buffer_bytes(ctypes.c_void_p(handle))):
+            raise AssertionError("capacity exceeds the buffer object's size")
+        return cls(sorter, name, handle, length, capacity, owned=True)
 
     def into_raw_parts(self):
-        """Give up ownership: returns (device_ptr, len, capacity)."""
+        """Give up ownership: returns (buffer object handle, len, capacity);
+        free it with from_raw_parts(...).free() or fs_buffer_destroy."""
         self._owned = False
-        return self._ptr, self._len, self._cap
+        h, self._h = self._h, 0
+        return h, self._len, self._cap
 
     def free(self) -> None:
-        if self._owned and self._ptr:
-            self._sorter._call(_lib.load().fs_free(self._sorter._h, ctypes.c_void_p(self._ptr)))
-        self._ptr = 0
+        if self._owned and self._h:
+            _lib.load().fs_buffer_destroy(ctypes.c_void_p(self._h))
+        self._h = 0
         self._owned = False
 
     def __del__(self):
         try:
-            if self._owned and self._ptr and self._sorter._h:
-                _lib.load().fs_free(self._sorter._h, ctypes.c_void_p(self._ptr))
+            self.free()
         except Exception:
             pass
 
@@ -265,17 +298,18 @@ class GpuSorter:
     # -- zero-copy buffers (src/lib.rs:694-738, 1000-1117, 2301-2590) -----------
     def alloc_sort_buffer(self, dt, capacity: int) -> SortBuffer:
         name = dtype_name(dt)
-        ptr = ctypes.c_void_p()
-        self._call(_lib.load().fs_alloc(self._h, capacity * _DT[name][2], 1, ctypes.byref(ptr)))
-        return SortBuffer(self, name, ptr.value, 0, capacity)
+        h = ctypes.c_void_p()
+        self._call(_lib.load().fs_buffer_create(self._h, max(capacity, 1) * _DT[name][2], ctypes.byref(h)))
+        return SortBuffer(self, name, h.value, 0, capacity)
 
-    def _sort_buf(self, buf: SortBuffer, want: str) -> None:
+    def _sort_buf(self, buf: SortBuffer, want: str, sync: bool = True) -> None:
         if buf.dtype != want:
             raise TypeError(f"SortBuffer<{buf.dtype}> passed where SortBuffer<{want}> is required")
         if buf.len() <= 1:
             return
-        self._call(_lib.load().fs_sort_keys(self._h, _DT[want][0], ctypes.c_void_p(buf.device_ptr()),
-                                            buf.len(), 1))
+        self._call(_lib.load().fs_sort_buffer(self._h, _DT[want][0], ctypes.c_void_p(buf.handle), buf.len(),
+                                              int(sync)))
+        self._pending = self._pending or not sync
 
     def sort_buffer(self, buf: SortBuffer) -> None:
         self._sort_buf(buf, "u32")
@@ -303,13 +337,13 @@ class GpuSorter:
             raise LengthMismatch(keys.len(), values.len())
         if keys.len() <= 1:
             return
-        self._call(_lib.load().fs_sort_pairs(self._h, _DT[keys.dtype][0], ctypes.c_void_p(keys.device_ptr()),
-                                             ctypes.c_void_p(values.device_ptr()), keys.len(), 1))
+        self._call(_lib.load().fs_sort_pairs_buffer(self._h, _DT[keys.dtype][0], ctypes.c_void_p(keys.handle),
+                                                    ctypes.c_void_p(values.handle), keys.len(), 1))
 
     def encode_sort(self, stream, buf: SortBuffer) -> None:
         """Enqueue an in-place u32 sort of `buf` on `stream` without waiting
-        (src/lib.rs:749-785: the caller commits and waits).  Synchronise the
-        stream (or call synchronize()) before reading the buffer."""
+        (src/lib.rs:749-785: the caller commits and waits).  Reading the
+        buffer afterwards (as_slice) waits for the sort."""
         if buf.dtype != "u32":
             raise TypeError("encode_sort takes a SortBuffer<u32>")
         if buf.len() <= 1:
@@ -317,9 +351,7 @@ class GpuSorter:
         h = _stream_handle(stream)
         if h is not None:
             self.set_stream(h)
-        self._call(_lib.load().fs_sort_keys(self._h, _lib.U32, ctypes.c_void_p(buf.device_ptr()),
-                                            buf.len(), 0))
-        self._pending = True
+        self._sort_buf(buf, "u32", sync=False)
 
     # -- host slices (src/lib.rs:791-998, 2238-2485) --------------------------
     def _sort_host(self, data, want: str) -> None:

@@ -11,9 +11,10 @@
  * Reference interfaces replaced (paths inside kavanaghpatrick/gpu-forge,
  * crate metal-forge-compute/forge-sort):
  *   src/lib.rs:596-686      GpuSorter::new / with_context  -> fs_create
- *   src/lib.rs:694-706      alloc_sort_buffer              -> fs_alloc
- *   src/lib.rs:708-738      sort_buffer (+ *_buffer forms) -> fs_sort_keys
- *   src/lib.rs:749-785      encode_sort (caller encoder)   -> fs_sort_keys(sync=0)
+ *   src/lib.rs:160-281      SortBuffer<T>                  -> fs_buffer_*
+ *   src/lib.rs:694-706      alloc_sort_buffer              -> fs_buffer_create
+ *   src/lib.rs:708-738      sort_buffer (+ *_buffer forms) -> fs_sort_buffer
+ *   src/lib.rs:749-785      encode_sort (caller encoder)   -> fs_sort_buffer(sync=0)
  *   src/lib.rs:791-2590     sort_{u32,i32,f32,u64,i64,f64} -> fs_host_sort_keys
  *   src/lib.rs:1675-2825    argsort_*                      -> fs_argsort / fs_host_argsort
  *   src/lib.rs:1923-3015    sort_pairs_*                   -> fs_sort_pairs / fs_host_sort_pairs
@@ -106,6 +107,46 @@ int fs_synchronize(fs_sorter* s);
  * time: 436 ms for 1 GB measured, against ~20 ms for the copy back.) */
 int fs_alloc(fs_sorter* s, size_t bytes, int managed, void** ptr);
 int fs_free(fs_sorter* s, void* ptr);
+
+/* ---- SortBuffer objects (zero-copy at device speed) ---------------------- */
+
+/* A SortBuffer: `bytes` of device memory plus a page-locked host mirror of
+ * the same size, kept coherent lazily.  The reference's SortBuffer is one
+ * unified-memory Metal buffer that the CPU and GPU share
+ * (src/lib.rs:160-281, alloc_sort_buffer :694-706); on a discrete GPU the
+ * two copies stand in for it:
+ *   - fs_sort_buffer / fs_sort_pairs_buffer sort the device copy in place and
+ *     copy nothing back; before sorting they copy over only the leading bytes
+ *     the host changed since the device last saw them.  Repeated sorts of a
+ *     buffer the host does not touch run at device speed;
+ *   - fs_buffer_host_read makes the host mirror current (waits for the sorts
+ *     that touched the buffer, copies back what they changed): call it
+ *     before reading fs_buffer_host(b) -- as_slice / copy_to_slice;
+ *   - fs_buffer_host_write = host_read, then marks the device copy stale:
+ *     call it before writing the host mirror -- as_mut_slice /
+ *     copy_from_slice (write, then sort);
+ *   - fs_buffer_device_use hands the device copy to other device code (a
+ *     gather, a kernel of the caller's): makes its leading `bytes` current
+ *     and counts them as possibly written, so the next host read waits for
+ *     the device and copies them back.
+ * A buffer lives on the creating sorter's device and may outlive that
+ * sorter.  Buffer-only calls report errors through fs_last_error(NULL). */
+typedef struct fs_buffer fs_buffer;
+int fs_buffer_create(fs_sorter* s, uint64_t bytes, fs_buffer** out);
+int fs_buffer_destroy(fs_buffer* b);
+void* fs_buffer_host(const fs_buffer* b);
+void* fs_buffer_device(const fs_buffer* b);
+uint64_t fs_buffer_bytes(const fs_buffer* b);
+int fs_buffer_host_read(fs_buffer* b);
+int fs_buffer_host_write(fs_buffer* b);
+int fs_buffer_device_use(fs_buffer* b, uint64_t bytes);
+/* Sort the first n keys of `keys` in place on the device (sort_buffer,
+ * sort_*_buffer, encode_sort: src/lib.rs:708-785, 1000-1117, 2301-2590);
+ * sync == 0 only enqueues on the sorter's stream. */
+int fs_sort_buffer(fs_sorter* s, int dtype, fs_buffer* keys, uint64_t n, int sync);
+/* Stable pairs form over two buffers (additive: sort_pairs_buffer). */
+int fs_sort_pairs_buffer(fs_sorter* s, int dtype, fs_buffer* keys, fs_buffer* vals,
+                         uint64_t n, int sync);
 
 /* ---- device-resident sorts (zero-copy path) ----------------------------- */
 

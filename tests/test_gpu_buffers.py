@@ -216,3 +216,68 @@ def test_gather_applies_argsort_permutation(sorter, width):
     bad[123] = n
     with pytest.raises(GpuExecution):
         sorter.gather_device(width, src.data_ptr(), n, bad.data_ptr(), dst.data_ptr(), n)
+
+
+def test_sort_buffer_coherence_between_host_and_device(sorter):
+    """The device copy and the host mirror of a SortBuffer stay coherent
+    through every access pattern of the reference's shared buffer: sorts
+    without host access in between, host writes after a sort (partial, then
+    a longer len), reads after writes."""
+    n = 1 << 16
+    buf = sorter.alloc_sort_buffer("u32", n)
+    x = orc.gen("u32", n // 2, seed=31)
+    buf.copy_from_slice(x)
+    sorter.sort_buffer(buf)
+    sorter.sort_buffer(buf)  # again with no host access: stays on the device
+    assert np.array_equal(buf.as_slice(), np.sort(x))
+    # write the second half through a fresh as_mut_slice session, sort all n
+    y = orc.gen("u32", n // 2, seed=32)
+    w = buf.as_mut_slice()
+    w[n // 2:] = y
+    buf.set_len(n)
+    sorter.sort_buffer(buf)
+    assert np.array_equal(buf.as_slice(), np.sort(np.concatenate([x, y])))
+    # overwrite a few leading elements after the sort, sort again
+    w = buf.as_mut_slice()
+    w[:3] = [7, 5, 6]
+    sorter.sort_buffer(buf)
+    want = np.sort(np.concatenate([[7, 5, 6], np.sort(np.concatenate([x, y]))[3:]]).astype(np.uint32))
+    assert np.array_equal(buf.as_slice(), want)
+    # a shorter len sorts only its prefix; the rest keeps its values
+    before = buf.as_slice().copy()
+    z = np.arange(100, 0, -1, dtype=np.uint32)
+    buf.as_mut_slice()[:100] = z
+    buf.set_len(100)
+    sorter.sort_buffer(buf)
+    buf.set_len(n)
+    got = buf.as_slice()
+    assert np.array_equal(got[:100], np.sort(z)) and np.array_equal(got[100:], before[100:])
+    buf.free()
+
+
+def test_sort_buffer_raw_parts_device_use_and_lifetime():
+    """into_raw_parts / from_raw_parts round trip; device code reading and
+    writing a SortBuffer through device_ptr() (here the library's gather);
+    the buffer outliving the sorter that created it."""
+    import torch
+    from forge_sort import GpuSorter, SortBuffer
+    s = GpuSorter.new()
+    g = GpuSorter.new()
+    x = orc.gen("f64_logu", 30_000, seed=4)
+    n = x.size
+    buf = s.alloc_sort_buffer("f64", n)
+    buf.copy_from_slice(x)
+    h, ln, cap = buf.into_raw_parts()
+    buf2 = SortBuffer.from_raw_parts(s, "f64", h, ln, cap)
+    s.sort_f64_buffer(buf2)
+    want = orc.sort_keys(x, "f64")
+    ident = torch.arange(n, dtype=torch.int32, device="cuda")
+    out = torch.empty(n, dtype=torch.int64, device="cuda")
+    g.gather_device(8, buf2.device_ptr(), n, ident.data_ptr(), out.data_ptr(), n)  # device reads the buffer
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), want.view(np.uint64))
+    neg = torch.from_numpy(np.ascontiguousarray(-want).view(np.int64)).cuda()
+    g.gather_device(8, neg.data_ptr(), n, ident.data_ptr(), buf2.device_ptr(), n)  # device writes it
+    s.close()  # the buffer outlives its sorter
+    g.close()
+    assert np.array_equal(buf2.as_slice().view(np.uint64), np.ascontiguousarray(-want).view(np.uint64))
+    buf2.free()
