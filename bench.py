@@ -586,6 +586,8 @@ SUITE = [  # (config, op, dtype, generator, n)
     ("configs[4] u64", "keys", "u64", "u64", 1 << 30),
     ("configs[4] sample-sort kernels, 2 buckets", "dispatch", "u32", "u32", 1 << 28),
     ("configs[4] sample-sort kernels, 8 buckets", "dispatch", "u32", "u32", 1 << 28),
+    ("small-n single CTA (gpu-search argsort_u64 path)", "keys", "u64", "u64", 4096),
+    ("permutation apply (GpuGather) u32", "gather", "u32", "u32", 1 << 24),
 ]
 
 
@@ -696,6 +698,13 @@ def run_suite(args):
             head = out[: min(cnt[0], 1 << 20)].cpu().numpy().view(np.uint32)
             tail = out[n - min(cnt[-1], 1 << 20):].cpu().numpy().view(np.uint32)
             assert (head < spl[0]).all() and (tail >= spl[-1]).all(), "dispatch put keys in the wrong bucket"
+        elif op == "gather":  # dst[i] = src[perm[i]]: random 4-byte reads, coalesced writes
+            perm = torch.randperm(n, device=dev, dtype=torch.int64).to(torch.int32)
+            dst = torch.empty_like(kin)
+            ms = timed(lambda: sorter.gather_device(4, kin.data_ptr(), n, perm.data_ptr(), dst.data_ptr(), n,
+                                                    sync=False), reps)
+            bpk = 12  # index read + source read + destination write
+            assert torch.equal(dst[:1000], kin[perm[:1000].to(torch.int64)])
         elif op == "argsort":
             idx = torch.empty(n, dtype=torch.int32, device=dev)
             ms = timed(lambda: sorter.argsort_device(dt, kin.data_ptr(), idx.data_ptr(), n, sync=False), reps)

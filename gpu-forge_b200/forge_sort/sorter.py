@@ -491,7 +491,7 @@ class GpuSorter:
     def set_kernel_timing(self, on: bool) -> None:
         self._call(_lib.load().fs_set_kernel_timing(self._h, int(on)))
 
-    def last_kernel_times(self, cap: int = 16):
+    def last_kernel_times(self, cap: int = 24):
         """Per-kernel device times (ms) of the last sort, launch order:
         histogram, plan, pass 0..P-1, finalize."""
         buf = (ctypes.c_float * cap)()
