@@ -33,6 +33,8 @@
 
 #include "fs_device.cuh"
 
+#include <type_traits>
+
 #ifndef FS_RANK_BALLOT
 #define FS_RANK_BALLOT 3
 #endif
@@ -114,7 +116,11 @@ struct RadixDigit {
   }
 };
 
-template <typename K, int XF>
+// LV: how the splitter search runs.  1, 2, 3: a fixed lower-bound tree of that
+// many levels over 1, 3 or 7 splitters held in registers (2, 4 or 8 GPUs;
+// unused entries hold the largest key); 0: a binary search over the
+// shared-memory copy, for any count up to 255.
+template <typename K, int XF, int LV = 3>
 struct SplitterDigit {
   const K* keys;         // nsplit raw splitter keys, ascending by (key, gpos)
   const uint64_t* gpos;  // their global positions
@@ -123,33 +129,58 @@ struct SplitterDigit {
   const K* s_keys = nullptr;
   const uint64_t* s_gpos = nullptr;
   uint32_t top = 0;  // largest power of two <= nsplit (0 if none)
-  K r[7] = {};       // up to 7 splitters (8 GPUs) in registers, padded with the largest key
+  K r[7] = {};       // up to 7 splitters in registers, padded with the largest key
   static constexpr int DIGITS = RADIX;
   static constexpr bool STAGE = true;  // digits staged in shared memory
   static constexpr bool DISPATCH = false;
+  static_assert(LV >= 0 && LV <= 3, "register tree of at most 3 levels");
   // Number of splitters <= (k, g) in (ordered key, position) order.  First
-  // the splitters whose key is below k: a branch-free lower bound over the
-  // shared-memory copy, log2(nsplit) + 1 steps, the same for every lane.
-  // Then, only for a key equal to splitter keys (rare but possible: heavy
-  // duplicates), the positions break the tie.
-  __device__ __forceinline__ uint32_t operator()(K k, uint64_t g) const {
-    __builtin_assume(__isShared(s_keys) && __isShared(s_gpos));
+  // the splitters whose key is below k (lower bound); the search also yields
+  // the first splitter key >= k, so a tie -- a key equal to a splitter key,
+  // rare but possible with heavy duplicates -- is seen without another load,
+  // and only then are positions compared.  gpos_of() returns the key's
+  // global position and runs on that path only.
+  template <typename G>
+  __device__ __forceinline__ uint32_t operator()(K k, G&& gpos_of) const {
     uint32_t pos = 0;
-    if (top <= 4) {
-      // up to 7 splitters (8 GPUs): three fixed steps over registers, whose
-      // entries nsplit..6 hold the largest key (never below k)
-      pos = r[3] < k ? 4u : 0u;
-      pos += (pos ? r[5] : r[1]) < k ? 2u : 0u;
-      const K m0 = (pos & 4) ? ((pos & 2) ? r[6] : r[4]) : ((pos & 2) ? r[2] : r[0]);
-      pos += m0 < k ? 1u : 0u;
+    K cand = ~K(0);  // smallest splitter key >= k seen by the search
+    if constexpr (LV == 1) {
+      const bool right = r[0] < k;
+      pos = right ? 1u : 0u;
+      cand = right ? cand : r[0];
+    } else if constexpr (LV == 2) {
+      bool right = r[1] < k;
+      pos = right ? 2u : 0u;
+      cand = right ? cand : r[1];
+      const K m = right ? r[2] : r[0];
+      right = m < k;
+      pos += right ? 1u : 0u;
+      cand = right ? cand : m;
+    } else if constexpr (LV == 3) {
+      bool right = r[3] < k;
+      pos = right ? 4u : 0u;
+      cand = right ? cand : r[3];
+      K m = right ? r[5] : r[1];
+      right = m < k;
+      pos += right ? 2u : 0u;
+      cand = right ? cand : m;
+      m = (pos & 4) ? ((pos & 2) ? r[6] : r[4]) : ((pos & 2) ? r[2] : r[0]);
+      right = m < k;
+      pos += right ? 1u : 0u;
+      cand = right ? cand : m;
     } else {
+      __builtin_assume(__isShared(s_keys));
       for (uint32_t step = top; step != 0; step >>= 1) {
         const uint32_t j = pos + step - 1;
         if (j < (uint32_t)nsplit && s_keys[j] < k) pos += step;
       }
+      cand = pos < (uint32_t)nsplit ? s_keys[pos] : ~K(0);
     }
-    if (pos < (uint32_t)nsplit && s_keys[pos] == k)
+    if (cand == k && pos < (uint32_t)nsplit) {
+      __builtin_assume(__isShared(s_keys) && __isShared(s_gpos));
+      const uint64_t g = gpos_of();
       while (pos < (uint32_t)nsplit && s_keys[pos] == k && s_gpos[pos] <= g) ++pos;
+    }
     return pos;
   }
   // Copy the splitters (ordered) into shared memory (at least 8 entries,
@@ -169,6 +200,11 @@ struct SplitterDigit {
   }
 };
 
+// Register-tree depth for nsplit splitters (0: shared-memory search).
+__host__ __device__ constexpr int splitter_levels(int nsplit) {
+  return nsplit <= 1 ? 1 : nsplit <= 3 ? 2 : nsplit <= 7 ? 3 : 0;
+}
+
 // Sample-sort dispatch: the splitter bucket is the digit, and bucket b's keys
 // go to dst[b] -- this rank's region of rank b's inbox, which may be another
 // GPU's memory reached with plain stores over NVLink -- at their stable rank
@@ -177,8 +213,8 @@ struct SplitterDigit {
 // (tile counters and scans sized for 8 digits, ranking by three ballots);
 // 256 covers any splitter count.
 // With a payload, value i goes to vdst[b] at the same position as key i.
-template <typename K, int XF, int NB = RADIX>
-struct SplitterDispatch : SplitterDigit<K, XF> {
+template <typename K, int XF, int NB = RADIX, int LV = 3>
+struct SplitterDispatch : SplitterDigit<K, XF, LV> {
   static constexpr int DIGITS = NB;
   static constexpr bool DISPATCH = true;
   K* const* dst;          // device array of nsplit + 1 key destinations
@@ -303,10 +339,17 @@ __global__ void __launch_bounds__(BLOCK)
 // bucket, so the warp counts each bucket with one ballot instead of 32
 // same-address atomics.
 // --------------------------------------------------------------------------
-template <typename K, int XF, int BLOCK, typename D>
+// PACK: how a thread counts.  2 (one splitter): the number of keys in
+// bucket 1 (bucket 0 is the rest of the slice); 4 / 8 (up to 3 / 7
+// splitters): one add per key into 8-bit fields of a 32- / 64-bit register,
+// folded every 250 or so keys into 16-bit fields (a thread sees fewer than
+// 2^16 keys of a slice), summed by the warp once per slice; 0: one
+// shared-memory atomic per key.
+template <typename K, int XF, int BLOCK, typename D, int PACK>
 __global__ void __launch_bounds__(BLOCK)
     k_bucket_hist(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
                   uint32_t* __restrict__ counts, const D dfn_in, const uint64_t gpos_base) {
+  static_assert(PACK == 0 || PACK == 2 || PACK == 4 || PACK == 8, "counting mode");
   constexpr int KV = 16 / (int)sizeof(K);  // keys per 16-byte load
   __shared__ uint32_t h[RADIX];
   __shared__ uint32_t tot[RADIX];
@@ -314,22 +357,33 @@ __global__ void __launch_bounds__(BLOCK)
   __shared__ uint64_t s_spg[RADIX];
   D dfn = dfn_in;
   dfn.stage_in(s_spk, s_spg);
-  const uint32_t nb = (uint32_t)dfn.nsplit + 1, lane = threadIdx.x & 31;
+  const uint32_t lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < RADIX; i += BLOCK) h[i] = tot[i] = 0;
   __syncthreads();
-  // Up to 8 buckets (one per GPU of a box): each thread counts in eight
-  // 16-bit fields of two registers and the warp adds them up once per slice
-  // (a thread sees at most keys_per_slice / BLOCK < 2^16 keys of a slice).
-  const bool packed = nb <= 8 && sl.keys_per_slice / BLOCK < 60000;
-  uint64_t c01 = 0, c23 = 0;  // buckets 0-3 and 4-7, 16 bits each
-  auto add = [&](uint32_t b, bool valid) {
-    if (packed) {
-      const uint64_t one = valid ? 1ull << (16 * (b & 3)) : 0ull;
-      if (b < 4) c01 += one; else c23 += one;
-    } else if (valid) {
+  using C8 = typename std::conditional<PACK == 8, uint64_t, uint32_t>::type;
+  constexpr C8 EVEN = (C8)0x00ff00ff00ff00ffull;  // the 8-bit fields of even buckets, as 16-bit fields
+  uint32_t c1 = 0;          // PACK 2: keys of bucket 1
+  C8 c8 = 0;                // PACK 4 / 8: bucket b in bits [8b, 8b+8)
+  C8 w_even = 0, w_odd = 0;  // 16-bit fields: buckets 0, 2, (4, 6) and 1, 3, (5, 7)
+  auto add = [&](uint32_t b) {
+    if constexpr (PACK == 2) {
+      c1 += b;
+    } else if constexpr (PACK == 4 || PACK == 8) {
+      c8 += (C8)1 << (8 * b);
+    } else {
       atomicAdd(&h[b], 1u);
     }
   };
+  auto fold = [&]() {  // 8-bit fields -> 16-bit fields, before any can reach 256
+    if constexpr (PACK == 4 || PACK == 8) {
+      w_even += c8 & EVEN;
+      w_odd += (c8 >> 8) & EVEN;
+      c8 = 0;
+    }
+  };
+  // keys a thread adds between folds: 2*KV per main-loop step, at most
+  // KV + 1 more after the loop, never 256
+  constexpr int FOLD_STEPS = (255 - KV - 1) / (2 * KV);
   const bool vec = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
   for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
     const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
@@ -342,34 +396,50 @@ __global__ void __launch_bounds__(BLOCK)
       const uint4* kv = reinterpret_cast<const uint4*>(keys + lo);
       const uint32_t nv = len / KV;
       uint32_t v = threadIdx.x;
+      int steps = 0;
       for (; v + BLOCK < nv; v += 2 * BLOCK) {
+        if (++steps == FOLD_STEPS) {
+          fold();
+          steps = 0;
+        }
         const uint4 a0 = __ldcs(kv + v), a1 = __ldcs(kv + v + BLOCK);
         const K* k0 = reinterpret_cast<const K*>(&a0);
         const K* k1 = reinterpret_cast<const K*>(&a1);
 #pragma unroll
-        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k0[q]), g0 + v * KV + q), true);
+        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k0[q]), [&] { return g0 + (uint64_t)(v * KV + q); }));
 #pragma unroll
-        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k1[q]), g0 + (v + BLOCK) * KV + q), true);
+        for (int q = 0; q < KV; ++q)
+          add(dfn(to_ordered<K, XF>(k1[q]), [&] { return g0 + (uint64_t)((v + BLOCK) * KV + q); }));
       }
       for (; v < nv; v += BLOCK) {
         const uint4 a0 = __ldcs(kv + v);
         const K* k0 = reinterpret_cast<const K*>(&a0);
 #pragma unroll
-        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k0[q]), g0 + v * KV + q), true);
+        for (int q = 0; q < KV; ++q) add(dfn(to_ordered<K, XF>(k0[q]), [&] { return g0 + (uint64_t)(v * KV + q); }));
       }
       done = nv * KV;
     }
-    for (uint32_t i = done + threadIdx.x; i < len; i += BLOCK) add(dfn(to_ordered<K, XF>(keys[lo + i]), g0 + i), true);
-    if (packed) {
+    for (uint32_t i = done + threadIdx.x; i < len; i += BLOCK)
+      add(dfn(to_ordered<K, XF>(keys[lo + i]), [&] { return g0 + i; }));
+    if constexpr (PACK == 2) {
+      const uint32_t v = __reduce_add_sync(0xffffffffu, c1);
+      if (lane == 0 && v) atomicAdd(&h[1], v);
+      c1 = 0;
+    } else if constexpr (PACK != 0) {
+      fold();
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t v = (uint32_t)(((q < 4 ? c01 : c23) >> (16 * (q & 3))) & 0xffffu);
+      for (int q = 0; q < PACK; ++q) {
+        uint32_t v = (uint32_t)(((q & 1 ? w_odd : w_even) >> (16 * (q >> 1))) & 0xffffu);
         v = __reduce_add_sync(0xffffffffu, v);
         if (lane == 0 && v) atomicAdd(&h[q], v);
       }
-      c01 = c23 = 0;
+      w_even = w_odd = 0;
     }
     __syncthreads();
+    if constexpr (PACK == 2) {
+      if (threadIdx.x == 0) h[0] = len - h[1];
+      __syncthreads();
+    }
     uint32_t* out = counts + (size_t)c * RADIX;
     for (int q = threadIdx.x; q < RADIX; q += BLOCK) {
       const uint32_t v = h[q];
@@ -708,7 +778,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
-      const uint32_t d = valid ? dfn(key[k], gbase + wofs + k * 32) : 0u;
+      const uint32_t d = valid ? dfn(key[k], [&] { return gbase + wofs + k * 32; }) : 0u;
       dpk[k >> 2] |= d << (8 * (k & 3));
     }
   }

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <unordered_map>
 
 using namespace fs;
@@ -606,14 +607,39 @@ int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
 }
 
 // ---- sample-sort partition --------------------------------------------------
+// The bucket count with the splitter search and counting mode fitted to the
+// splitter count (register trees of 1-3 levels for 2-8 buckets, packed
+// per-thread counters while a thread sees fewer than 2^16 keys of a slice).
+template <typename K, int XF>
+void launch_bucket_hist(const Exec& e, const Slices& sl, const void* keys, uint64_t n, const void* spl_keys,
+                        const uint64_t* spl_gpos, int nsplit, uint64_t gpos_base) {
+  const bool packed = sl.keys_per_slice / HIST_BLOCK < 60000;
+  const unsigned grid = stream_grid(e, sl);
+  auto go = [&](auto lv, auto pack) {
+    using D = SplitterDigit<K, XF, decltype(lv)::value>;
+    const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
+    k_bucket_hist<K, XF, HIST_BLOCK, D, decltype(pack)::value><<<grid, HIST_BLOCK, 0, e.stream>>>(
+        static_cast<const K*>(keys), n, e.ctl, sl, e.counts, dfn, gpos_base);
+  };
+  using std::integral_constant;
+  if (nsplit <= 1 && packed)
+    go(integral_constant<int, 1>{}, integral_constant<int, 2>{});
+  else if (nsplit <= 3 && packed)
+    go(integral_constant<int, 2>{}, integral_constant<int, 4>{});
+  else if (nsplit <= 7 && packed)
+    go(integral_constant<int, 3>{}, integral_constant<int, 8>{});
+  else if (nsplit <= 7)
+    go(integral_constant<int, 3>{}, integral_constant<int, 0>{});
+  else
+    go(integral_constant<int, 0>{}, integral_constant<int, 0>{});
+}
+
 // One stable pass that moves every key to the splitter bucket its (ordered
 // key, global position) falls in: the same slice / count / scatter machinery
 // as a radix pass, with the bucket index as the digit.
 template <typename K, int XF>
 int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_t n, uint64_t gpos_base,
                       const void* spl_keys, const uint64_t* spl_gpos, int nsplit, unsigned long long* counts_out) {
-  using D = SplitterDigit<K, XF>;
-  const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
   s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
   Exec e = exec_of(s);
   const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
@@ -633,11 +659,19 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
   a.counts_out = counts_out;
   a.ncounts = nsplit + 1;
   FS_CUDA(s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
-  k_bucket_hist<K, XF, HIST_BLOCK, D><<<stream_grid(e, sl), HIST_BLOCK, 0, e.stream>>>(
-      static_cast<const K*>(keys_in), n, e.ctl, sl, e.counts, dfn, gpos_base);
+  launch_bucket_hist<K, XF>(e, sl, keys_in, n, spl_keys, spl_gpos, nsplit, gpos_base);
   k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
   k_slice_scan<<<SCAN_GROUPS, SCAN_WARPS * 32, 0, e.stream>>>(e.ctl, 0, sl, e.counts, e.offsets, 0);
-  if ((rc = launch_scatter<K, false, XF, PartCfg<K>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base))) return rc;
+  if (nsplit <= 7) {
+    using D = SplitterDigit<K, XF, 3>;
+    const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
+    rc = launch_scatter<K, false, XF, PartCfg<K>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base);
+  } else {
+    using D = SplitterDigit<K, XF, 0>;
+    const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
+    rc = launch_scatter<K, false, XF, PartCfg<K>, SCATTER_ANY>(e, 0, n, sl, dfn, gpos_base);
+  }
+  if (rc) return rc;
   uint64_t fb = (n + 255) / 256;
   const uint64_t fcap = (uint64_t)e.sm_count * 4;
   k_finalize<K><<<(unsigned)(fb < fcap ? fb : fcap), 256, 0, e.stream>>>(e.ctl, n, e.err_out);
@@ -655,8 +689,6 @@ template <typename K, int XF>
 int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t gpos_base, const void* spl_keys,
                             const uint64_t* spl_gpos, int nsplit, unsigned long long* host_counts,
                             unsigned long long* dev_counts = nullptr) {
-  using D = SplitterDigit<K, XF>;
-  const D dfn{static_cast<const K*>(spl_keys), spl_gpos, nsplit};
   Exec e = exec_of(s);
   const Slices sl = make_slices(e, n, tile_of<StableCfg<K, false>>());
   int rc = ensure_slice_buffers(s, sl);
@@ -665,8 +697,7 @@ int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t
   s->ev_used = 0;
   FS_CUDA(s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
   t_begin(e);
-  k_bucket_hist<K, XF, HIST_BLOCK, D><<<stream_grid(e, sl), HIST_BLOCK, 0, e.stream>>>(
-      static_cast<const K*>(keys), n, e.ctl, sl, e.counts, dfn, gpos_base);
+  launch_bucket_hist<K, XF>(e, sl, keys, n, spl_keys, spl_gpos, nsplit, gpos_base);
   t_end(e);
   FS_CUDA(s, cudaGetLastError());
   if (!host_counts) {
@@ -706,11 +737,11 @@ __global__ void __launch_bounds__(RADIX)
 
 // dst_host / vdst_host: destinations from the host (copied into the table);
 // nullptr: the table was already written on the device (k_dispatch_table).
-template <typename K, int XF, int NB, bool VALS>
+template <typename K, int XF, int NB, int LV, bool VALS>
 int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t* vals, uint64_t n,
                                   uint64_t gpos_base, const void* spl_keys, const uint64_t* spl_gpos, int nsplit,
                                   void* const* dst_host, uint32_t* const* vdst_host) {
-  using D = SplitterDispatch<K, XF, NB>;
+  using D = SplitterDispatch<K, XF, NB, LV>;
   D dfn{};
   dfn.keys = static_cast<const K*>(spl_keys);
   dfn.gpos = spl_gpos;
@@ -761,23 +792,22 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t
   return FS_OK;
 }
 
-// Up to 8 buckets (the GPUs of one box) take the 8-digit instantiation.
+// Up to 8 buckets (the GPUs of one box) take the 8-digit instantiation, with
+// the splitters in registers (one compare for 2 buckets, a 3-level tree for
+// up to 8); more buckets search the shared-memory copy.
 template <typename K, int XF>
 int enqueue_partition_dispatch(fs_sorter* s, const void* keys, const uint32_t* vals, bool with_vals, uint64_t n,
                                uint64_t gpos_base, const void* spl_keys, const uint64_t* spl_gpos, int nsplit,
                                void* const* dst_host, uint32_t* const* vdst_host) {
-  if (with_vals) {
-    if (nsplit < 8)
-      return enqueue_partition_dispatch_nb<K, XF, 8, true>(s, keys, vals, n, gpos_base, spl_keys, spl_gpos, nsplit,
-                                                           dst_host, vdst_host);
-    return enqueue_partition_dispatch_nb<K, XF, RADIX, true>(s, keys, vals, n, gpos_base, spl_keys, spl_gpos, nsplit,
-                                                             dst_host, vdst_host);
-  }
-  if (nsplit < 8)
-    return enqueue_partition_dispatch_nb<K, XF, 8, false>(s, keys, nullptr, n, gpos_base, spl_keys, spl_gpos, nsplit,
-                                                          dst_host, nullptr);
-  return enqueue_partition_dispatch_nb<K, XF, RADIX, false>(s, keys, nullptr, n, gpos_base, spl_keys, spl_gpos,
-                                                            nsplit, dst_host, nullptr);
+#define FS_DISPATCH_NB(NB, LV)                                                                                     \
+  (with_vals ? enqueue_partition_dispatch_nb<K, XF, NB, LV, true>(s, keys, vals, n, gpos_base, spl_keys, spl_gpos, \
+                                                                   nsplit, dst_host, vdst_host)                   \
+             : enqueue_partition_dispatch_nb<K, XF, NB, LV, false>(s, keys, nullptr, n, gpos_base, spl_keys,      \
+                                                                    spl_gpos, nsplit, dst_host, nullptr))
+  if (nsplit <= 1) return FS_DISPATCH_NB(8, 1);
+  if (nsplit < 8) return FS_DISPATCH_NB(8, 3);
+  return FS_DISPATCH_NB(RADIX, 0);
+#undef FS_DISPATCH_NB
 }
 
 int finish(fs_sorter* s, int sync) {
