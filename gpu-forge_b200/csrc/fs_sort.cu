@@ -6,6 +6,7 @@
 // on that stream (P = key bytes), with no host round trip in between.
 #include "forgesort.h"
 #include "forgesort_bench.h"
+#include "fs_coop.cuh"
 #include "fs_hoststage.h"
 #include "fs_kernels.cuh"
 
@@ -43,6 +44,8 @@ struct fs_sorter {
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
   void* dst_tab = nullptr;  // sample-sort dispatch: 256 destination pointers
+  uint64_t coop_max_bytes = 8ull << 20;  // keys-only sorts up to this many key bytes run as one
+                                         // cooperative launch (FORGESORT_COOP_MAX_BYTES; 0: off)
   uint32_t small_max = SMALL_N_MAX;  // single-CTA sorts up to this n (FORGESORT_SMALL_SORT);
                                      // with a payload up to min(small_max, SMALL_N_PAYLOAD_MAX)
   // fs_host_sort_keys_copy_async: two device buffers used in turn, and copy
@@ -589,11 +592,82 @@ int dispatch_small(fs_sorter* s, int dtype, const PlanArgs& a) {
   }
 }
 
+// Keys-only sorts of up to a few million keys: the whole sort in one
+// cooperative launch (k_coop_sort), one CTA per slice, all resident.
+template <typename K, int XF>
+int enqueue_coop(fs_sorter* s, const PlanArgs& a) {
+  constexpr int BLOCK = 256, IPT = 16, P = (int)sizeof(K);
+  using Ly = ScatterLayout<K, false, BLOCK, IPT, false, RADIX>;
+  auto kern = k_coop_sort<K, XF, BLOCK, IPT>;
+  static std::atomic<int> bps_dev[MAX_DEVICES];  // resident CTAs per SM, 0 = not configured yet
+  if (s->device < 0 || s->device >= MAX_DEVICES)
+    return fail(s, FS_E_INVALID, "device %d outside [0, %d)", s->device, MAX_DEVICES);
+  int bps = bps_dev[s->device].load();
+  if (bps == 0) {
+    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES));
+    bps = blocks_per_sm(s, kern, BLOCK, Ly::BYTES);
+    if (bps < 0) return -bps;
+    bps_dev[s->device].store(bps);
+  }
+  const uint64_t tile = (uint64_t)BLOCK * IPT;
+  const uint64_t ntiles = (a.n + tile - 1) / tile;
+  const uint64_t cap = (uint64_t)bps * s->sm_count;
+  const uint64_t want = ntiles < cap ? ntiles : cap;
+  const uint64_t tps = (ntiles + want - 1) / want;  // tiles per slice
+  Slices sl{};
+  sl.keys_per_slice = tps * tile;
+  sl.count = (uint32_t)((ntiles + tps - 1) / tps);
+  const uint32_t groups = (sl.count + COOP_GROUP - 1) / COOP_GROUP;
+  const size_t grp_bytes = (size_t)P * groups * RADIX * 4;
+  int rc = grow(s, &s->counts, &s->counts_bytes, (size_t)sl.count * RADIX * 4, false);
+  if (!rc) rc = grow(s, &s->offsets, &s->offsets_bytes, grp_bytes, false);
+  if (rc) return rc;
+  FS_CUDA(s, cudaMemsetAsync(s->ctl, 0, CTL_ACCUM_BYTES, s->stream));
+  FS_CUDA(s, cudaMemsetAsync(&s->ctl->err, 0, sizeof(int), s->stream));
+  FS_CUDA(s, cudaMemsetAsync(s->offsets, 0, grp_bytes, s->stream));
+  CoopArgs ca{};
+  ca.kin = a.kin;
+  ca.kfinal = a.kfinal;
+  ca.kother = a.kother;
+  ca.n = a.n;
+  ca.ctl = s->ctl;
+  ca.counts = static_cast<uint32_t*>(s->counts);
+  ca.grp = static_cast<uint32_t*>(s->offsets);
+  ca.sl = sl;
+  ca.groups = groups;
+  ca.timeout_ns = s->timeout_ns;
+  ca.host_err = s->host_err_dev;
+  void* params[] = {&ca};
+  Exec e = exec_of(s);
+  s->ev_used = 0;
+  t_begin(e);
+  FS_CUDA(s, cudaLaunchCooperativeKernel((const void*)kern, dim3(sl.count), dim3(BLOCK), params, Ly::BYTES,
+                                         s->stream));
+  t_end(e);
+  s->last_launches = 1;
+  return FS_OK;
+}
+
+int dispatch_coop(fs_sorter* s, int dtype, const PlanArgs& a) {
+  switch (dtype) {
+    case FS_U32: return enqueue_coop<uint32_t, XF_NONE>(s, a);
+    case FS_I32: return enqueue_coop<uint32_t, XF_SIGN>(s, a);
+    case FS_F32: return enqueue_coop<uint32_t, XF_FLOAT>(s, a);
+    case FS_U64: return enqueue_coop<uint64_t, XF_NONE>(s, a);
+    case FS_I64: return enqueue_coop<uint64_t, XF_SIGN>(s, a);
+    case FS_F64: return enqueue_coop<uint64_t, XF_FLOAT>(s, a);
+    default: return fail(s, FS_E_INVALID, "unknown dtype %d", dtype);
+  }
+}
+
 // The sorter's path: size the slices, grow its scratch, enqueue.
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
   const uint32_t small_cap = a.has_vals && s->small_max > SMALL_N_PAYLOAD_MAX ? SMALL_N_PAYLOAD_MAX : s->small_max;
   if (a.n <= small_cap) return dispatch_small(s, dtype, a);
+  if (!a.has_vals && a.unstable_first && !s->test_withhold &&
+      a.n * (uint64_t)key_bytes_of(dtype) <= s->coop_max_bytes)
+    return dispatch_coop(s, dtype, a);
   Exec e = exec_of(s);
   const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);
   int rc = ensure_slice_buffers(s, sl);
@@ -926,6 +1000,10 @@ int fs_create(int device, void* stream, fs_sorter** out) {
     s->small_max = v <= 0 ? 0u : (uint32_t)(v < (long long)SMALL_N_MAX ? v : SMALL_N_MAX);
   }
   s->timeout_ns = wait_timeout_ns_env();
+  if (const char* t = getenv("FORGESORT_COOP_MAX_BYTES")) {  // bytes of keys; 0: never one launch
+    const long long v = atoll(t);
+    s->coop_max_bytes = v <= 0 ? 0ull : (uint64_t)v;
+  }
   *out = s;
   return FS_OK;
 }
@@ -1719,6 +1797,12 @@ int fs_set_wait_timeout_ms(fs_sorter* s, uint64_t ms) {
   if (ms == 0 || ms > 3600000ull) return fail(s, FS_E_INVALID, "wait timeout %llu ms outside [1, 3600000]",
                                              (unsigned long long)ms);
   s->timeout_ns = ms * 1000000ull;
+  return FS_OK;
+}
+
+int fs_set_single_launch_max(fs_sorter* s, uint64_t key_bytes) {
+  if (!s) return FS_E_INVALID;
+  s->coop_max_bytes = key_bytes;
   return FS_OK;
 }
 

@@ -90,6 +90,7 @@ SIGNATURES = {
 BENCH_SIGNATURES = {
     "fs_generate": (_i32, [_i32, _u64, _u64, _u64, _vp, _vp]),
     "fs_set_wait_timeout_ms": (_i32, [_vp, _u64]),
+    "fs_set_single_launch_max": (_i32, [_vp, _u64]),
     "fs_test_inject": (_i32, [_vp, _i32, _i32]),
 }
 TEST_WITHHOLD_COPY, TEST_FAIL_ALLOC = 1, 2

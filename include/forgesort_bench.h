@@ -42,6 +42,12 @@ int fs_generate(int dist, uint64_t seed, uint64_t start, uint64_t n, void* out,
  * that the call fails with the right status and that the sorter works again
  * afterwards. */
 
+/* Keys-only sorts whose keys take at most `key_bytes` bytes (and more than
+ * the single-CTA limit) run as one cooperative launch instead of the chain of
+ * 2 + 3P kernels; 0 always uses the chain.  fs_create takes the limit from
+ * FORGESORT_COOP_MAX_BYTES (default 8 MiB: 2^21 four-byte keys). */
+int fs_set_single_launch_max(fs_sorter* s, uint64_t key_bytes);
+
 /* Bound on every device-side wait of this sorter (the mbarrier waits of the
  * scatter's bulk copies), in milliseconds (> 0).  fs_create takes it from
  * FORGESORT_WAIT_TIMEOUT_MS (default 2000). */

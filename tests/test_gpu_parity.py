@@ -102,3 +102,48 @@ def test_deterministic_repeat(sorter):
     a = sorter.argsort_u32(x)
     b = sorter.argsort_u32(x)
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("n", [8193, 65_537, 1 << 20, (1 << 21) - 5])
+@pytest.mark.parametrize("dt,dist", DT_DIST, ids=[d for d, _ in DT_DIST])
+def test_single_launch_matches_chain_and_oracle(dt, dist, n):
+    """Keys-only sorts up to 8 MiB of keys run as one cooperative launch
+    (k_coop_sort): bit-exact against the oracle and the chained kernels, in
+    place and out of place, including inputs with skipped passes."""
+    import torch
+    from forge_sort import GpuSorter
+    kb = 8 if dt in ("u64", "i64", "f64") else 4
+    if n * kb > (8 << 20):
+        n = (8 << 20) // kb - 3
+    x = orc.gen(dist, n, seed=4000 + n)
+    xb = bits(x, dt)
+    want = bits(orc.sort_keys(x, dt), dt)
+    iv = np.int32 if kb == 4 else np.int64
+    one = GpuSorter.new()
+    chain = GpuSorter.new()
+    chain.set_single_launch_max(0)
+    try:
+        for s in (one, chain):
+            a = torch.from_numpy(xb.view(iv).copy()).cuda()
+            s.sort_device(dt, a.data_ptr(), n)  # in place
+            assert np.array_equal(a.cpu().numpy().view(xb.dtype), want)
+            b = torch.from_numpy(xb.view(iv).copy()).cuda()
+            out = torch.empty_like(b)
+            s.sort_device_copy(dt, b.data_ptr(), out.data_ptr(), n)
+            assert np.array_equal(out.cpu().numpy().view(xb.dtype), want)
+            assert np.array_equal(b.cpu().numpy().view(xb.dtype), xb)  # input untouched
+        assert one.last_launch_count() == 1
+        # low bits only vary: odd and even numbers of executed passes
+        for mask_bits in (8, 16, 24):
+            y = (xb & xb.dtype.type((1 << mask_bits) - 1)).view(orc.NP_DTYPE[dt])
+            a = torch.from_numpy(np.ascontiguousarray(y).view(iv).copy()).cuda()
+            one.sort_device(dt, a.data_ptr(), n)
+            assert np.array_equal(a.cpu().numpy().view(xb.dtype), bits(orc.sort_keys(y, dt), dt)), mask_bits
+        z = np.full(n, 7, orc.NP_DTYPE[dt])  # nothing varies
+        a = torch.from_numpy(np.ascontiguousarray(z).view(iv).copy()).cuda()
+        out = torch.empty_like(a)
+        one.sort_device_copy(dt, a.data_ptr(), out.data_ptr(), n)
+        assert np.array_equal(out.cpu().numpy().view(xb.dtype), bits(z, dt))
+    finally:
+        one.close()
+        chain.close()
