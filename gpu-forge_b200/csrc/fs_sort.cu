@@ -44,8 +44,8 @@ struct fs_sorter {
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
   void* dst_tab = nullptr;  // sample-sort dispatch: 256 destination pointers
-  uint64_t coop_max_bytes = 8ull << 20;  // keys-only sorts up to this many key bytes run as one
-                                         // cooperative launch (FORGESORT_COOP_MAX_BYTES; 0: off)
+  uint64_t coop_max_bytes = 2ull << 20;  // keys-only 32-bit sorts up to this many key bytes run as
+                                         // one cooperative launch (FORGESORT_COOP_MAX_BYTES; 0: off)
   uint32_t small_max = SMALL_N_MAX;  // single-CTA sorts up to this n (FORGESORT_SMALL_SORT);
                                      // with a payload up to min(small_max, SMALL_N_PAYLOAD_MAX)
   // fs_host_sort_keys_copy_async: two device buffers used in turn, and copy
@@ -653,10 +653,7 @@ int dispatch_coop(fs_sorter* s, int dtype, const PlanArgs& a) {
     case FS_U32: return enqueue_coop<uint32_t, XF_NONE>(s, a);
     case FS_I32: return enqueue_coop<uint32_t, XF_SIGN>(s, a);
     case FS_F32: return enqueue_coop<uint32_t, XF_FLOAT>(s, a);
-    case FS_U64: return enqueue_coop<uint64_t, XF_NONE>(s, a);
-    case FS_I64: return enqueue_coop<uint64_t, XF_SIGN>(s, a);
-    case FS_F64: return enqueue_coop<uint64_t, XF_FLOAT>(s, a);
-    default: return fail(s, FS_E_INVALID, "unknown dtype %d", dtype);
+    default: return fail(s, FS_E_INVALID, "single-launch sort: 32-bit keys only (dtype %d)", dtype);
   }
 }
 
@@ -665,8 +662,11 @@ int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
   const uint32_t small_cap = a.has_vals && s->small_max > SMALL_N_PAYLOAD_MAX ? SMALL_N_PAYLOAD_MAX : s->small_max;
   if (a.n <= small_cap) return dispatch_small(s, dtype, a);
-  if (!a.has_vals && a.unstable_first && !s->test_withhold &&
-      a.n * (uint64_t)key_bytes_of(dtype) <= s->coop_max_bytes)
+  // measured on one B200 (device time per call): one launch 58-65 us against
+  // 75 us chained for 2^14..2^19 u32 keys; slower from 2^20 (82 vs 78 us) and
+  // for 64-bit keys at every size (8 passes: twice the grid barriers)
+  if (!a.has_vals && a.unstable_first && !s->test_withhold && key_bytes_of(dtype) == 4 &&
+      a.n * 4 <= s->coop_max_bytes)
     return dispatch_coop(s, dtype, a);
   Exec e = exec_of(s);
   const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);

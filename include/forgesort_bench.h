@@ -42,10 +42,10 @@ int fs_generate(int dist, uint64_t seed, uint64_t start, uint64_t n, void* out,
  * that the call fails with the right status and that the sorter works again
  * afterwards. */
 
-/* Keys-only sorts whose keys take at most `key_bytes` bytes (and more than
- * the single-CTA limit) run as one cooperative launch instead of the chain of
- * 2 + 3P kernels; 0 always uses the chain.  fs_create takes the limit from
- * FORGESORT_COOP_MAX_BYTES (default 8 MiB: 2^21 four-byte keys). */
+/* Keys-only sorts of 32-bit keys whose keys take at most `key_bytes` bytes
+ * (and more than the single-CTA limit) run as one cooperative launch instead
+ * of the chain of 2 + 3P kernels; 0 always uses the chain.  fs_create takes
+ * the limit from FORGESORT_COOP_MAX_BYTES (default 2 MiB: 2^19 keys). */
 int fs_set_single_launch_max(fs_sorter* s, uint64_t key_bytes);
 
 /* Bound on every device-side wait of this sorter (the mbarrier waits of the

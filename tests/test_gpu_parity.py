@@ -107,9 +107,10 @@ def test_deterministic_repeat(sorter):
 @pytest.mark.parametrize("n", [8193, 65_537, 1 << 20, (1 << 21) - 5])
 @pytest.mark.parametrize("dt,dist", DT_DIST, ids=[d for d, _ in DT_DIST])
 def test_single_launch_matches_chain_and_oracle(dt, dist, n):
-    """Keys-only sorts up to 8 MiB of keys run as one cooperative launch
-    (k_coop_sort): bit-exact against the oracle and the chained kernels, in
-    place and out of place, including inputs with skipped passes."""
+    """Keys-only 32-bit sorts run as one cooperative launch (k_coop_sort; on
+    by default up to 2 MiB, forced here up to 8 MiB): bit-exact against the
+    oracle and the chained kernels, in place and out of place, including
+    inputs with skipped passes.  64-bit keys always take the chain."""
     import torch
     from forge_sort import GpuSorter
     kb = 8 if dt in ("u64", "i64", "f64") else 4
@@ -120,6 +121,7 @@ def test_single_launch_matches_chain_and_oracle(dt, dist, n):
     want = bits(orc.sort_keys(x, dt), dt)
     iv = np.int32 if kb == 4 else np.int64
     one = GpuSorter.new()
+    one.set_single_launch_max(8 << 20)
     chain = GpuSorter.new()
     chain.set_single_launch_max(0)
     try:
@@ -132,7 +134,7 @@ def test_single_launch_matches_chain_and_oracle(dt, dist, n):
             s.sort_device_copy(dt, b.data_ptr(), out.data_ptr(), n)
             assert np.array_equal(out.cpu().numpy().view(xb.dtype), want)
             assert np.array_equal(b.cpu().numpy().view(xb.dtype), xb)  # input untouched
-        assert one.last_launch_count() == 1
+        assert one.last_launch_count() == (1 if kb == 4 else 2 + 3 * kb)
         # low bits only vary: odd and even numbers of executed passes
         for mask_bits in (8, 16, 24):
             y = (xb & xb.dtype.type((1 << mask_bits) - 1)).view(orc.NP_DTYPE[dt])
