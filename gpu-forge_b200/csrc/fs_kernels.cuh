@@ -705,7 +705,11 @@ __device__ __forceinline__ uint32_t warp_peers(uint32_t d, bool valid) {
 
 __host__ __device__ constexpr int log2_of(int v) { return v <= 1 ? 0 : 1 + log2_of(v >> 1); }
 
-template <typename K, bool VALS, int BLOCK, int IPT, bool STAGE_DIG, int R = RADIX>
+// SLOTS: bulk-copy slots for the keys.  2: the next tile's copy lands in the
+// other slot while this tile is processed.  1 (keys only): the next tile's
+// copy is issued into the same slot as soon as this tile's keys are in
+// registers -- half the shared memory, so more CTAs fit per SM.
+template <typename K, bool VALS, int BLOCK, int IPT, bool STAGE_DIG, int R = RADIX, int SLOTS = 2>
 struct ScatterLayout {
   static constexpr int WARPS = BLOCK / 32;
   static constexpr int TILE = BLOCK * IPT;
@@ -716,7 +720,8 @@ struct ScatterLayout {
   // dynamic shared memory:
   //   [slot 0 | slot 1 | stage keys | stage vals | warp digit counters |
   //    warp digit owners | staged digits]
-  static constexpr size_t STAGE_OFF = 2 * SLOT;
+  static_assert(SLOTS == 2 || (SLOTS == 1 && !VALS), "one slot: keys-only passes");
+  static constexpr size_t STAGE_OFF = SLOTS * SLOT;
   static constexpr size_t CNT_OFF = STAGE_OFF + KEYS + VALB;
   static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * R * 4;  // per-warp digit owners
   static constexpr size_t DIG_OFF = REP_OFF + (((size_t)WARPS * R + 15) & ~(size_t)15);
@@ -726,7 +731,40 @@ struct ScatterLayout {
   static_assert(KEYS % 16 == 0, "bulk copies move multiples of 16 bytes");
 };
 
-template <typename K, bool VALS, int XF, int BLOCK, int IPT, bool FULL, bool FROM_SLOT, bool UNSTABLE, typename D>
+// Per-key ranks of a tile: a register each, or (PACK) two 16-bit ranks per
+// register (a rank is below 32 * IPT), which frees IPT/2 registers.
+#ifndef FS_PACK_RANKS
+#define FS_PACK_RANKS 0
+#endif
+template <int IPT, bool PACK>
+struct Ranks {
+  uint32_t r[PACK ? (IPT + 1) / 2 : IPT];
+  __device__ __forceinline__ void set(int k, uint32_t v) {
+    if constexpr (PACK) {
+      if (k & 1)
+        r[k >> 1] |= v << 16;
+      else
+        r[k >> 1] = v;
+    } else {
+      r[k] = v;
+    }
+  }
+  __device__ __forceinline__ uint32_t get(int k) const {
+    if constexpr (PACK)
+      return (k & 1) ? r[k >> 1] >> 16 : r[k >> 1] & 0xffffu;
+    else
+      return r[k];
+  }
+};
+
+struct NoHook {
+  __device__ __forceinline__ void operator()() const {}
+};
+
+// `on_loaded` runs on every thread once the tile's keys are in registers
+// (single-slot scatter: it issues the next tile's copy into the slot).
+template <typename K, bool VALS, int XF, int BLOCK, int IPT, bool FULL, bool FROM_SLOT, bool UNSTABLE,
+          typename D, int SLOTS = 2, typename Hook = NoHook>
 __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_t tile_n, const uint64_t n,
                                              const uint32_t flags, const K* __restrict__ kin,
                                              K* __restrict__ kout, const uint32_t* __restrict__ vin,
@@ -734,9 +772,9 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
                                              unsigned char* dsm, uint32_t* s_run, uint32_t* s_off,
                                              uint32_t* s_wsum, SortCtl* __restrict__ ctl, const D& dfn,
                                              const uint64_t gpos_base, K* const* s_dst, const uint32_t* s_lim,
-                                             uint32_t* const* s_vdst) {
+                                             uint32_t* const* s_vdst, const Hook& on_loaded = Hook{}) {
   constexpr int R = D::DIGITS;
-  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R>;
+  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R, SLOTS>;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t lt_mask = (1u << lane) - 1u;
   const uint64_t gbase = gpos_base + tbase;
@@ -760,6 +798,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     else
       key[k] = (FULL || li < tile_n) ? kin[tbase + li] : K(0);
   }
+  if constexpr (FROM_SLOT && SLOTS == 1) on_loaded();
   if constexpr (XF != XF_NONE) {
     if (flags & PD_XF_IN) {
 #pragma unroll
@@ -793,7 +832,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   // Per key: the lanes sharing its digit; all read the warp's running count
   // for that digit, the group's highest lane advances it.  After the loop
   // the counters hold the warp's per-digit totals.
-  uint32_t rank[IPT];
+  Ranks<IPT, FS_PACK_RANKS != 0> rank;
   if constexpr (UNSTABLE) {
     // Keys-only first pass: no earlier order to keep, so any order among
     // equal digits is correct -- one shared atomic per key ranks it.
@@ -801,7 +840,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
       const uint32_t d = digit(k);
-      rank[k] = valid ? atomicAdd(&wcnt[d], 1u) : 0u;
+      rank.set(k, valid ? atomicAdd(&wcnt[d], 1u) : 0u);
     }
   } else if constexpr (FS_RANK_BALLOT == 3 && R > 32) {
     // Owner election: every lane writes its lane number into its digit's
@@ -828,7 +867,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       __syncwarp();
       if (valid && lane == own) wcnt[d] = old + __popc(peers);
       __syncwarp();
-      rank[k] = old + __popc(peers & lt_mask);
+      rank.set(k, old + __popc(peers & lt_mask));
     }
   } else {
 #pragma unroll
@@ -841,7 +880,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       __syncwarp();
       if (valid && lane == 31u - __clz(peers)) wcnt[d] = old + __popc(peers);
       __syncwarp();
-      rank[k] = old + __popc(peers & lt_mask);
+      rank.set(k, old + __popc(peers & lt_mask));
     }
   }
   __syncthreads();
@@ -882,7 +921,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     const uint32_t li = wofs + k * 32;
     if (FULL || li < tile_n) {
       const uint32_t d = digit(k);
-      const uint32_t pos = wcnt[d] + rank[k];
+      const uint32_t pos = wcnt[d] + rank.get(k);
       skeys[pos] = key[k];
       if constexpr (VALS) {
         uint32_t v;
@@ -949,13 +988,13 @@ enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1 };
 // keys (and payload) are bulk-copied (cp.async.bulk global->shared, no
 // multicast) into the other of two slots while the current one is processed.
 // Every mbarrier wait is bounded; no CTA exits with a copy still in flight.
-template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, int MODE, typename D>
+template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, int MODE, typename D, int SLOTS = 2>
 __global__ void __launch_bounds__(BLOCK, MINB)
     k_scatter(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
               const uint32_t* __restrict__ offsets, const uint64_t timeout_ns, const D dfn_in,
               const uint64_t gpos_base) {
   constexpr int R = D::DIGITS;
-  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R>;
+  using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R, SLOTS>;
   extern __shared__ __align__(128) unsigned char dsm[];
   __shared__ uint32_t s_run[R];
   __shared__ uint32_t s_off[R];
@@ -1029,7 +1068,7 @@ __global__ void __launch_bounds__(BLOCK, MINB)
     if (tid < R) s_run[tid] = offsets[(size_t)c * RADIX + tid];  // row stride stays 256
     if (tid == 0) issue(lo, hi, s);
     __syncthreads();
-    for (uint64_t t0 = lo; t0 < hi; t0 += Ly::TILE, s ^= 1) {
+    for (uint64_t t0 = lo; t0 < hi; t0 += Ly::TILE, s ^= (SLOTS == 2 ? 1 : 0)) {
       const uint32_t tile_n = hi - t0 < (uint64_t)Ly::TILE ? (uint32_t)(hi - t0) : (uint32_t)Ly::TILE;
       const bool full = tile_n == (uint32_t)Ly::TILE;
       const bool from_slot = full && bulk_ok;
@@ -1039,7 +1078,9 @@ __global__ void __launch_bounds__(BLOCK, MINB)
         if (tid == 0) armed &= ~(1u << s);
       }
       if (tid == 0) {
-        issue(t0 + Ly::TILE, hi, s ^ 1);  // the other slot was consumed by the previous tile
+        // two slots: the other one was consumed by the previous tile; one
+        // slot: the copy is issued once this tile's keys are in registers
+        if (SLOTS == 2) issue(t0 + Ly::TILE, hi, s ^ 1);
         if (ld_relaxed_s32(&ctl->err) != 0) s_abort = 1;
       }
       __syncthreads();  // one abort decision for the CTA
@@ -1048,15 +1089,22 @@ __global__ void __launch_bounds__(BLOCK, MINB)
         break;
       }
       const unsigned char* slot = dsm + (size_t)s * Ly::SLOT;
+      auto refill = [&]() {
+        __syncthreads();  // every thread has read its keys from the slot
+        if (tid == 0) issue(t0 + Ly::TILE, hi, 0);
+      };
       if (from_slot)
-        scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                         slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim, s_vdst);
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE, D, SLOTS>(
+            t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
+            s_dst, s_lim, s_vdst, refill);
       else if (full)
-        scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                          slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim, s_vdst);
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE, D, SLOTS>(
+            t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
+            s_dst, s_lim, s_vdst, refill);
       else
-        scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE>(t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout,
-                                                           slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base, s_dst, s_lim, s_vdst);
+        scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE, D, SLOTS>(
+            t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
+            s_dst, s_lim, s_vdst, refill);
     }
   }
   // never leave a bulk copy into this CTA's shared memory in flight

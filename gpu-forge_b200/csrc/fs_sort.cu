@@ -150,24 +150,31 @@ int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
 #define FS_U32_UNSTABLE_MINB 2
 #endif
 template <typename K, bool VALS> struct StableCfg;
+#ifndef FS_U32_STABLE_SLOTS
+#define FS_U32_STABLE_SLOTS 2
+#endif
+#ifndef FS_U32_UNSTABLE_SLOTS
+#define FS_U32_UNSTABLE_SLOTS 2
+#endif
 template <> struct StableCfg<uint32_t, false> {
-  static constexpr int BLOCK = 256, IPT = FS_U32_STABLE_IPT, MINB = FS_U32_STABLE_MINB;
+  static constexpr int BLOCK = 256, IPT = FS_U32_STABLE_IPT, MINB = FS_U32_STABLE_MINB, SLOTS = FS_U32_STABLE_SLOTS;
 };
 template <> struct StableCfg<uint32_t, true> {
-  static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
+  static constexpr int BLOCK = 256, IPT = 16, MINB = 2, SLOTS = 2;
 };
 template <> struct StableCfg<uint64_t, false> {
-  static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
+  static constexpr int BLOCK = 256, IPT = 16, MINB = 2, SLOTS = 2;
 };
 template <> struct StableCfg<uint64_t, true> {
-  static constexpr int BLOCK = 256, IPT = 8, MINB = 2;
+  static constexpr int BLOCK = 256, IPT = 8, MINB = 2, SLOTS = 2;
 };
 template <typename K> struct UnstableCfg;
 template <> struct UnstableCfg<uint32_t> {
-  static constexpr int BLOCK = 256, IPT = FS_U32_UNSTABLE_IPT, MINB = FS_U32_UNSTABLE_MINB;
+  static constexpr int BLOCK = 256, IPT = FS_U32_UNSTABLE_IPT, MINB = FS_U32_UNSTABLE_MINB,
+                       SLOTS = FS_U32_UNSTABLE_SLOTS;
 };
 template <> struct UnstableCfg<uint64_t> {
-  static constexpr int BLOCK = 256, IPT = 16, MINB = 2;
+  static constexpr int BLOCK = 256, IPT = 16, MINB = 2, SLOTS = 2;
 };
 // Sample-sort partition / dispatch pass: the stable tile with room for the
 // splitter search (2 CTAs/SM; same tile as StableCfg<K, false>).
@@ -179,7 +186,7 @@ template <> struct UnstableCfg<uint64_t> {
 #endif
 template <typename K> struct PartCfg {
   // 64-bit keys need the registers of 3 CTAs/SM (the splitters sit in registers)
-  static constexpr int BLOCK = 256, IPT = FS_PART_IPT, MINB = sizeof(K) == 8 ? 3 : FS_PART_MINB;
+  static constexpr int BLOCK = 256, IPT = FS_PART_IPT, MINB = sizeof(K) == 8 ? 3 : FS_PART_MINB, SLOTS = 2;
   static_assert(StableCfg<K, false>::BLOCK * StableCfg<K, false>::IPT % (BLOCK * IPT) == 0,
                 "partition tiles must divide the slice unit");
 };
@@ -363,8 +370,8 @@ int blocks_per_sm(fs_sorter* s, Kern k, int block, size_t smem) {
 // limit on the current device the first time; allocates nothing.
 template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int scatter_occupancy(const Exec& e) {
-  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS>;
-  auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D>;
+  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS, C::SLOTS>;
+  auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D, C::SLOTS>;
   // sorters on several host threads may get here at once: the attribute
   // call is idempotent, the cache words are atomic
   static std::atomic<bool> configured[MAX_DEVICES];  // per device (the attribute is per context)
@@ -415,12 +422,12 @@ int chain_launch(const Exec& e, void (*kern)(KArgs...), unsigned grid, unsigned 
 
 template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const D& dfn, uint64_t gpos_base) {
-  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS>;
+  using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS, C::SLOTS>;
   const int bps = scatter_occupancy<K, VALS, XF, C, MODE, D>(e);
   if (bps < 0) return -bps;
   const uint64_t cap = (uint64_t)bps * e.sm_count;
   const unsigned grid = (unsigned)(sl.count < cap ? sl.count : cap);
-  return chain_launch(e, k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D>, grid, C::BLOCK, Ly::BYTES,
+  return chain_launch(e, k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D, C::SLOTS>, grid, C::BLOCK, Ly::BYTES,
                       e.ctl, pass, n, sl, static_cast<const uint32_t*>(e.offsets), e.timeout_ns, dfn, gpos_base);
 }
 
