@@ -733,9 +733,6 @@ struct ScatterLayout {
 
 // Per-key ranks of a tile: a register each, or (PACK) two 16-bit ranks per
 // register (a rank is below 32 * IPT), which frees IPT/2 registers.
-#ifndef FS_PACK_RANKS
-#define FS_PACK_RANKS 0
-#endif
 template <int IPT, bool PACK>
 struct Ranks {
   uint32_t r[PACK ? (IPT + 1) / 2 : IPT];
@@ -764,7 +761,7 @@ struct NoHook {
 // `on_loaded` runs on every thread once the tile's keys are in registers
 // (single-slot scatter: it issues the next tile's copy into the slot).
 template <typename K, bool VALS, int XF, int BLOCK, int IPT, bool FULL, bool FROM_SLOT, bool UNSTABLE,
-          typename D, int SLOTS = 2, typename Hook = NoHook>
+          typename D, int SLOTS = 2, typename Hook = NoHook, bool PACK = false>
 __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_t tile_n, const uint64_t n,
                                              const uint32_t flags, const K* __restrict__ kin,
                                              K* __restrict__ kout, const uint32_t* __restrict__ vin,
@@ -832,7 +829,7 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
   // Per key: the lanes sharing its digit; all read the warp's running count
   // for that digit, the group's highest lane advances it.  After the loop
   // the counters hold the warp's per-digit totals.
-  Ranks<IPT, FS_PACK_RANKS != 0> rank;
+  Ranks<IPT, PACK> rank;
   if constexpr (UNSTABLE) {
     // Keys-only first pass: no earlier order to keep, so any order among
     // equal digits is correct -- one shared atomic per key ranks it.
@@ -988,7 +985,8 @@ enum ScatterMode : int { SCATTER_ANY = 0, SCATTER_UNSTABLE = 1 };
 // keys (and payload) are bulk-copied (cp.async.bulk global->shared, no
 // multicast) into the other of two slots while the current one is processed.
 // Every mbarrier wait is bounded; no CTA exits with a copy still in flight.
-template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, int MODE, typename D, int SLOTS = 2>
+template <typename K, bool VALS, int XF, int BLOCK, int IPT, int MINB, int MODE, typename D, int SLOTS = 2,
+          bool PACK = false>
 __global__ void __launch_bounds__(BLOCK, MINB)
     k_scatter(SortCtl* __restrict__ ctl, const int pass, const uint64_t n, const Slices sl,
               const uint32_t* __restrict__ offsets, const uint64_t timeout_ns, const D dfn_in,
@@ -1094,15 +1092,15 @@ __global__ void __launch_bounds__(BLOCK, MINB)
         if (tid == 0) issue(t0 + Ly::TILE, hi, 0);
       };
       if (from_slot)
-        scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE, D, SLOTS>(
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE, D, SLOTS, decltype(refill), PACK>(
             t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
             s_dst, s_lim, s_vdst, refill);
       else if (full)
-        scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE, D, SLOTS>(
+        scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE, D, SLOTS, decltype(refill), PACK>(
             t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
             s_dst, s_lim, s_vdst, refill);
       else
-        scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE, D, SLOTS>(
+        scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE, D, SLOTS, decltype(refill), PACK>(
             t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
             s_dst, s_lim, s_vdst, refill);
     }

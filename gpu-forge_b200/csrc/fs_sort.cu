@@ -130,7 +130,11 @@ int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
     if (e_ != cudaSuccess) return cuda_fail((s), e_, #call);   \
   } while (0)
 
-// Scatter tile shapes (threads x keys per thread, resident CTAs per SM).
+// Scatter tile shapes (threads x keys per thread, resident CTAs per SM,
+// bulk-copy slots, 16-bit packed ranks).  The stable u32 pass runs with one
+// copy slot and packed ranks at 4 CTAs/SM: measured on one B200, 2^30 u32
+// keys, 4.23 -> 3.95 ms per stable pass (sort 18.4 -> 17.5 ms on that box);
+// one slot made the unstable pass slower (2.9 -> 3.2-3.6 ms), so it keeps two.
 // StableCfg ranks with the ballot multisplit (every pass of argsort / pairs,
 // and the passes after the first of a keys-only sort); UnstableCfg ranks
 // with one shared atomic per key (the first executed pass of a keys-only
@@ -141,7 +145,7 @@ int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
 #define FS_U32_STABLE_IPT 16
 #endif
 #ifndef FS_U32_STABLE_MINB
-#define FS_U32_STABLE_MINB 3
+#define FS_U32_STABLE_MINB 4
 #endif
 #ifndef FS_U32_UNSTABLE_IPT
 #define FS_U32_UNSTABLE_IPT 32
@@ -151,30 +155,42 @@ int cuda_fail(fs_sorter* s, cudaError_t e, const char* what) {
 #endif
 template <typename K, bool VALS> struct StableCfg;
 #ifndef FS_U32_STABLE_SLOTS
-#define FS_U32_STABLE_SLOTS 2
+#define FS_U32_STABLE_SLOTS 1
 #endif
 #ifndef FS_U32_UNSTABLE_SLOTS
 #define FS_U32_UNSTABLE_SLOTS 2
 #endif
+#ifndef FS_STABLE_PACK
+#define FS_STABLE_PACK 1
+#endif
+#ifndef FS_UNSTABLE_PACK
+#define FS_UNSTABLE_PACK 0
+#endif
 template <> struct StableCfg<uint32_t, false> {
   static constexpr int BLOCK = 256, IPT = FS_U32_STABLE_IPT, MINB = FS_U32_STABLE_MINB, SLOTS = FS_U32_STABLE_SLOTS;
+  static constexpr bool PACK = FS_STABLE_PACK != 0;
 };
 template <> struct StableCfg<uint32_t, true> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2, SLOTS = 2;
+  static constexpr bool PACK = FS_STABLE_PACK != 0;
 };
 template <> struct StableCfg<uint64_t, false> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2, SLOTS = 2;
+  static constexpr bool PACK = FS_STABLE_PACK != 0;
 };
 template <> struct StableCfg<uint64_t, true> {
   static constexpr int BLOCK = 256, IPT = 8, MINB = 2, SLOTS = 2;
+  static constexpr bool PACK = FS_STABLE_PACK != 0;
 };
 template <typename K> struct UnstableCfg;
 template <> struct UnstableCfg<uint32_t> {
   static constexpr int BLOCK = 256, IPT = FS_U32_UNSTABLE_IPT, MINB = FS_U32_UNSTABLE_MINB,
                        SLOTS = FS_U32_UNSTABLE_SLOTS;
+  static constexpr bool PACK = FS_UNSTABLE_PACK != 0;
 };
 template <> struct UnstableCfg<uint64_t> {
   static constexpr int BLOCK = 256, IPT = 16, MINB = 2, SLOTS = 2;
+  static constexpr bool PACK = FS_UNSTABLE_PACK != 0;
 };
 // Sample-sort partition / dispatch pass: the stable tile with room for the
 // splitter search (2 CTAs/SM; same tile as StableCfg<K, false>).
@@ -187,6 +203,7 @@ template <> struct UnstableCfg<uint64_t> {
 template <typename K> struct PartCfg {
   // 64-bit keys need the registers of 3 CTAs/SM (the splitters sit in registers)
   static constexpr int BLOCK = 256, IPT = FS_PART_IPT, MINB = sizeof(K) == 8 ? 3 : FS_PART_MINB, SLOTS = 2;
+  static constexpr bool PACK = false;
   static_assert(StableCfg<K, false>::BLOCK * StableCfg<K, false>::IPT % (BLOCK * IPT) == 0,
                 "partition tiles must divide the slice unit");
 };
@@ -371,7 +388,7 @@ int blocks_per_sm(fs_sorter* s, Kern k, int block, size_t smem) {
 template <typename K, bool VALS, int XF, typename C, int MODE, typename D>
 int scatter_occupancy(const Exec& e) {
   using Ly = ScatterLayout<K, VALS, C::BLOCK, C::IPT, D::STAGE, D::DIGITS, C::SLOTS>;
-  auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D, C::SLOTS>;
+  auto kern = k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D, C::SLOTS, C::PACK>;
   // sorters on several host threads may get here at once: the attribute
   // call is idempotent, the cache words are atomic
   static std::atomic<bool> configured[MAX_DEVICES];  // per device (the attribute is per context)
@@ -427,7 +444,8 @@ int launch_scatter(const Exec& e, int pass, uint64_t n, const Slices& sl, const 
   if (bps < 0) return -bps;
   const uint64_t cap = (uint64_t)bps * e.sm_count;
   const unsigned grid = (unsigned)(sl.count < cap ? sl.count : cap);
-  return chain_launch(e, k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D, C::SLOTS>, grid, C::BLOCK, Ly::BYTES,
+  return chain_launch(e, k_scatter<K, VALS, XF, C::BLOCK, C::IPT, C::MINB, MODE, D, C::SLOTS, C::PACK>, grid, C::BLOCK,
+                      Ly::BYTES,
                       e.ctl, pass, n, sl, static_cast<const uint32_t*>(e.offsets), e.timeout_ns, dfn, gpos_base);
 }
 
