@@ -127,8 +127,6 @@ struct SortCtl {
   unsigned long long hist[MAX_PASSES][RADIX];  // global digit counts of each pass
   unsigned long long kor;    // OR of all ordered keys
   unsigned long long kandn;  // OR of all complemented ordered keys (= ~AND)
-  unsigned bar_count;        // single-launch sort: CTAs arrived at the grid barrier
-  unsigned bar_gen;          // single-launch sort: barrier generation (any start value)
   PassDesc pass[MAX_PASSES];
   FinalDesc fin;
   int err;  // first device-side failure (DEV_ERR_*)
@@ -144,9 +142,8 @@ struct Slices {
 
 // Per-sort arguments of the plan kernel: where the keys and payload come from
 // and where they must end up.
-// Bytes of SortCtl that are zeroed before every sort: hist, kor, kandn and
-// the grid barrier's arrival count.
-constexpr size_t CTL_ACCUM_BYTES = sizeof(unsigned long long) * (MAX_PASSES * RADIX + 2) + 2 * sizeof(unsigned);
+// Bytes of SortCtl that are zeroed before every sort: hist, kor and kandn.
+constexpr size_t CTL_ACCUM_BYTES = sizeof(unsigned long long) * (MAX_PASSES * RADIX + 2);
 static_assert(offsetof(SortCtl, pass) == CTL_ACCUM_BYTES, "accumulators lead SortCtl");
 
 struct PlanArgs {

@@ -6,7 +6,7 @@
 // on that stream (P = key bytes), with no host round trip in between.
 #include "forgesort.h"
 #include "forgesort_bench.h"
-#include "fs_coop.cuh"
+#include "fs_resident.cuh"
 #include "fs_hoststage.h"
 #include "fs_kernels.cuh"
 
@@ -44,7 +44,17 @@ struct fs_sorter {
   void* dvals = nullptr;
   size_t dvals_bytes = 0;
   void* dst_tab = nullptr;  // sample-sort dispatch: 256 destination pointers
-  uint64_t coop_max_bytes = 2ull << 20;  // keys-only 32-bit sorts up to this many key bytes run as
+  // single-launch sort (k_resident_sort): two accumulator sets used by
+  // alternate launches, per-CTA digit counts
+  void* res_acc = nullptr;
+  size_t res_acc_bytes = 0;
+  void* res_counts = nullptr;
+  size_t res_counts_bytes = 0;
+  int res_parity = 0;
+  // after a failure the device error word may be left set: the next sort
+  // clears it first
+  bool ctl_dirty = true;
+  uint64_t coop_max_bytes = 8ull << 20;  // keys-only 32-bit sorts up to this many key bytes run as
                                          // one cooperative launch (FORGESORT_COOP_MAX_BYTES; 0: off)
   uint32_t small_max = SMALL_N_MAX;  // single-CTA sorts up to this n (FORGESORT_SMALL_SORT);
                                      // with a payload up to min(small_max, SMALL_N_PAYLOAD_MAX)
@@ -77,6 +87,7 @@ struct fs_sorter {
   HostStage stage;  // page-locked chunk ring for pageable host-slice copies
   int test_withhold = 0;    // fs_test_inject(FS_TEST_WITHHOLD_COPY): next radix sort
   int test_fail_alloc = 0;  // fs_test_inject(FS_TEST_FAIL_ALLOC): countdown to a failed growth
+  int test_skip_arrival = 0;  // fs_test_inject(FS_TEST_SKIP_ARRIVAL): next single-launch sort
   std::unordered_map<void*, size_t> allocs;  // fs_alloc'd pointers -> bytes
   std::unordered_map<void*, int> managed;
   std::string err;
@@ -108,10 +119,12 @@ int fail(fs_sorter* s, int code, const char* fmt, ...) {
   va_start(ap, fmt);
   vsnprintf(buf, sizeof buf, fmt, ap);
   va_end(ap);
-  if (s)
+  if (s) {
     s->err = buf;
-  else
+    s->ctl_dirty = true;  // a failed call may leave the device error word set
+  } else {
     g_create_err = buf;
+  }
   return code;
 }
 
@@ -617,67 +630,97 @@ int dispatch_small(fs_sorter* s, int dtype, const PlanArgs& a) {
   }
 }
 
-// Keys-only sorts of up to a few million keys: the whole sort in one
-// cooperative launch (k_coop_sort), one CTA per slice, all resident.
-template <typename K, int XF>
-int enqueue_coop(fs_sorter* s, const PlanArgs& a) {
-  constexpr int BLOCK = 256, IPT = 16, P = (int)sizeof(K);
-  using Ly = ScatterLayout<K, false, BLOCK, IPT, false, RADIX>;
-  auto kern = k_coop_sort<K, XF, BLOCK, IPT>;
-  static std::atomic<int> bps_dev[MAX_DEVICES];  // resident CTAs per SM, 0 = not configured yet
-  if (s->device < 0 || s->device >= MAX_DEVICES)
-    return fail(s, FS_E_INVALID, "device %d outside [0, %d)", s->device, MAX_DEVICES);
-  int bps = bps_dev[s->device].load();
-  if (bps == 0) {
-    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES));
-    bps = blocks_per_sm(s, kern, BLOCK, Ly::BYTES);
-    if (bps < 0) return -bps;
-    bps_dev[s->device].store(bps);
-  }
-  const uint64_t tile = (uint64_t)BLOCK * IPT;
-  const uint64_t ntiles = (a.n + tile - 1) / tile;
-  const uint64_t cap = (uint64_t)bps * s->sm_count;
-  const uint64_t want = ntiles < cap ? ntiles : cap;
-  const uint64_t tps = (ntiles + want - 1) / want;  // tiles per slice
-  Slices sl{};
-  sl.keys_per_slice = tps * tile;
-  sl.count = (uint32_t)((ntiles + tps - 1) / tps);
-  const uint32_t groups = (sl.count + COOP_GROUP - 1) / COOP_GROUP;
-  const size_t grp_bytes = (size_t)P * groups * RADIX * 4;
-  int rc = grow(s, &s->counts, &s->counts_bytes, (size_t)sl.count * RADIX * 4, false);
-  if (!rc) rc = grow(s, &s->offsets, &s->offsets_bytes, grp_bytes, false);
-  if (rc) return rc;
-  FS_CUDA(s, cudaMemsetAsync(s->ctl, 0, CTL_ACCUM_BYTES, s->stream));
+// Clear the device error word after a failed call (stream-ordered, before
+// the next sort's kernels): the single-launch sort leaves it set.
+int rearm_ctl(fs_sorter* s) {
+  if (!s->ctl_dirty) return FS_OK;
   FS_CUDA(s, cudaMemsetAsync(&s->ctl->err, 0, sizeof(int), s->stream));
-  FS_CUDA(s, cudaMemsetAsync(s->offsets, 0, grp_bytes, s->stream));
-  CoopArgs ca{};
-  ca.kin = a.kin;
-  ca.kfinal = a.kfinal;
-  ca.kother = a.kother;
-  ca.n = a.n;
-  ca.ctl = s->ctl;
-  ca.counts = static_cast<uint32_t*>(s->counts);
-  ca.grp = static_cast<uint32_t*>(s->offsets);
-  ca.sl = sl;
-  ca.groups = groups;
-  ca.timeout_ns = s->timeout_ns;
-  ca.host_err = s->host_err_dev;
-  void* params[] = {&ca};
-  Exec e = exec_of(s);
-  s->ev_used = 0;
-  t_begin(e);
-  FS_CUDA(s, cudaLaunchCooperativeKernel((const void*)kern, dim3(sl.count), dim3(BLOCK), params, Ly::BYTES,
-                                         s->stream));
-  t_end(e);
-  s->last_launches = 1;
+  s->ctl_dirty = false;
   return FS_OK;
 }
 
-int dispatch_coop(fs_sorter* s, int dtype, const PlanArgs& a) {
+// Keys-only sorts of up to a few million keys: the whole sort in one
+// cooperative launch (k_resident_sort), one CTA of RES_BLOCK threads per SM,
+// every key in registers.  Keys per thread: the fewest of RES_IPTS that fit
+// the keys on the SMs.
+constexpr int RES_IPTS[] = {2, 4, 7, 14};
+constexpr int RES_IPT_MAX = 14;
+
+uint64_t resident_max_keys(int sm_count) {
+  return (uint64_t)(sm_count < RES_MAX_CTAS ? sm_count : RES_MAX_CTAS) * RES_BLOCK * RES_IPT_MAX;
+}
+
+template <typename K, int XF, int IPT>
+int launch_resident(fs_sorter* s, const PlanArgs& a) {
+  using Ly = ResLayout<K, RES_BLOCK, IPT>;
+  constexpr int P = (int)sizeof(K);
+  auto kern = k_resident_sort<K, XF, RES_BLOCK, IPT>;
+  static std::atomic<int> bps_dev[MAX_DEVICES];  // resident CTAs per SM, 0 = not configured yet
+  int bps = bps_dev[s->device].load();
+  if (bps == 0) {
+    FS_CUDA(s, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ly::BYTES));
+    bps = blocks_per_sm(s, kern, RES_BLOCK, Ly::BYTES);
+    if (bps < 0) return -bps;
+    bps_dev[s->device].store(bps);
+  }
+  const uint64_t grid = (a.n + Ly::TILE - 1) / Ly::TILE;
+  if (grid > (uint64_t)bps * s->sm_count || grid > (uint64_t)RES_MAX_CTAS)
+    return fail(s, FS_E_INVALID, "single-launch sort: %llu keys need %llu CTAs, %d fit", (unsigned long long)a.n,
+                (unsigned long long)grid, bps * s->sm_count);
+  // accumulators laid out for the most CTAs any launch of this sorter uses,
+  // so alternate launches of different sizes clear what the next one reads
+  // (every launch clears the set the next one uses before it waits anywhere,
+  // so a launch that failed still leaves that set clean)
+  const uint32_t max_grid = (uint32_t)RES_MAX_CTAS;
+  const uint32_t groups = (max_grid + RES_GROUP - 1) / RES_GROUP;
+  const size_t set_words = res_acc_words(MAX_PASSES, groups);
+  int rc = grow(s, &s->res_acc, &s->res_acc_bytes, 2 * set_words * 4, true);
+  if (!rc) rc = grow(s, &s->res_counts, &s->res_counts_bytes, (size_t)MAX_PASSES * max_grid * RADIX * 4, false);
+  if (rc) return rc;
+  uint32_t* acc = static_cast<uint32_t*>(s->res_acc);
+  ResArgs ra{};
+  ra.kin = a.kin;
+  ra.kout = a.kfinal;
+  ra.n = a.n;
+  ra.ctl = s->ctl;
+  ra.counts = static_cast<uint32_t*>(s->res_counts);
+  ra.acc = acc + (size_t)s->res_parity * set_words;
+  ra.acc_next = acc + (size_t)(s->res_parity ^ 1) * set_words;
+  ra.acc_words = (uint32_t)set_words;
+  ra.groups = groups;
+  ra.timeout_ns = s->timeout_ns;
+  ra.host_err = s->host_err_dev;
+  ra.test_skip_arrival = s->test_skip_arrival;
+  s->test_skip_arrival = 0;  // one-shot
+  void* params[] = {&ra};
+  Exec e = exec_of(s);
+  s->ev_used = 0;
+  t_begin(e);
+  FS_CUDA(s, cudaLaunchCooperativeKernel((const void*)kern, dim3((unsigned)grid), dim3(RES_BLOCK), params, Ly::BYTES,
+                                         s->stream));
+  t_end(e);
+  s->res_parity ^= 1;
+  s->last_launches = 1;
+  static_assert(P <= MAX_PASSES, "accumulator sets sized for MAX_PASSES");
+  return FS_OK;
+}
+
+template <typename K, int XF>
+int enqueue_resident(fs_sorter* s, const PlanArgs& a) {
+  if (s->device < 0 || s->device >= MAX_DEVICES)
+    return fail(s, FS_E_INVALID, "device %d outside [0, %d)", s->device, MAX_DEVICES);
+  const uint64_t per_cta = (a.n + s->sm_count - 1) / s->sm_count;
+  if (per_cta <= (uint64_t)RES_BLOCK * RES_IPTS[0]) return launch_resident<K, XF, RES_IPTS[0]>(s, a);
+  if (per_cta <= (uint64_t)RES_BLOCK * RES_IPTS[1]) return launch_resident<K, XF, RES_IPTS[1]>(s, a);
+  if (per_cta <= (uint64_t)RES_BLOCK * RES_IPTS[2]) return launch_resident<K, XF, RES_IPTS[2]>(s, a);
+  return launch_resident<K, XF, RES_IPTS[3]>(s, a);
+}
+
+int dispatch_resident(fs_sorter* s, int dtype, const PlanArgs& a) {
   switch (dtype) {
-    case FS_U32: return enqueue_coop<uint32_t, XF_NONE>(s, a);
-    case FS_I32: return enqueue_coop<uint32_t, XF_SIGN>(s, a);
-    case FS_F32: return enqueue_coop<uint32_t, XF_FLOAT>(s, a);
+    case FS_U32: return enqueue_resident<uint32_t, XF_NONE>(s, a);
+    case FS_I32: return enqueue_resident<uint32_t, XF_SIGN>(s, a);
+    case FS_F32: return enqueue_resident<uint32_t, XF_FLOAT>(s, a);
     default: return fail(s, FS_E_INVALID, "single-launch sort: 32-bit keys only (dtype %d)", dtype);
   }
 }
@@ -685,17 +728,19 @@ int dispatch_coop(fs_sorter* s, int dtype, const PlanArgs& a) {
 // The sorter's path: size the slices, grow its scratch, enqueue.
 int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   s->part.ready = false;  // the slice counts of a pending dispatch are overwritten
+  int rc = rearm_ctl(s);
+  if (rc) return rc;
   const uint32_t small_cap = a.has_vals && s->small_max > SMALL_N_PAYLOAD_MAX ? SMALL_N_PAYLOAD_MAX : s->small_max;
   if (a.n <= small_cap) return dispatch_small(s, dtype, a);
   // measured on one B200 (device time per call): one launch 58-65 us against
   // 75 us chained for 2^14..2^19 u32 keys; slower from 2^20 (82 vs 78 us) and
   // for 64-bit keys at every size (8 passes: twice the grid barriers)
   if (!a.has_vals && a.unstable_first && !s->test_withhold && key_bytes_of(dtype) == 4 &&
-      a.n * 4 <= s->coop_max_bytes)
-    return dispatch_coop(s, dtype, a);
+      a.n * 4 <= s->coop_max_bytes && a.n <= resident_max_keys(s->sm_count))
+    return dispatch_resident(s, dtype, a);
   Exec e = exec_of(s);
   const Slices sl = dispatch_slices(e, dtype, a.n, a.has_vals != 0, a.unstable_first != 0);
-  int rc = ensure_slice_buffers(s, sl);
+  rc = ensure_slice_buffers(s, sl);
   if (rc) return rc;
   e.counts = static_cast<uint32_t*>(s->counts);
   e.offsets = static_cast<uint32_t*>(s->offsets);
@@ -757,6 +802,7 @@ int enqueue_partition(fs_sorter* s, const void* keys_in, void* keys_out, uint64_
   a.key_bytes = (int)sizeof(K);
   a.counts_out = counts_out;
   a.ncounts = nsplit + 1;
+  if (int rc0 = rearm_ctl(s)) return rc0;
   FS_CUDA(s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
   launch_bucket_hist<K, XF>(e, sl, keys_in, n, spl_keys, spl_gpos, nsplit, gpos_base);
   k_plan<<<1, RADIX, 0, e.stream>>>(e.ctl, a);
@@ -794,6 +840,7 @@ int enqueue_partition_count(fs_sorter* s, const void* keys, uint64_t n, uint64_t
   if (rc) return rc;
   e.counts = static_cast<uint32_t*>(s->counts);
   s->ev_used = 0;
+  if (int rc0 = rearm_ctl(s)) return rc0;
   FS_CUDA(s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
   t_begin(e);
   launch_bucket_hist<K, XF>(e, sl, keys, n, spl_keys, spl_gpos, nsplit, gpos_base);
@@ -918,7 +965,7 @@ int finish(fs_sorter* s, int sync) {
     *(volatile int*)s->host_err = 0;
     if (he == DEV_ERR_BOUNDS)
       return fail(s, FS_E_GPU_EXECUTION, "a device position fell out of range (scatter offset or gather index)");
-    return fail(s, FS_E_TIMEOUT, "device wait timeout: a bulk copy did not complete within %llu ms",
+    return fail(s, FS_E_TIMEOUT, "device wait timeout: a bulk copy or grid barrier did not complete within %llu ms",
                 (unsigned long long)(s->timeout_ns / 1000000ull));
   }
   return FS_OK;
@@ -1837,6 +1884,10 @@ int fs_test_inject(fs_sorter* s, int kind, int arg) {
     case 0:
       s->test_withhold = 0;
       s->test_fail_alloc = 0;
+      s->test_skip_arrival = 0;
+      return FS_OK;
+    case FS_TEST_SKIP_ARRIVAL:
+      s->test_skip_arrival = 1;
       return FS_OK;
     case FS_TEST_WITHHOLD_COPY:
       s->test_withhold = 1;

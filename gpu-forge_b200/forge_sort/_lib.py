@@ -93,7 +93,7 @@ BENCH_SIGNATURES = {
     "fs_set_single_launch_max": (_i32, [_vp, _u64]),
     "fs_test_inject": (_i32, [_vp, _i32, _i32]),
 }
-TEST_WITHHOLD_COPY, TEST_FAIL_ALLOC = 1, 2
+TEST_WITHHOLD_COPY, TEST_FAIL_ALLOC, TEST_SKIP_ARRIVAL = 1, 2, 3
 GEN_U32, GEN_U64, GEN_SKEW_U32 = 0, 1, 2
 
 _lib = None

@@ -293,7 +293,7 @@ class GpuSorter:
 
     def set_single_launch_max(self, key_bytes: int) -> None:
         """Keys-only 32-bit sorts of up to `key_bytes` bytes of keys run as
-        one cooperative launch (default 2 MiB; 0: always the chained kernels)."""
+        one cooperative launch (default 8 MiB; 0: always the chained kernels)."""
         self._call(_lib.load().fs_set_single_launch_max(self._h, int(key_bytes)))
 
     def _test_inject(self, kind: int, arg: int = 0) -> None:

@@ -76,9 +76,10 @@ int fs_create(int device, void* stream, fs_sorter** out);
  *                              (default and maximum 8192 keys alone, 4096 with
  *                              a payload; 0: always the radix passes)
  *   FORGESORT_COOP_MAX_BYTES   keys-only sorts of 32-bit keys of up to this
- *                              many key bytes (default 2 MiB) run as one
- *                              cooperative launch with grid barriers instead
- *                              of the chained kernels; 0: always chained
+ *                              many key bytes (default 8 MiB, and at most
+ *                              14336 keys per SM) run as one cooperative
+ *                              launch with grid barriers instead of the
+ *                              chained kernels; 0: always chained
  * and once per process:
  *   FORGESORT_CHAIN_LAUNCH     0: launch a sort's kernels without programmatic
  *                              stream serialization (default: chained) */

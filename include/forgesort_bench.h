@@ -43,9 +43,10 @@ int fs_generate(int dist, uint64_t seed, uint64_t start, uint64_t n, void* out,
  * afterwards. */
 
 /* Keys-only sorts of 32-bit keys whose keys take at most `key_bytes` bytes
- * (and more than the single-CTA limit) run as one cooperative launch instead
- * of the chain of 2 + 3P kernels; 0 always uses the chain.  fs_create takes
- * the limit from FORGESORT_COOP_MAX_BYTES (default 2 MiB: 2^19 keys). */
+ * (more than the single-CTA limit, at most 14336 keys per SM) run as one
+ * cooperative launch instead of the chain of 2 + 3P kernels; 0 always uses
+ * the chain.  fs_create takes the limit from FORGESORT_COOP_MAX_BYTES
+ * (default 8 MiB: 2^21 keys). */
 int fs_set_single_launch_max(fs_sorter* s, uint64_t key_bytes);
 
 /* Bound on every device-side wait of this sorter (the mbarrier waits of the
@@ -62,11 +63,16 @@ typedef enum fs_test_inject_kind {
   /* The arg-th next growth of the sorter's device scratch (arg >= 1) fails
    * as if cudaMalloc had run out of memory: the call returns FS_E_OOM and
    * the scratch slot is left empty (the next call grows it again). */
-  FS_TEST_FAIL_ALLOC = 2
+  FS_TEST_FAIL_ALLOC = 2,
+  /* The next single-launch sort (fs_set_single_launch_max) runs with CTA 0
+   * leaving before the first grid barrier: every other CTA's bounded wait
+   * runs out (fs_set_wait_timeout_ms), the call returns FS_E_TIMEOUT and the
+   * next sort clears the barrier state.  One-shot. */
+  FS_TEST_SKIP_ARRIVAL = 3
 } fs_test_inject_kind;
 
 /* Arm one injected failure (kind above) on sorter `s`; arg as the kind says.
- * kind 0 disarms both. */
+ * kind 0 disarms all. */
 int fs_test_inject(fs_sorter* s, int kind, int arg);
 
 #ifdef __cplusplus

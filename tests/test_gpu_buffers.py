@@ -114,12 +114,12 @@ def test_device_pointer_checks(sorter):
 def test_launch_count(sorter):
     x = orc.gen("u32", 100_000, seed=1)
     sorter.sort_u32(x.copy())
-    assert sorter.last_launch_count() == 1  # keys-only 32-bit up to 2 MiB: one cooperative launch
+    assert sorter.last_launch_count() == 1  # keys-only 32-bit up to 8 MiB: one cooperative launch
     sorter.set_single_launch_max(0)
     try:
         sorter.sort_u32(x.copy())
     finally:
-        sorter.set_single_launch_max(2 << 20)
+        sorter.set_single_launch_max(8 << 20)
     # first count, plan, per pass (count -- pass 0 is counted by the first
     # count --, scan, scatter -- pass 0 ranks unstably, the others stably),
     # finalize

@@ -7,6 +7,9 @@ The reference maps a failed command buffer to SortError::GpuExecution
     (fs_test_inject FS_TEST_WITHHOLD_COPY), the scatter's mbarrier wait gives
     up after the sorter's wait bound (10 ms here), the kernels stop early and
     the call fails with a timeout (GpuExecution);
+  - a grid barrier that never completes: CTA 0 of the single-launch sort
+    leaves before the first barrier (FS_TEST_SKIP_ARRIVAL), the other CTAs'
+    bounded waits run out and the call fails with a timeout;
   - a device allocation that fails (FS_TEST_FAIL_ALLOC): the call fails with
     an out-of-memory GpuExecution, nothing leaks into the next call.
 After each, the same sorter must sort correctly again (bit-exact against the
@@ -40,6 +43,30 @@ def test_bounded_wait_runs_out_then_sorter_recovers():
             assert np.array_equal(b.view(orc.BITS_DTYPE[dt]), orc.sort_keys(y, dt).view(orc.BITS_DTYPE[dt]))
         idx = s.argsort_f32(orc.gen("f32_mix", 100_000, seed=3))
         assert np.array_equal(idx, orc.argsort(orc.gen("f32_mix", 100_000, seed=3), "f32"))
+    finally:
+        s.close()
+
+
+def test_grid_barrier_wait_runs_out_then_sorter_recovers():
+    from forge_sort import GpuSorter, _lib
+    from forge_sort.errors import GpuExecution
+
+    s = GpuSorter.new()
+    try:
+        s.set_single_launch_max(8 << 20)
+        s.set_wait_timeout_ms(10)
+        x = orc.gen("u32", 1 << 20, seed=321)
+        s._test_inject(_lib.TEST_SKIP_ARRIVAL)
+        with pytest.raises(GpuExecution) as ei:
+            s.sort_u32(x.copy())
+        assert "timeout" in str(ei.value)
+        # the barrier count and error word are cleared before the next sort
+        for dt, dist, n in (("u32", "u32", 1 << 20), ("f32", "f32_mix", 300_001), ("i32", "i32", 8193),
+                            ("u64", "u64", 200_000)):
+            y = orc.gen(dist, n, seed=9)
+            b = y.copy()
+            getattr(s, f"sort_{dt}")(b)
+            assert np.array_equal(b.view(orc.BITS_DTYPE[dt]), orc.sort_keys(y, dt).view(orc.BITS_DTYPE[dt])), dt
     finally:
         s.close()
 

@@ -104,13 +104,14 @@ def test_deterministic_repeat(sorter):
     assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("n", [8193, 65_537, 1 << 20, (1 << 21) - 5])
+@pytest.mark.parametrize("n", [8193, 65_537, 300_001, 500_000, 1 << 20, (1 << 21) - 5])
 @pytest.mark.parametrize("dt,dist", DT_DIST, ids=[d for d, _ in DT_DIST])
 def test_single_launch_matches_chain_and_oracle(dt, dist, n):
-    """Keys-only 32-bit sorts run as one cooperative launch (k_coop_sort; on
-    by default up to 2 MiB, forced here up to 8 MiB): bit-exact against the
-    oracle and the chained kernels, in place and out of place, including
-    inputs with skipped passes.  64-bit keys always take the chain."""
+    """Keys-only 32-bit sorts run as one cooperative launch (k_resident_sort,
+    forced here up to 8 MiB): bit-exact against the oracle and the chained
+    kernels, in place and out of place, including inputs with skipped passes.
+    The sizes reach every keys-per-thread shape (2, 4, 7, 14 on 148 SMs) with a
+    partial last CTA.  64-bit keys always take the chain."""
     import torch
     from forge_sort import GpuSorter
     kb = 8 if dt in ("u64", "i64", "f64") else 4
@@ -149,3 +150,31 @@ def test_single_launch_matches_chain_and_oracle(dt, dist, n):
     finally:
         one.close()
         chain.close()
+
+
+def test_single_launch_alternating_sizes():
+    """Launches of k_resident_sort alternate two accumulator sets, each launch
+    clearing the one the next uses: calls of different sizes and grids, back
+    to back without a wait between them, must each be bit-exact."""
+    import torch
+    from forge_sort import GpuSorter
+    s = GpuSorter.new()
+    s.set_single_launch_max(8 << 20)
+    try:
+        sizes = [1 << 20, 8193, (1 << 21) - 5, 300_001, 65_537, 1 << 20, 500_000]
+        cases = []
+        for i, n in enumerate(sizes * 2):
+            dt, dist = DT_DIST[i % len(DT_DIST)]
+            if dt in ("u64", "i64", "f64"):
+                dt, dist = "u32", "zipf_u32"
+            x = orc.gen(dist, n, seed=77 + i)
+            xb = bits(x, dt)
+            a = torch.from_numpy(xb.view(np.int32).copy()).cuda()
+            s.sort_device(dt, a.data_ptr(), n, sync=False)
+            assert s.last_launch_count() == 1
+            cases.append((a, bits(orc.sort_keys(x, dt), dt)))
+        s.synchronize()
+        for a, want in cases:
+            assert np.array_equal(a.cpu().numpy().view(want.dtype), want)
+    finally:
+        s.close()
