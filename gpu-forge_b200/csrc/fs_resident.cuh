@@ -84,11 +84,12 @@ __device__ __forceinline__ bool res_grid_sync(unsigned* bar, unsigned k, uint64_
   return *s_ok != 0;
 }
 
-// Accumulator set (32-bit words): [passes][groups][RADIX] group sums, then
-// the OR and ~AND words of the ordered keys (lo, hi each) and the barrier
-// counter, padded to 16 bytes.
-__host__ __device__ constexpr uint32_t res_acc_words(int passes, uint32_t groups) {
-  return (uint32_t)passes * RADIX * groups + 8u;
+// Accumulator set (32-bit words): [slots][groups][RADIX] group sums (one
+// slot per digit pass, one more for the most-significant-digit partition),
+// then the OR and ~AND words of the ordered keys (lo, hi each) and the
+// barrier counter, padded to 16 bytes.
+__host__ __device__ constexpr uint32_t res_acc_words(int slots, uint32_t groups) {
+  return (uint32_t)slots * RADIX * groups + 8u;
 }
 
 struct ResArgs {
@@ -96,7 +97,7 @@ struct ResArgs {
   void* kout;         // may equal kin (in place)
   uint64_t n;         // 2 .. gridDim.x * TILE
   SortCtl* ctl;       // err
-  uint32_t* counts;   // [passes][gridDim.x][RADIX], plain stores
+  uint32_t* counts;   // [slots][gridDim.x][RADIX], plain stores
   uint32_t* acc;      // this launch's accumulator set (zero on entry)
   uint32_t* acc_next; // the next launch's set: cleared here
   uint32_t acc_words; // words of a set (the largest layout any launch uses)
@@ -106,7 +107,7 @@ struct ResArgs {
   int test_skip_arrival;  // failure-path test: CTA 0 leaves before the first barrier
 };
 
-template <typename K, int BLOCK, int IPT>
+template <typename K, int BLOCK, int IPT, bool MSD = false>
 struct ResLayout {
   static constexpr int WARPS = BLOCK / 32;
   static constexpr int TILE = BLOCK * IPT;
@@ -114,49 +115,275 @@ struct ResLayout {
   static constexpr int Q = BLOCK / RADIX;  // threads per digit in the per-digit phases
   static constexpr int MAXG = ((RES_MAX_CTAS + RES_GROUP - 1) / RES_GROUP + Q - 1) / Q;  // group loads a thread
   static constexpr int MAXW = (RES_GROUP - 1 + Q - 1) / Q;  // in-group count loads a thread
-  // dynamic shared memory: [warp digit counters | warp digit owners | staged keys]
+  // dynamic shared memory: [warp digit counters | warp digit owners | staged
+  // keys: one tile, or (MSD) a segment of up to two tiles]
+  static constexpr int STAGE_KEYS = MSD ? 2 * TILE : TILE;
   static constexpr size_t CNT_OFF = 0;
   static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;
   static constexpr size_t STAGE_OFF = REP_OFF + (size_t)WARPS * RADIX;
-  static constexpr size_t BYTES = STAGE_OFF + (size_t)TILE * sizeof(K);
+  static constexpr size_t BYTES = STAGE_OFF + (size_t)STAGE_KEYS * sizeof(K);
   static_assert(BLOCK % RADIX == 0 && WARPS % Q == 0, "whole warps per digit-thread group");
   static_assert(STAGE_OFF % 16 == 0, "staging alignment");
 };
 
-template <typename K, int XF, int BLOCK, int IPT>
+// Shared state of one CTA of k_resident_sort.
+struct ResShared {
+  uint32_t* cnt;    // [WARPS][RADIX] per-warp digit counters
+  uint8_t* rep;     // [WARPS][RADIX] per-warp digit owners
+  uint32_t (*q)[RADIX];   // [Q][RADIX] partial sums per digit-thread group
+  uint32_t (*q2)[RADIX];  // [Q][RADIX] partial digit totals
+  uint32_t* tpart;  // [RADIX] tile-local digit start within its warp of digits
+  uint32_t* tstart; // [RADIX] tile-local start of each digit
+  uint32_t* off;    // [RADIX] global position - staging index, per digit
+  uint32_t* wsum;   // [RADIX / 32]
+  uint32_t* orw;    // [4] OR / ~AND of the CTA's ordered keys
+};
+
+// Warp-local ranks of `rows` rows of 32 keys: lane l's k-th key is element
+// wofs + 32k of the CTA's range (`lim` of them valid).  `unstable`: shared
+// atomics (any order among equal digits); otherwise owner election through a
+// byte per digit and five ballots over the owner's lane bits, which keeps the
+// order.  After the loop wcnt holds the warp's count of each digit.
+template <typename K, int NR, bool PACK>
+__device__ __forceinline__ void res_rank(const K (&key)[NR], Ranks<NR, PACK>& rank, int rows, uint32_t wofs,
+                                         uint32_t lim, int shift, bool unstable, uint32_t* wcnt, uint8_t* wrep) {
+  const uint32_t lane = threadIdx.x & 31, lt_mask = (1u << lane) - 1u;
+  if (unstable) {
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+      if (k < rows) {
+        const bool valid = wofs + k * 32 < lim;
+        rank.set(k, valid ? atomicAdd(&wcnt[(uint32_t)(key[k] >> shift) & (RADIX - 1)], 1u) : 0u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+      if (k < rows) {
+        const bool valid = wofs + k * 32 < lim;
+        const uint32_t d = (uint32_t)(key[k] >> shift) & (RADIX - 1);
+        if (valid) wrep[d] = (uint8_t)lane;
+        __syncwarp();
+        const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
+        uint32_t diff = 0;
+#pragma unroll
+        for (int b = 0; b < 5; ++b) {
+          const uint32_t bit = (own >> b) & 1u;
+          diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
+        }
+        const uint32_t peers = ~diff;
+        uint32_t old = 0;
+        if (valid) old = wcnt[d];
+        __syncwarp();
+        if (valid && lane == own) wcnt[d] = old + __popc(peers);
+        __syncwarp();
+        rank.set(k, old + __popc(peers & lt_mask));
+      }
+    }
+  }
+}
+
+// After ranking (and a __syncthreads): turn the per-warp counters into each
+// warp's start per digit (tile-local digit start + the counts of the earlier
+// warps).  `on_total(tot)` runs on threads tid < RADIX with the CTA's count of
+// digit tid, between the two internal barriers.  sh.tstart gets the
+// tile-local digit starts.  Ends without a barrier.
+template <int BLOCK, typename F>
+__device__ __forceinline__ void res_warp_starts(const ResShared& sh, F&& on_total) {
+  constexpr int Q = BLOCK / RADIX, WPQ = BLOCK / 32 / Q;
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t d = tid % RADIX, q = tid / RADIX;
+  {
+    uint32_t sum = 0;
+#pragma unroll
+    for (int w = 0; w < WPQ; ++w) sum += sh.cnt[(q * WPQ + w) * RADIX + d];
+    sh.q[q][d] = sum;
+  }
+  __syncthreads();
+  {
+    uint32_t run = 0, tot = 0;
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq) {
+      const uint32_t v = sh.q[qq][d];
+      if (qq < (int)q) run += v;
+      tot += v;
+    }
+#pragma unroll
+    for (int w = 0; w < WPQ; ++w) {  // exclusive prefix over the warps, per digit
+      uint32_t* cw = &sh.cnt[(q * WPQ + w) * RADIX + d];
+      const uint32_t v = *cw;
+      *cw = run;
+      run += v;
+    }
+    if (tid < RADIX) {
+      on_total(tot);
+      uint32_t x = tot;  // tile-local digit starts: exclusive scan of tot over the digits
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if ((int)lane >= o) x += y;
+      }
+      if (lane == 31) sh.wsum[warp] = x;
+      sh.tpart[tid] = x - tot;
+    }
+  }
+  __syncthreads();
+  uint32_t ts = sh.tpart[d];
+  for (uint32_t w = 0; w < (d >> 5); ++w) ts += sh.wsum[w];
+  if (q == 0) sh.tstart[d] = ts;
+#pragma unroll
+  for (int w = 0; w < WPQ; ++w) sh.cnt[(q * WPQ + w) * RADIX + d] += ts;
+}
+
+// After a grid barrier: the output base of each digit of accumulator slot
+// `slot` for CTA c, minus the tile-local digit start (sh.off), and the digit
+// totals' exclusive scan (sh.q2[0], when `starts`).  Loads first (at most
+// MAXG + MAXW a thread), then two block barriers.  Returns the largest digit
+// total (threads tid < RADIX; the caller reduces it if it needs it).
+template <int BLOCK, int MAXG, int MAXW>
+__device__ __forceinline__ uint32_t res_offsets(const ResShared& sh, const uint32_t* grp, const uint32_t* counts,
+                                                uint32_t groups, int slot, bool starts) {
+  constexpr int Q = BLOCK / RADIX;
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t d = tid % RADIX, q = tid / RADIX;
+  const uint32_t c = blockIdx.x, G = gridDim.x;
+  const uint32_t g_me = c / RES_GROUP, ngrp = (G + RES_GROUP - 1) / RES_GROUP;
+  uint32_t gv[MAXG], wv[MAXW];
+  {
+    const uint32_t* gp = grp + (size_t)slot * groups * RADIX + d;
+    const uint32_t* cp = counts + ((size_t)slot * G + g_me * RES_GROUP) * RADIX + d;
+    const uint32_t nw = c - g_me * RES_GROUP;
+#pragma unroll
+    for (int i = 0; i < MAXG; ++i) {
+      const uint32_t g = q + i * Q;
+      gv[i] = g < ngrp ? __ldcg(gp + (size_t)g * RADIX) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < MAXW; ++i) {
+      const uint32_t j = q + i * Q;
+      wv[i] = j < nw ? __ldcg(cp + (size_t)j * RADIX) : 0u;
+    }
+  }
+  {
+    uint32_t tot = 0, pre = 0;
+#pragma unroll
+    for (int i = 0; i < MAXG; ++i) {
+      tot += gv[i];
+      if (q + i * Q < g_me) pre += gv[i];
+    }
+#pragma unroll
+    for (int i = 0; i < MAXW; ++i) pre += wv[i];
+    sh.q[q][d] = pre;
+    sh.q2[q][d] = tot;
+  }
+  __syncthreads();
+  uint32_t tot = 0, dstart = 0;
+  if (tid < RADIX) {
+    uint32_t pre = 0;
+#pragma unroll
+    for (int qq = 0; qq < Q; ++qq) {
+      tot += sh.q2[qq][tid];
+      pre += sh.q[qq][tid];
+    }
+    uint32_t x = tot;  // digit starts: exclusive scan of the totals
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if ((int)lane >= o) x += y;
+    }
+    if (lane == 31) sh.wsum[warp] = x;
+    dstart = x - tot;
+    sh.off[tid] = dstart + pre - sh.tstart[tid];
+  }
+  __syncthreads();
+  if (tid < RADIX) {
+    uint32_t add = 0;
+    for (uint32_t w = 0; w < (tid >> 5); ++w) add += sh.wsum[w];
+    sh.off[tid] += add;
+    if (starts) sh.q2[0][tid] = dstart + add;
+  }
+  return tot;
+}
+
+// Stage the tile's keys in digit order (warp starts in sh.cnt plus ranks),
+// then write them to kout at sh.off[digit] + staging index (`xout`: inverse
+// order transform).  Out-of-range positions record DEV_ERR_BOUNDS and are
+// dropped.  Ends without a barrier after the writes.
+template <typename K, int XF, int BLOCK, int IPT, int STAGE_KEYS, bool PACK>
+__device__ __forceinline__ void res_scatter(const ResShared& sh, K* stage, const K (&key)[IPT],
+                                            const Ranks<IPT, PACK>& rank, uint32_t wofs, uint32_t tile_n, int shift,
+                                            K* kout, uint64_t n, bool xout, SortCtl* ctl) {
+  const uint32_t tid = threadIdx.x;
+  const uint32_t* wcnt = sh.cnt + (tid >> 5) * RADIX;
+  bool oob = false;
+#pragma unroll
+  for (int k = 0; k < IPT; ++k) {
+    if (wofs + k * 32 < tile_n) {
+      const uint32_t si = wcnt[(uint32_t)(key[k] >> shift) & (RADIX - 1)] + rank.get(k);
+      if (si < (uint32_t)STAGE_KEYS)
+        stage[si] = key[k];
+      else
+        oob = true;
+    }
+  }
+  __syncthreads();
+  const uint64_t lastpos = n - 1;
+#pragma unroll
+  for (int j = 0; j < IPT; ++j) {
+    const uint32_t i = j * BLOCK + tid;
+    if (i < tile_n) {
+      const K kk = stage[i];
+      const uint64_t pos = (uint64_t)sh.off[(uint32_t)(kk >> shift) & (RADIX - 1)] + i;
+      if (pos <= lastpos)
+        kout[pos] = xout ? from_ordered<K, XF>(kk) : kk;
+      else
+        oob = true;
+    }
+  }
+  if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
+}
+
+// MSD: first partition by the top digit across the grid (one pass, ranked
+// with shared atomics), then each CTA sorts a segment of whole top-digit
+// buckets -- those starting in its tile's range, at most two tiles when no
+// bucket holds more than a tile -- in shared memory with the LSD passes of
+// every varying digit and no grid barrier between them.  When a bucket is
+// larger than a tile (skewed keys, or the top digit constant) the same launch
+// runs the plain LSD passes instead.
+template <typename K, int XF, int BLOCK, int IPT, bool MSD>
 __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
-  using Ly = ResLayout<K, BLOCK, IPT>;
+  using Ly = ResLayout<K, BLOCK, IPT, MSD>;
   constexpr int P = (int)sizeof(K);
   constexpr int Q = Ly::Q;
-  constexpr int WPQ = Ly::WARPS / Q;  // warps per digit-thread group
   extern __shared__ __align__(128) unsigned char dsm[];
-  __shared__ uint32_t s_q[Q][RADIX];    // per-group partial sums
-  __shared__ uint32_t s_q2[Q][RADIX];   // per-group partial digit totals
-  __shared__ uint32_t s_tpart[RADIX];   // tile-local digit start within its warp of digits
-  __shared__ uint32_t s_tstart[RADIX];  // tile-local start of each digit
-  __shared__ uint32_t s_off[RADIX];     // global position - staging index, per digit
+  __shared__ uint32_t s_q[Q][RADIX];
+  __shared__ uint32_t s_q2[Q][RADIX];
+  __shared__ uint32_t s_tpart[RADIX];
+  __shared__ uint32_t s_tstart[RADIX];
+  __shared__ uint32_t s_off[RADIX];
   __shared__ uint32_t s_wsum[RADIX / 32];
   __shared__ uint32_t s_or[4];
+  __shared__ uint32_t s_seg[3];  // MSD: segment start, end, largest bucket
   __shared__ int s_ok;
 
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t lt_mask = (1u << lane) - 1u;
   const uint32_t c = blockIdx.x, G = gridDim.x;
   const uint64_t n = a.n;
   const uint64_t tbase = (uint64_t)c * Ly::TILE;
   const uint32_t tile_n = n - tbase < (uint64_t)Ly::TILE ? (uint32_t)(n - tbase) : (uint32_t)Ly::TILE;
   const uint32_t wofs = warp * Ly::SEG + lane;
-  uint32_t* cnt = reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF);
-  uint32_t* wcnt = cnt + warp * RADIX;
-  uint8_t* wrep = dsm + Ly::REP_OFF + warp * RADIX;
+  const ResShared sh{reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF), dsm + Ly::REP_OFF, s_q, s_q2, s_tpart,
+                     s_tstart, s_off, s_wsum, s_or};
+  uint32_t* wcnt = sh.cnt + warp * RADIX;
+  uint8_t* wrep = sh.rep + warp * RADIX;
   K* stage = reinterpret_cast<K*>(dsm + Ly::STAGE_OFF);
   SortCtl* ctl = a.ctl;
-  uint32_t* grp = a.acc;                                   // [P][groups][RADIX]
-  uint32_t* orand = a.acc + (size_t)P * a.groups * RADIX;  // or lo, or hi, ~and lo, ~and hi
+  uint32_t* grp = a.acc;                                         // [P + 1][groups][RADIX]
+  uint32_t* orand = a.acc + (size_t)(P + 1) * a.groups * RADIX;  // or lo, or hi, ~and lo, ~and hi
   unsigned* bar = orand + 4;
   unsigned nbar = 0;
-  const uint32_t d_me = tid % RADIX, q_me = tid / RADIX;
-  const uint32_t g_me = c / RES_GROUP, ngrp = (G + RES_GROUP - 1) / RES_GROUP;
+  const uint32_t g_me = c / RES_GROUP;
+  K* kout = static_cast<K*>(a.kout);
 
   auto finish = [&]() {  // hand a device-side error to the host
     if (tid == 0) {
@@ -164,11 +391,52 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
       if (e != 0) *(volatile int*)a.host_err = e;
     }
   };
+  auto zero_cnt = [&]() {
+    for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) sh.cnt[i] = 0;
+  };
+  // publish the CTA's digit counts of accumulator slot `slot`
+  auto publisher = [&](int slot, bool with_or) {
+    return [&, slot, with_or](uint32_t tot) {
+      __stcg(&a.counts[((size_t)slot * G + c) * RADIX + tid], tot);
+      if (tot) atomicAdd(&grp[((size_t)slot * a.groups + g_me) * RADIX + tid], tot);
+      if (with_or && tid < 4 && s_or[tid]) atomicOr(&orand[tid], s_or[tid]);
+    };
+  };
+  auto or_reduce = [&](K kor, K kandn) {  // one shared OR per warp
+    const uint32_t lo_or = __reduce_or_sync(0xffffffffu, (uint32_t)kor);
+    const uint32_t lo_an = __reduce_or_sync(0xffffffffu, (uint32_t)kandn);
+    uint32_t hi_or = 0, hi_an = 0;
+    if constexpr (sizeof(K) == 8) {
+      hi_or = __reduce_or_sync(0xffffffffu, (uint32_t)((uint64_t)kor >> 32));
+      hi_an = __reduce_or_sync(0xffffffffu, (uint32_t)((uint64_t)kandn >> 32));
+    }
+    if (lane == 0) {
+      atomicOr(&s_or[0], lo_or);
+      atomicOr(&s_or[1], hi_or);
+      atomicOr(&s_or[2], lo_an);
+      atomicOr(&s_or[3], hi_an);
+    }
+  };
+  auto plan_of = [&]() -> uint32_t {  // digits that vary across all keys
+    const unsigned long long o = ((unsigned long long)__ldcg(&orand[1]) << 32) | __ldcg(&orand[0]);
+    const unsigned long long an = ((unsigned long long)__ldcg(&orand[3]) << 32) | __ldcg(&orand[2]);
+    const unsigned long long varying = o & an;
+    uint32_t e = 0;
+#pragma unroll
+    for (int pp = 0; pp < P; ++pp)
+      if ((varying >> (RADIX_BITS * pp)) & (RADIX - 1)) e |= 1u << pp;
+    return e;
+  };
 
   // clear the next launch's accumulators and this CTA's counters
   for (uint32_t i = c * BLOCK + tid; i < a.acc_words; i += G * BLOCK) a.acc_next[i] = 0;
-  for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
+  zero_cnt();
   if (tid < 4) s_or[tid] = 0;
+  if (tid == 0) {
+    s_seg[0] = (uint32_t)n;
+    s_seg[1] = (uint32_t)n;
+    s_seg[2] = 0;
+  }
 
   // ---- keys -> registers (forward order transform) -----------------------------
   K key[IPT];
@@ -190,145 +458,119 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
   __syncthreads();
 
   Ranks<IPT, true> rank;
-  K* kout = static_cast<K*>(a.kout);
-  bool moved = false;           // some pass has scattered: keys are no longer in input order
-  uint32_t exec = 0xffffffffu;  // passes that run (known after the first barrier)
-  uint32_t last_exec = P - 1;
+  uint32_t exec = 0;
+  bool planned = false;
 
-  for (int p = 0; p < P; ++p) {
-    if (!((exec >> p) & 1u)) continue;
-    const int shift = p * RADIX_BITS;
-    auto digit = [&](K k) -> uint32_t { return (uint32_t)(k >> shift) & (RADIX - 1); };
-
-    // ---- 1. warp-local ranks ------------------------------------------------------
-    if (!moved) {
+  if constexpr (MSD) {
+    // ---- partition by the top digit -------------------------------------------------
+    constexpr int TOP = (P - 1) * RADIX_BITS;
+    res_rank<K, IPT, true>(key, rank, IPT, wofs, tile_n, TOP, true, wcnt, wrep);
+    or_reduce(kor, kandn);
+    __syncthreads();
+    res_warp_starts<BLOCK>(sh, publisher(P, true));
+    if (a.test_skip_arrival && c == 0) return;
+    if (!res_grid_sync(bar, ++nbar, a.timeout_ns, ctl, a.host_err, &s_ok)) return finish();
+    exec = plan_of();
+    planned = true;
+    if (exec == 0) {  // every key equal: the output is the input
+      if (a.kout != a.kin) {
 #pragma unroll
-      for (int k = 0; k < IPT; ++k) {
-        const bool valid = (wofs + k * 32) < tile_n;
-        rank.set(k, valid ? atomicAdd(&wcnt[digit(key[k])], 1u) : 0u);
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < IPT; ++k) {
-        const bool valid = (wofs + k * 32) < tile_n;
-        const uint32_t d = digit(key[k]);
-        if (valid) wrep[d] = (uint8_t)lane;
-        __syncwarp();
-        const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
-        uint32_t diff = 0;
-#pragma unroll
-        for (int b = 0; b < 5; ++b) {
-          const uint32_t bit = (own >> b) & 1u;
-          diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
+        for (int k = 0; k < IPT; ++k) {
+          const uint32_t li = wofs + k * 32;
+          if (li < tile_n) kout[tbase + li] = from_ordered<K, XF>(key[k]);
         }
-        const uint32_t peers = ~diff;
-        uint32_t old = 0;
-        if (valid) old = wcnt[d];
-        __syncwarp();
-        if (valid && lane == own) wcnt[d] = old + __popc(peers);
-        __syncwarp();
-        rank.set(k, old + __popc(peers & lt_mask));
       }
+      return finish();
     }
-    if (p == 0) {  // which digits vary across all keys: one shared OR per warp
-      const uint32_t lo_or = __reduce_or_sync(0xffffffffu, (uint32_t)kor);
-      const uint32_t lo_an = __reduce_or_sync(0xffffffffu, (uint32_t)kandn);
-      uint32_t hi_or = 0, hi_an = 0;
-      if constexpr (sizeof(K) == 8) {
-        hi_or = __reduce_or_sync(0xffffffffu, (uint32_t)((uint64_t)kor >> 32));
-        hi_an = __reduce_or_sync(0xffffffffu, (uint32_t)((uint64_t)kandn >> 32));
-      }
-      if (lane == 0) {
-        atomicOr(&s_or[0], lo_or);
-        atomicOr(&s_or[1], hi_or);
-        atomicOr(&s_or[2], lo_an);
-        atomicOr(&s_or[3], hi_an);
-      }
+    const uint32_t tot = res_offsets<BLOCK, Ly::MAXG, Ly::MAXW>(sh, grp, a.counts, a.groups, P, true);
+    if (tid < RADIX) {  // the largest bucket
+      const uint32_t m = __reduce_max_sync(0xffffffffu, tot);
+      if (lane == 0) atomicMax(&s_seg[2], m);
     }
     __syncthreads();
-
-    // ---- 2. CTA digit counts, warp prefixes, tile-local digit starts -------------
-    {
-      uint32_t sum = 0;
-#pragma unroll
-      for (int w = 0; w < WPQ; ++w) sum += cnt[(q_me * WPQ + w) * RADIX + d_me];
-      s_q[q_me][d_me] = sum;
-    }
-    __syncthreads();
-    {
-      uint32_t run = 0, tot = 0;
-#pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        const uint32_t v = s_q[q][d_me];
-        if (q < (int)q_me) run += v;
-        tot += v;
-      }
-      // exclusive prefix over the warps, per digit
-#pragma unroll
-      for (int w = 0; w < WPQ; ++w) {
-        uint32_t* cw = &cnt[(q_me * WPQ + w) * RADIX + d_me];
-        const uint32_t v = *cw;
-        *cw = run;
-        run += v;
-      }
+    if (((exec >> (P - 1)) & 1u) && s_seg[2] <= (uint32_t)Ly::TILE) {
+      // this CTA's segment: the buckets starting in [c*TILE, (c+1)*TILE)
       if (tid < RADIX) {
-        __stcg(&a.counts[((size_t)p * G + c) * RADIX + tid], tot);
-        if (tot) atomicAdd(&grp[((size_t)p * a.groups + g_me) * RADIX + tid], tot);
-        // tile-local digit starts: exclusive scan of tot over the digits
-        uint32_t x = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-          if ((int)lane >= o) x += y;
-        }
-        if (lane == 31) s_wsum[warp] = x;
-        s_tpart[tid] = x - tot;
+        const uint32_t st = s_q2[0][tid], prev = tid ? s_q2[0][tid - 1] : 0u;
+        const uint32_t t0 = c * (uint32_t)Ly::TILE, t1 = t0 + (uint32_t)Ly::TILE;
+        if (st >= t0 && (tid == 0 || prev < t0)) s_seg[0] = st;
+        if (st >= t1 && (tid == 0 || prev < t1)) s_seg[1] = st;
       }
-      if (p == 0 && tid < 4) {
-        const uint32_t v = s_or[tid];
-        if (v) atomicOr(&orand[tid], v);
-      }
-    }
-    __syncthreads();
-    {  // fold the tile-local digit start into the warp prefixes
-      uint32_t ts = s_tpart[d_me];
-      for (uint32_t w = 0; w < (d_me >> 5); ++w) ts += s_wsum[w];
-      if (q_me == 0) s_tstart[d_me] = ts;
-#pragma unroll
-      for (int w = 0; w < WPQ; ++w) cnt[(q_me * WPQ + w) * RADIX + d_me] += ts;
-    }
+      res_scatter<K, XF, BLOCK, IPT, Ly::STAGE_KEYS, true>(sh, stage, key, rank, wofs, tile_n, TOP, kout, n, false,
+                                                            ctl);
+      zero_cnt();
+      if (!res_grid_sync(bar, ++nbar, a.timeout_ns, ctl, a.host_err, &s_ok)) return finish();
 
-    // ---- 3. grid barrier: every CTA's counts are in ------------------------------
+      // ---- sort the segment in shared memory: LSD passes, no grid barrier -----------
+      constexpr int NB = 2 * IPT;
+      const uint32_t seg_lo = s_seg[0], L = s_seg[1] - s_seg[0];
+      const int rows = (int)((L + BLOCK - 1) / BLOCK);
+      const uint32_t wofs_b = warp * 32 * (uint32_t)rows + lane;
+      K kb[NB];
+#pragma unroll
+      for (int k = 0; k < NB; ++k) {
+        const uint32_t i = wofs_b + k * 32;
+        kb[k] = (k < rows && i < L) ? __ldcg(kout + seg_lo + i) : K(0);
+      }
+      Ranks<NB, true> rb;
+      const uint32_t last = 31 - __clz(exec);
+      bool first = true, oob = false;
+      for (int p = 0; p < P; ++p) {
+        if (!((exec >> p) & 1u)) continue;
+        const int shift = p * RADIX_BITS;
+        res_rank<K, NB, true>(kb, rb, rows, wofs_b, L, shift, first, wcnt, wrep);
+        __syncthreads();
+        res_warp_starts<BLOCK>(sh, [](uint32_t) {});
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+          if (k < rows && wofs_b + k * 32 < L) {
+            const uint32_t si = wcnt[(uint32_t)(kb[k] >> shift) & (RADIX - 1)] + rb.get(k);
+            if (si < L)
+              stage[si] = kb[k];
+            else
+              oob = true;
+          }
+        }
+        __syncthreads();
+        first = false;
+        if ((uint32_t)p == last) break;
+#pragma unroll
+        for (int k = 0; k < NB; ++k) {
+          const uint32_t i = wofs_b + k * 32;
+          if (k < rows && i < L) kb[k] = stage[i];
+        }
+        zero_cnt();
+        __syncthreads();
+      }
+      if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
+      for (uint32_t i = tid; i < L; i += BLOCK) kout[seg_lo + i] = from_ordered<K, XF>(stage[i]);
+      return finish();
+    }
+    // a bucket holds more than a tile: nothing was written, the LSD passes
+    // below start from the keys still in registers
+    zero_cnt();
+    __syncthreads();
+  }
+
+  // ---- LSD passes ----------------------------------------------------------------
+  bool moved = false;  // some pass has scattered: keys are no longer in input order
+  uint32_t last_exec = P - 1;
+  if (planned) last_exec = 31 - __clz(exec);
+  for (int p = 0; p < P; ++p) {
+    if (planned && !((exec >> p) & 1u)) continue;
+    const int shift = p * RADIX_BITS;
+    res_rank<K, IPT, true>(key, rank, IPT, wofs, tile_n, shift, !moved, wcnt, wrep);
+    if (!planned) or_reduce(kor, kandn);
+    __syncthreads();
+    res_warp_starts<BLOCK>(sh, publisher(p, !planned));
     // (failure-path test: CTA 0 never arrives, so every other CTA's bounded
     // wait runs out and records DEV_ERR_TIMEOUT)
     if (a.test_skip_arrival && c == 0) return;
     if (!res_grid_sync(bar, ++nbar, a.timeout_ns, ctl, a.host_err, &s_ok)) return finish();
-
-    // ---- 4. output base of each digit: loads first, the plan meanwhile -------------
-    uint32_t gv[Ly::MAXG], wv[Ly::MAXW];
-    {
-      const uint32_t* gp = grp + (size_t)p * a.groups * RADIX + d_me;
-      const uint32_t* cp = a.counts + ((size_t)p * G + g_me * RES_GROUP) * RADIX + d_me;
-      const uint32_t nw = c - g_me * RES_GROUP;
-#pragma unroll
-      for (int i = 0; i < Ly::MAXG; ++i) {
-        const uint32_t g = q_me + i * Q;
-        gv[i] = g < ngrp ? __ldcg(gp + (size_t)g * RADIX) : 0u;
-      }
-#pragma unroll
-      for (int i = 0; i < Ly::MAXW; ++i) {
-        const uint32_t j = q_me + i * Q;
-        wv[i] = j < nw ? __ldcg(cp + (size_t)j * RADIX) : 0u;
-      }
-    }
-    if (p == 0) {
-      const unsigned long long o = ((unsigned long long)__ldcg(&orand[1]) << 32) | __ldcg(&orand[0]);
-      const unsigned long long an = ((unsigned long long)__ldcg(&orand[3]) << 32) | __ldcg(&orand[2]);
-      const unsigned long long varying = o & an;
-      exec = 0;
-#pragma unroll
-      for (int pp = 0; pp < P; ++pp)
-        if ((varying >> (RADIX_BITS * pp)) & (RADIX - 1)) exec |= 1u << pp;
+    if (!planned) {
+      exec = plan_of();
+      planned = true;
       if (exec == 0) {  // every key equal: the output is the input
         if (a.kout != a.kin) {
 #pragma unroll
@@ -340,81 +582,18 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
         return finish();
       }
       last_exec = 31 - __clz(exec);
-      if (!(exec & 1u)) {  // digit 0 never varies: nothing moves in this pass
-        for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
+      if (!((exec >> p) & 1u)) {  // this digit never varies: nothing moves in this pass
+        zero_cnt();
         __syncthreads();
         continue;
       }
     }
-    {
-      uint32_t tot = 0, pre = 0;
-#pragma unroll
-      for (int i = 0; i < Ly::MAXG; ++i) {
-        tot += gv[i];
-        if (q_me + i * Q < g_me) pre += gv[i];
-      }
-#pragma unroll
-      for (int i = 0; i < Ly::MAXW; ++i) pre += wv[i];
-      s_q[q_me][d_me] = pre;
-      s_q2[q_me][d_me] = tot;
-    }
-    __syncthreads();
-    if (tid < RADIX) {
-      uint32_t tot = 0, pre = 0;
-#pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        tot += s_q2[q][tid];
-        pre += s_q[q][tid];
-      }
-      uint32_t x = tot;  // digit starts: exclusive scan of the totals
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
-        if ((int)lane >= o) x += y;
-      }
-      if (lane == 31) s_wsum[warp] = x;
-      s_off[tid] = x - tot + pre - s_tstart[tid];
-    }
-
-    // ---- 5. stage in digit order, write coalesced ---------------------------------
-    bool oob = false;
-#pragma unroll
-    for (int k = 0; k < IPT; ++k) {
-      if ((wofs + k * 32) < tile_n) {
-        const uint32_t si = wcnt[digit(key[k])] + rank.get(k);
-        if (si < (uint32_t)Ly::TILE)
-          stage[si] = key[k];
-        else
-          oob = true;
-      }
-    }
-    __syncthreads();
-    if (tid < RADIX) {
-      uint32_t add = 0;
-      for (uint32_t w = 0; w < (tid >> 5); ++w) add += s_wsum[w];
-      s_off[tid] += add;
-    }
-    __syncthreads();
-    const bool xout = (uint32_t)p == last_exec;
-    const uint64_t lastpos = n - 1;
-#pragma unroll
-    for (int j = 0; j < IPT; ++j) {
-      const uint32_t i = j * BLOCK + tid;
-      if (i < tile_n) {
-        const K kk = stage[i];
-        const uint64_t pos = (uint64_t)s_off[digit(kk)] + i;
-        if (pos <= lastpos)
-          kout[pos] = xout ? from_ordered<K, XF>(kk) : kk;
-        else
-          oob = true;
-      }
-    }
-    if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
+    res_offsets<BLOCK, Ly::MAXG, Ly::MAXW>(sh, grp, a.counts, a.groups, p, false);
+    res_scatter<K, XF, BLOCK, IPT, Ly::STAGE_KEYS, true>(sh, stage, key, rank, wofs, tile_n, shift, kout, n,
+                                                          (uint32_t)p == last_exec, ctl);
     moved = true;
     if ((uint32_t)p == last_exec) break;
-
-    // ---- 6. grid barrier, then this CTA's positions of the output again -----------
-    for (int i = tid; i < Ly::WARPS * RADIX; i += BLOCK) cnt[i] = 0;
+    zero_cnt();
     if (!res_grid_sync(bar, ++nbar, a.timeout_ns, ctl, a.host_err, &s_ok)) return finish();
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {

@@ -650,11 +650,18 @@ uint64_t resident_max_keys(int sm_count) {
   return (uint64_t)(sm_count < RES_MAX_CTAS ? sm_count : RES_MAX_CTAS) * RES_BLOCK * RES_IPT_MAX;
 }
 
+// Most-significant-digit first (a partition, then segments sorted in shared
+// memory) where the segment keys fit the registers: up to 7 keys per thread.
+#ifndef FS_RES_MSD
+#define FS_RES_MSD 1
+#endif
+
 template <typename K, int XF, int IPT>
 int launch_resident(fs_sorter* s, const PlanArgs& a) {
-  using Ly = ResLayout<K, RES_BLOCK, IPT>;
+  constexpr bool MSD = FS_RES_MSD && IPT <= 7;
+  using Ly = ResLayout<K, RES_BLOCK, IPT, MSD>;
   constexpr int P = (int)sizeof(K);
-  auto kern = k_resident_sort<K, XF, RES_BLOCK, IPT>;
+  auto kern = k_resident_sort<K, XF, RES_BLOCK, IPT, MSD>;
   static std::atomic<int> bps_dev[MAX_DEVICES];  // resident CTAs per SM, 0 = not configured yet
   int bps = bps_dev[s->device].load();
   if (bps == 0) {
@@ -673,9 +680,10 @@ int launch_resident(fs_sorter* s, const PlanArgs& a) {
   // so a launch that failed still leaves that set clean)
   const uint32_t max_grid = (uint32_t)RES_MAX_CTAS;
   const uint32_t groups = (max_grid + RES_GROUP - 1) / RES_GROUP;
-  const size_t set_words = res_acc_words(MAX_PASSES, groups);
+  const size_t set_words = res_acc_words(MAX_PASSES + 1, groups);  // a slot per pass, one for the partition
   int rc = grow(s, &s->res_acc, &s->res_acc_bytes, 2 * set_words * 4, true);
-  if (!rc) rc = grow(s, &s->res_counts, &s->res_counts_bytes, (size_t)MAX_PASSES * max_grid * RADIX * 4, false);
+  if (!rc)
+    rc = grow(s, &s->res_counts, &s->res_counts_bytes, (size_t)(MAX_PASSES + 1) * max_grid * RADIX * 4, false);
   if (rc) return rc;
   uint32_t* acc = static_cast<uint32_t*>(s->res_acc);
   ResArgs ra{};
@@ -701,7 +709,7 @@ int launch_resident(fs_sorter* s, const PlanArgs& a) {
   t_end(e);
   s->res_parity ^= 1;
   s->last_launches = 1;
-  static_assert(P <= MAX_PASSES, "accumulator sets sized for MAX_PASSES");
+  static_assert(P <= MAX_PASSES, "accumulator sets sized for MAX_PASSES + 1 slots");
   return FS_OK;
 }
 

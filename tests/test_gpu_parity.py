@@ -136,12 +136,28 @@ def test_single_launch_matches_chain_and_oracle(dt, dist, n):
             assert np.array_equal(out.cpu().numpy().view(xb.dtype), want)
             assert np.array_equal(b.cpu().numpy().view(xb.dtype), xb)  # input untouched
         assert one.last_launch_count() == (1 if kb == 4 else 2 + 3 * kb)
-        # low bits only vary: odd and even numbers of executed passes
+        # low bits only vary: odd and even numbers of executed passes (and,
+        # for 32-bit keys, a top digit that never varies: the single launch
+        # falls back from the top-digit partition to the LSD passes)
         for mask_bits in (8, 16, 24):
             y = (xb & xb.dtype.type((1 << mask_bits) - 1)).view(orc.NP_DTYPE[dt])
             a = torch.from_numpy(np.ascontiguousarray(y).view(iv).copy()).cuda()
             one.sort_device(dt, a.data_ptr(), n)
             assert np.array_equal(a.cpu().numpy().view(xb.dtype), bits(orc.sort_keys(y, dt), dt)), mask_bits
+        # 32-bit keys: only the top byte varies (the partition alone orders
+        # them); two top-digit buckets (each larger than a tile: fallback);
+        # the top byte and the low byte vary
+        if kb == 4:
+            for mask in (0xFF000000, 0x100000FF):
+                y = (xb & xb.dtype.type(mask)).view(orc.NP_DTYPE[dt])
+                a = torch.from_numpy(np.ascontiguousarray(y).view(iv).copy()).cuda()
+                one.sort_device(dt, a.data_ptr(), n)
+                assert np.array_equal(a.cpu().numpy().view(xb.dtype), bits(orc.sort_keys(y, dt), dt)), hex(mask)
+            y = (xb & xb.dtype.type(0xFF0000FF)).view(orc.NP_DTYPE[dt])
+            a = torch.from_numpy(np.ascontiguousarray(y).view(iv).copy()).cuda()
+            out = torch.empty_like(a)
+            one.sort_device_copy(dt, a.data_ptr(), out.data_ptr(), n)
+            assert np.array_equal(out.cpu().numpy().view(xb.dtype), bits(orc.sort_keys(y, dt), dt))
         z = np.full(n, 7, orc.NP_DTYPE[dt])  # nothing varies
         a = torch.from_numpy(np.ascontiguousarray(z).view(iv).copy()).cuda()
         out = torch.empty_like(a)
@@ -161,7 +177,7 @@ def test_single_launch_alternating_sizes():
     s = GpuSorter.new()
     s.set_single_launch_max(8 << 20)
     try:
-        sizes = [1 << 20, 8193, (1 << 21) - 5, 300_001, 65_537, 1 << 20, 500_000]
+        sizes = [1 << 20, 8193, (1 << 21) - 5, 300_001, 65_537, 1 << 20, 500_000, 20_000, 150_000]
         cases = []
         for i, n in enumerate(sizes * 2):
             dt, dist = DT_DIST[i % len(DT_DIST)]
