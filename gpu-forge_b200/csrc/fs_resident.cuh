@@ -116,12 +116,15 @@ struct ResLayout {
   static constexpr int MAXG = ((RES_MAX_CTAS + RES_GROUP - 1) / RES_GROUP + Q - 1) / Q;  // group loads a thread
   static constexpr int MAXW = (RES_GROUP - 1 + Q - 1) / Q;  // in-group count loads a thread
   // dynamic shared memory: [warp digit counters | warp digit owners | staged
-  // keys: one tile, or (MSD) a segment of up to two tiles]
-  static constexpr int STAGE_KEYS = MSD ? 2 * TILE : TILE;
+  // keys: one tile, or (MSD) two buffers of a segment of up to two tiles,
+  // rounded up to whole 256-key runs]
+  static constexpr int STAGE_KEYS = MSD ? (2 * TILE + 255) / 256 * 256 : TILE;
   static constexpr size_t CNT_OFF = 0;
   static constexpr size_t REP_OFF = CNT_OFF + (size_t)WARPS * RADIX * 4;
   static constexpr size_t STAGE_OFF = REP_OFF + (size_t)WARPS * RADIX;
-  static constexpr size_t BYTES = STAGE_OFF + (size_t)STAGE_KEYS * sizeof(K);
+  static constexpr size_t BYTES =
+      STAGE_OFF + (MSD ? 2 * (size_t)(STAGE_KEYS + STAGE_KEYS / 32) : (size_t)STAGE_KEYS) * sizeof(K);
+  static_assert(!MSD || 2 * TILE <= 16 * BLOCK, "a merge level covers a segment in one round");
   static_assert(BLOCK % RADIX == 0 && WARPS % Q == 0, "whole warps per digit-thread group");
   static_assert(STAGE_OFF % 16 == 0, "staging alignment");
 };
@@ -343,6 +346,123 @@ __device__ __forceinline__ void res_scatter(const ResShared& sh, K* stage, const
   if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
 }
 
+// ---- merge sort of a segment in shared memory (keys only) ----------------------
+// Equal keys are identical bits, so no order among them has to be kept: a
+// bitonic sort of 256 keys per warp in registers, then merge-path merges of
+// sorted runs between two shared-memory buffers.
+constexpr int RES_RUN = 256;  // keys a warp sorts in registers (8 a lane)
+
+// Bitonic sort of 256 keys held blocked across the warp (lane l holds
+// elements 8l .. 8l+7): the three low index bits are a lane's registers,
+// the five high bits its lane number.
+template <typename K>
+__device__ __forceinline__ void warp_sort256(K (&x)[8]) {
+  const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= RES_RUN; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 8) {  // partner: same register of lane ^ (j / 8)
+        const uint32_t lm = (uint32_t)j >> 3;
+        const bool lower = (lane & lm) == 0;
+        const bool up = ((lane * 8) & (uint32_t)k) == 0;  // k >= 16: the block direction is the lane's
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const K y = __shfl_xor_sync(0xffffffffu, x[i], lm);
+          x[i] = (lower == up) ? (x[i] < y ? x[i] : y) : (x[i] < y ? y : x[i]);
+        }
+      } else {  // partner: register i ^ j of the same lane
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int pi = i ^ j;
+          if (pi > i) {
+            const bool up = ((lane * 8 + (uint32_t)i) & (uint32_t)k) == 0;
+            const K lo = x[i] < x[pi] ? x[i] : x[pi];
+            const K hi = x[i] < x[pi] ? x[pi] : x[i];
+            x[i] = up ? lo : hi;
+            x[pi] = up ? hi : lo;
+          }
+        }
+      }
+    }
+  }
+}
+
+// Segment buffers are indexed with one padding word per 32 keys, so that
+// lanes 8 keys apart (a lane's run slice, a thread's merge outputs) fall in
+// different banks.
+__device__ __forceinline__ uint32_t res_pad(uint32_t i) { return i + (i >> 5); }
+__host__ __device__ constexpr uint32_t res_padded(uint32_t n) { return n + n / 32; }
+
+// One merge level: the sorted runs of length r in src[0, len) merged in
+// pairs into dst (len a multiple of RES_RUN, r a power of two >= RES_RUN,
+// len <= PER * BLOCK).  Thread t writes outputs [PER*t, PER*t + PER): a
+// binary search on its merge-path diagonal, then PER merge steps.
+template <typename K, int BLOCK, int PER>
+__device__ __forceinline__ void res_merge_level(const K* src, K* dst, uint32_t len, uint32_t r) {
+  const uint32_t o0 = threadIdx.x * PER;
+  if (o0 >= len) return;
+  const uint32_t base = o0 & ~(2 * r - 1);
+  const uint32_t la = min(r, len - base);
+  const uint32_t lb = min(r, len - base - la);
+  const uint32_t a0 = base, b0 = base + la;
+  const uint32_t diag = o0 - base;
+  uint32_t lo = diag > lb ? diag - lb : 0u, hi = min(diag, la);
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (src[res_pad(a0 + mid)] <= src[res_pad(b0 + diag - 1 - mid)])
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  // merge steps without divergence: one load a step, of the run that advanced
+  uint32_t ia = lo, ib = diag - lo;
+  K ka = ia < la ? src[res_pad(a0 + ia)] : K(0), kb = ib < lb ? src[res_pad(b0 + ib)] : K(0);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const bool take_a = ib >= lb || (ia < la && ka <= kb);
+    dst[res_pad(o0 + e)] = take_a ? ka : kb;
+    ia += take_a;
+    ib += !take_a;
+    const uint32_t nx = take_a ? a0 + ia : b0 + ib;
+    const bool in = take_a ? ia < la : ib < lb;
+    const K v = in ? src[res_pad(nx)] : K(0);
+    ka = take_a ? v : ka;
+    kb = take_a ? kb : v;
+  }
+}
+
+// Top-bits partition of the MSD form: 2^RES_MB buckets (about 512 keys each
+// at 2^20 uniform keys, so every CTA's segment stays close to one tile).
+constexpr int RES_MB = 11;
+constexpr int RES_MR = 1 << RES_MB;
+
+// Exclusive scan of one value a thread over the block (w32: 32 words of
+// shared memory).  Two block barriers.
+template <int BLOCK>
+__device__ __forceinline__ uint32_t res_block_exclusive_scan(uint32_t v, uint32_t* w32) {
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if ((int)lane >= o) x += y;
+  }
+  if (lane == 31) w32[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t t = lane < (uint32_t)(BLOCK / 32) ? w32[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, t, o);
+      if ((int)lane >= o) t += y;
+    }
+    w32[lane] = t;  // inclusive over warps
+  }
+  __syncthreads();
+  return x - v + (warp ? w32[warp - 1] : 0u);
+}
+
 // MSD: first partition by the top digit across the grid (one pass, ranked
 // with shared atomics), then each CTA sorts a segment of whole top-digit
 // buckets -- those starting in its tile's range, at most two tiles when no
@@ -364,6 +484,7 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
   __shared__ uint32_t s_wsum[RADIX / 32];
   __shared__ uint32_t s_or[4];
   __shared__ uint32_t s_seg[3];  // MSD: segment start, end, largest bucket
+  __shared__ uint32_t s_w32[32];
   __shared__ int s_ok;
 
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -378,8 +499,10 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
   uint8_t* wrep = sh.rep + warp * RADIX;
   K* stage = reinterpret_cast<K*>(dsm + Ly::STAGE_OFF);
   SortCtl* ctl = a.ctl;
-  uint32_t* grp = a.acc;                                         // [P + 1][groups][RADIX]
-  uint32_t* orand = a.acc + (size_t)(P + 1) * a.groups * RADIX;  // or lo, or hi, ~and lo, ~and hi
+  // [P][groups][RADIX] per digit pass, then (MSD) [groups][RES_MR] for the partition
+  constexpr int SLOTS = P + (MSD ? RES_MR / RADIX : 0);
+  uint32_t* grp = a.acc;
+  uint32_t* orand = a.acc + (size_t)SLOTS * a.groups * RADIX;  // or lo, or hi, ~and lo, ~and hi
   unsigned* bar = orand + 4;
   unsigned nbar = 0;
   const uint32_t g_me = c / RES_GROUP;
@@ -462,16 +585,83 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
   bool planned = false;
 
   if constexpr (MSD) {
-    // ---- partition by the top digit -------------------------------------------------
-    constexpr int TOP = (P - 1) * RADIX_BITS;
-    res_rank<K, IPT, true>(key, rank, IPT, wofs, tile_n, TOP, true, wcnt, wrep);
+    // ---- partition by the top MB bits --------------------------------------------------
+    // CTA-wide counters (ranks by shared atomics: keys only, any order among
+    // equal buckets), MR / BLOCK buckets a thread for the scans and offsets
+    constexpr int DPT = RES_MR / BLOCK;
+    constexpr int MSHIFT = 8 * P - RES_MB;
+    static_assert(RES_MR % BLOCK == 0 && RES_MR <= Ly::WARPS * RADIX, "bucket counters fit the warp counters");
+    static_assert(res_padded(Ly::STAGE_KEYS) * sizeof(K) >= 2 * RES_MR * sizeof(uint32_t),
+                  "bucket offsets and starts fit the idle segment buffer");
+    uint32_t* mcnt = sh.cnt;                                  // [MR]: counts, then tile-local starts
+    uint32_t* moff = reinterpret_cast<uint32_t*>(stage + res_padded(Ly::STAGE_KEYS));  // [MR] in the idle buffer
+    uint32_t* mstart = moff + RES_MR;                         // [MR] bucket starts
+    uint32_t* grp_m = grp + (size_t)P * a.groups * RADIX;     // [groups][MR]
+    uint32_t* cnt_m = a.counts + (size_t)P * G * RADIX;       // [G][MR]
+    uint32_t mr[IPT];
+#pragma unroll
+    for (int k = 0; k < IPT; ++k)
+      mr[k] = (wofs + k * 32 < tile_n) ? atomicAdd(&mcnt[(uint32_t)(key[k] >> MSHIFT)], 1u) : 0u;
     or_reduce(kor, kandn);
     __syncthreads();
-    res_warp_starts<BLOCK>(sh, publisher(P, true));
+    {
+      uint32_t cv[DPT], sum = 0;
+#pragma unroll
+      for (int j = 0; j < DPT; ++j) {
+        const uint32_t d = tid * DPT + j;
+        cv[j] = mcnt[d];
+        __stcg(&cnt_m[(size_t)c * RES_MR + d], cv[j]);
+        if (cv[j]) atomicAdd(&grp_m[(size_t)g_me * RES_MR + d], cv[j]);
+        sum += cv[j];
+      }
+      if (tid < 4 && s_or[tid]) atomicOr(&orand[tid], s_or[tid]);
+      uint32_t run = res_block_exclusive_scan<BLOCK>(sum, s_w32);
+#pragma unroll
+      for (int j = 0; j < DPT; ++j) {
+        mcnt[tid * DPT + j] = run;
+        run += cv[j];
+      }
+    }
     if (a.test_skip_arrival && c == 0) return;
     if (!res_grid_sync(bar, ++nbar, a.timeout_ns, ctl, a.host_err, &s_ok)) return finish();
-    exec = plan_of();
+    exec = plan_of();  // (its loads are in flight with the offsets' loads)
     planned = true;
+    {
+      // bucket totals (all group sums) and this CTA's prefix (the group sums
+      // before its group, the counts of the CTAs before it in its group)
+      constexpr int NG = (RES_MAX_CTAS + RES_GROUP - 1) / RES_GROUP;
+      const uint32_t ngrp = (G + RES_GROUP - 1) / RES_GROUP, nw = c - g_me * RES_GROUP;
+      uint32_t tot[DPT], pre[DPT], sum = 0, mx = 0;
+#pragma unroll
+      for (int j = 0; j < DPT; ++j) {
+        const uint32_t d = tid * DPT + j;
+        uint32_t t = 0, q = 0;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          const uint32_t v = (uint32_t)g < ngrp ? __ldcg(&grp_m[(size_t)g * RES_MR + d]) : 0u;
+          t += v;
+          if ((uint32_t)g < g_me) q += v;
+        }
+#pragma unroll
+        for (int w = 0; w < RES_GROUP - 1; ++w)
+          q += (uint32_t)w < nw ? __ldcg(&cnt_m[(size_t)(g_me * RES_GROUP + w) * RES_MR + d]) : 0u;
+        tot[j] = t;
+        pre[j] = q;
+        sum += t;
+        mx = max(mx, t);
+      }
+      uint32_t run = res_block_exclusive_scan<BLOCK>(sum, s_w32);
+#pragma unroll
+      for (int j = 0; j < DPT; ++j) {
+        const uint32_t d = tid * DPT + j;
+        mstart[d] = run;
+        moff[d] = run + pre[j] - mcnt[d];
+        run += tot[j];
+      }
+      mx = __reduce_max_sync(0xffffffffu, mx);
+      if (lane == 0) atomicMax(&s_seg[2], mx);
+    }
+    __syncthreads();
     if (exec == 0) {  // every key equal: the output is the input
       if (a.kout != a.kin) {
 #pragma unroll
@@ -482,69 +672,83 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
       }
       return finish();
     }
-    const uint32_t tot = res_offsets<BLOCK, Ly::MAXG, Ly::MAXW>(sh, grp, a.counts, a.groups, P, true);
-    if (tid < RADIX) {  // the largest bucket
-      const uint32_t m = __reduce_max_sync(0xffffffffu, tot);
-      if (lane == 0) atomicMax(&s_seg[2], m);
-    }
-    __syncthreads();
-    if (((exec >> (P - 1)) & 1u) && s_seg[2] <= (uint32_t)Ly::TILE) {
+    if (s_seg[2] <= (uint32_t)Ly::TILE) {
       // this CTA's segment: the buckets starting in [c*TILE, (c+1)*TILE)
-      if (tid < RADIX) {
-        const uint32_t st = s_q2[0][tid], prev = tid ? s_q2[0][tid - 1] : 0u;
+      {
         const uint32_t t0 = c * (uint32_t)Ly::TILE, t1 = t0 + (uint32_t)Ly::TILE;
-        if (st >= t0 && (tid == 0 || prev < t0)) s_seg[0] = st;
-        if (st >= t1 && (tid == 0 || prev < t1)) s_seg[1] = st;
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) {
+          const uint32_t d = tid * DPT + j;
+          const uint32_t st = mstart[d], prev = d ? mstart[d - 1] : 0u;
+          if (st >= t0 && (d == 0 || prev < t0)) s_seg[0] = st;
+          if (st >= t1 && (d == 0 || prev < t1)) s_seg[1] = st;
+        }
       }
-      res_scatter<K, XF, BLOCK, IPT, Ly::STAGE_KEYS, true>(sh, stage, key, rank, wofs, tile_n, TOP, kout, n, false,
-                                                            ctl);
+      // stage in bucket order, write to the buckets' positions
+      bool oob = false;
+#pragma unroll
+      for (int k = 0; k < IPT; ++k) {
+        if (wofs + k * 32 < tile_n) {
+          const uint32_t si = mcnt[(uint32_t)(key[k] >> MSHIFT)] + mr[k];
+          if (si < (uint32_t)Ly::TILE)
+            stage[si] = key[k];
+          else
+            oob = true;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < IPT; ++j) {
+        const uint32_t i = j * BLOCK + tid;
+        if (i < tile_n) {
+          const K kk = stage[i];
+          const uint64_t pos = (uint64_t)moff[(uint32_t)(kk >> MSHIFT)] + i;
+          if (pos < n)
+            kout[pos] = kk;
+          else
+            oob = true;
+        }
+      }
+      if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
       zero_cnt();
       if (!res_grid_sync(bar, ++nbar, a.timeout_ns, ctl, a.host_err, &s_ok)) return finish();
 
-      // ---- sort the segment in shared memory: LSD passes, no grid barrier -----------
-      constexpr int NB = 2 * IPT;
+      // ---- sort the segment in shared memory: warp sorts, then merges ---------------
+      // (the segment is padded to whole runs with all-ones keys, which sort
+      // last; only its first L keys are written back)
       const uint32_t seg_lo = s_seg[0], L = s_seg[1] - s_seg[0];
-      const int rows = (int)((L + BLOCK - 1) / BLOCK);
-      const uint32_t wofs_b = warp * 32 * (uint32_t)rows + lane;
-      K kb[NB];
-#pragma unroll
-      for (int k = 0; k < NB; ++k) {
-        const uint32_t i = wofs_b + k * 32;
-        kb[k] = (k < rows && i < L) ? __ldcg(kout + seg_lo + i) : K(0);
+      if (s_seg[1] < s_seg[0] || L > 2u * Ly::TILE) {  // cannot happen with buckets <= TILE
+        if (tid == 0) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
+        return finish();
       }
-      Ranks<NB, true> rb;
-      const uint32_t last = 31 - __clz(exec);
-      bool first = true, oob = false;
-      for (int p = 0; p < P; ++p) {
-        if (!((exec >> p) & 1u)) continue;
-        const int shift = p * RADIX_BITS;
-        res_rank<K, NB, true>(kb, rb, rows, wofs_b, L, shift, first, wcnt, wrep);
-        __syncthreads();
-        res_warp_starts<BLOCK>(sh, [](uint32_t) {});
-        __syncthreads();
+      const uint32_t len = (L + RES_RUN - 1) & ~(uint32_t)(RES_RUN - 1);
+      K* buf0 = stage;
+      K* buf1 = stage + res_padded(Ly::STAGE_KEYS);
+      for (uint32_t i = tid; i < len; i += BLOCK) buf0[res_pad(i)] = i < L ? __ldcg(kout + seg_lo + i) : ~K(0);
+      __syncthreads();
+      for (uint32_t run = warp; run * RES_RUN < len; run += Ly::WARPS) {
+        K x[8];
+        const uint32_t b = run * RES_RUN + lane * 8;
 #pragma unroll
-        for (int k = 0; k < NB; ++k) {
-          if (k < rows && wofs_b + k * 32 < L) {
-            const uint32_t si = wcnt[(uint32_t)(kb[k] >> shift) & (RADIX - 1)] + rb.get(k);
-            if (si < L)
-              stage[si] = kb[k];
-            else
-              oob = true;
-          }
-        }
-        __syncthreads();
-        first = false;
-        if ((uint32_t)p == last) break;
+        for (int i = 0; i < 8; ++i) x[i] = buf0[res_pad(b + i)];
+        warp_sort256<K>(x);
 #pragma unroll
-        for (int k = 0; k < NB; ++k) {
-          const uint32_t i = wofs_b + k * 32;
-          if (k < rows && i < L) kb[k] = stage[i];
-        }
-        zero_cnt();
-        __syncthreads();
+        for (int i = 0; i < 8; ++i) buf0[res_pad(b + i)] = x[i];
       }
-      if (oob) atomicCAS(&ctl->err, 0, DEV_ERR_BOUNDS);
-      for (uint32_t i = tid; i < L; i += BLOCK) kout[seg_lo + i] = from_ordered<K, XF>(stage[i]);
+      __syncthreads();
+      K* src = buf0;
+      K* dst = buf1;
+      for (uint32_t r = RES_RUN; r < len; r <<= 1) {
+        if (len <= 8u * BLOCK)
+          res_merge_level<K, BLOCK, 8>(src, dst, len, r);
+        else
+          res_merge_level<K, BLOCK, 16>(src, dst, len, r);
+        __syncthreads();
+        K* t = src;
+        src = dst;
+        dst = t;
+      }
+      for (uint32_t i = tid; i < L; i += BLOCK) kout[seg_lo + i] = from_ordered<K, XF>(src[res_pad(i)]);
       return finish();
     }
     // a bucket holds more than a tile: nothing was written, the LSD passes

@@ -680,10 +680,11 @@ int launch_resident(fs_sorter* s, const PlanArgs& a) {
   // so a launch that failed still leaves that set clean)
   const uint32_t max_grid = (uint32_t)RES_MAX_CTAS;
   const uint32_t groups = (max_grid + RES_GROUP - 1) / RES_GROUP;
-  const size_t set_words = res_acc_words(MAX_PASSES + 1, groups);  // a slot per pass, one for the partition
+  // a slot of RADIX words per digit pass, RES_MR / RADIX slots for the top-bits partition
+  constexpr int SLOTS = MAX_PASSES + RES_MR / RADIX;
+  const size_t set_words = res_acc_words(SLOTS, groups);
   int rc = grow(s, &s->res_acc, &s->res_acc_bytes, 2 * set_words * 4, true);
-  if (!rc)
-    rc = grow(s, &s->res_counts, &s->res_counts_bytes, (size_t)(MAX_PASSES + 1) * max_grid * RADIX * 4, false);
+  if (!rc) rc = grow(s, &s->res_counts, &s->res_counts_bytes, (size_t)SLOTS * max_grid * RADIX * 4, false);
   if (rc) return rc;
   uint32_t* acc = static_cast<uint32_t*>(s->res_acc);
   ResArgs ra{};
@@ -709,7 +710,7 @@ int launch_resident(fs_sorter* s, const PlanArgs& a) {
   t_end(e);
   s->res_parity ^= 1;
   s->last_launches = 1;
-  static_assert(P <= MAX_PASSES, "accumulator sets sized for MAX_PASSES + 1 slots");
+  static_assert(P <= MAX_PASSES, "accumulator sets sized for MAX_PASSES digit passes");
   return FS_OK;
 }
 
