@@ -292,8 +292,11 @@ int fs_partition_count(fs_sorter* s, int dtype, const void* keys, uint64_t n,
                        uint64_t gpos_base, const void* splitter_keys,
                        const uint64_t* splitter_gpos, int nsplit,
                        uint64_t* bucket_counts_host);
-/* Step 2 stores every key of bucket b, in input order, at bucket_dst[b][0 ..
- * count_b) -- bucket_dst (host array of nsplit+1 device pointers) may point
+/* Step 2 stores every key of bucket b at bucket_dst[b][0 .. count_b), in no
+ * particular order within the bucket (keys only: the receiving rank's sort
+ * orders them, and equal keys are identical bits; from 3 buckets up the pass
+ * ranks with shared atomics) -- bucket_dst (host array of nsplit+1 device
+ * pointers) may point
  * into other GPUs' memory (fs_ipc_open), which the kernel writes with plain
  * stores over NVLink; it makes those stores visible system-wide before it
  * ends.  Must directly follow fs_partition_count on the same sorter with the
@@ -322,7 +325,9 @@ int fs_partition_dispatch_pairs(fs_sorter* s, int dtype, const void* keys,
  * fs_partition_count_async: as fs_partition_count, but the bucket sizes go
  * to device memory bucket_counts_dev (nsplit+1 u64), stream-ordered, and the
  * call returns at once.
- * fs_partition_dispatch_matrix: as fs_partition_dispatch(_pairs), with the
+ * fs_partition_dispatch_matrix: as fs_partition_dispatch(_pairs) (with a
+ * payload the keys keep their input order within a bucket, without one they
+ * need not), with the
  * destinations computed on the device: send_matrix (device, G x G u64,
  * G = nsplit+1, row r = the bucket sizes rank r counted, e.g. the counts
  * all-gathered in rank order) and this rank's index `rank` give

@@ -185,7 +185,9 @@ def test_async_count_and_matrix_dispatch(sorter, dt, dist, nspl, payload, with_v
     free form of the sample sort's exchange, as rank r of G ranks on one GPU:
     the counts land in device memory, and bucket b's keys (and values) land in
     inbox b after what the lower ranks send there (rows of the send matrix
-    other than r are made up); nothing else in the inboxes is touched."""
+    other than r are made up); nothing else in the inboxes is touched.  With
+    a payload a bucket keeps the input order; keys alone may arrive in any
+    order within their bucket (compared as multisets)."""
     import torch
     from forge_sort.samplesort import choose_splitters, ordered_bits
     G = nspl + 1
@@ -234,7 +236,10 @@ def test_async_count_and_matrix_dispatch(sorter, dt, dist, nspl, payload, with_v
         lo = int(M[:rank, b].sum())
         c = int(wcounts[b])
         got = inbox_k[b].cpu().numpy().view(bits)
-        assert np.array_equal(got[lo:lo + c], want_k[starts[b]:starts[b] + c]), b
+        if payload:
+            assert np.array_equal(got[lo:lo + c], want_k[starts[b]:starts[b] + c]), b
+        else:
+            assert np.array_equal(np.sort(got[lo:lo + c]), np.sort(want_k[starts[b]:starts[b] + c])), b
         assert bool((inbox_k[b][:lo] == -1).all()) and bool((inbox_k[b][lo + c:] == -1).all()), b
         if payload:
             gv = inbox_v[b].cpu().numpy().view(np.uint32)
