@@ -892,6 +892,15 @@ __global__ void __launch_bounds__(RADIX)
 
 // dst_host / vdst_host: destinations from the host (copied into the table);
 // nullptr: the table was already written on the device (k_dispatch_table).
+// Keys-only dispatch ranks with shared atomics from this many buckets up; with
+// fewer, most lanes of a warp add to the same counter and the stable rank's
+// ballots cost less.  Measured on one B200, 2^28 u32 keys, dispatch ms stable
+// / atomics: 2 buckets 0.943 / 1.180, 3: 1.152 / 1.125, 4: 1.160 / 1.080,
+// 6: 1.160 / 0.989, 8: 1.176 / 0.976.
+#ifndef FS_DISPATCH_UNSTABLE_MIN
+#define FS_DISPATCH_UNSTABLE_MIN 3
+#endif
+
 template <typename K, int XF, int NB, int LV, bool VALS>
 int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t* vals, uint64_t n,
                                   uint64_t gpos_base, const void* spl_keys, const uint64_t* spl_gpos, int nsplit,
@@ -953,14 +962,6 @@ int enqueue_partition_dispatch_nb(fs_sorter* s, const void* keys, const uint32_t
   return FS_OK;
 }
 
-// Keys-only dispatch ranks with shared atomics from this many buckets up; with
-// fewer, most lanes of a warp add to the same counter and the stable rank's
-// ballots cost less.  Measured on one B200, 2^28 u32 keys, dispatch ms stable
-// / atomics: 2 buckets 0.943 / 1.180, 3: 1.152 / 1.125, 4: 1.160 / 1.080,
-// 6: 1.160 / 0.989, 8: 1.176 / 0.976.
-#ifndef FS_DISPATCH_UNSTABLE_MIN
-#define FS_DISPATCH_UNSTABLE_MIN 3
-#endif
 
 // Up to 8 buckets (the GPUs of one box) take the 8-digit instantiation, with
 // the splitters in registers (one compare for 2 buckets, a 3-level tree for
