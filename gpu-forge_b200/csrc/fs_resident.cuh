@@ -1,34 +1,38 @@
-// fs_resident.cuh -- a whole keys-only LSD radix sort in one cooperative
-// launch with every key held in registers, for the sizes where the chained
-// launches of fs_kernels.cuh cost more than their kernels (up to a few
-// million keys).
+// fs_resident.cuh -- a whole keys-only sort of up to a few million 32-bit
+// keys in one cooperative launch, for the sizes where the chained launches of
+// fs_kernels.cuh cost more than their kernels.  One CTA per SM, all resident;
+// CTA c owns positions [c*TILE, (c+1)*TILE) (TILE = BLOCK*IPT) and holds them
+// in registers from its first load.
 //
-// CTA c owns positions [c*TILE, (c+1)*TILE) of the array (TILE = BLOCK*IPT),
-// one CTA per SM, all resident.  Per executed digit pass:
-//   1. rank its TILE keys (registers) by the digit: per-warp counters in
-//      shared memory, shared atomics for the first executed pass (keys only:
-//      order among equal keys is free), owner election + five ballots after;
-//   2. publish the CTA's digit counts (plain stores) and add them to its
-//      16-CTA group's sums (reductions in L2);
-//   3. grid barrier;
-//   4. output base of each digit: the digit totals (all group sums), the
-//      group sums before this CTA's group and the counts of the CTAs before it
-//      in its group -- at most 7 L2 loads a thread, all issued at once;
-//   5. stage the tile in digit order in shared memory, write it coalesced;
-//   6. grid barrier, then load the CTA's positions of the output again.
-// The passes run in place in the output array: a pass's loads all happen
-// before its first barrier and its stores after it.  The first pass's OR /
-// AND words give every CTA the same plan (which digits vary) after the first
-// barrier, so trivial passes cost nothing and the last executed pass applies
-// the inverse order transform.
+// Main form (MSD, up to 7 keys a thread):
+//   1. rank the tile by the top RES_MB bits with shared atomics (keys only:
+//      any order among equal buckets), publish the CTA's bucket counts and add
+//      them to 16-CTA group sums in L2;
+//   2. grid barrier; each bucket's output base = the buckets before it (all
+//      group sums) + the group sums before this CTA's group + the counts of
+//      the CTAs before it in its group; stage the tile in bucket order and
+//      write it;
+//   3. grid barrier; load this CTA's segment -- the buckets that start in its
+//      tile's range -- and sort it in shared memory: bitonic sorts of 256 keys
+//      per warp in registers, then merge-path merges, no grid barrier.
+// When a bucket holds more than a tile (skewed keys, or top bits that never
+// vary) the same launch runs LSD passes instead, per executed 8-bit digit:
+// rank (shared atomics for the first executed pass, owner election and five
+// ballots after), publish, barrier, offsets, stage and write coalesced,
+// barrier, reload.  The passes run in place in the output array: a pass's
+// loads all happen before its first barrier and its stores after it.  The
+// OR / AND words published with the first counts give every CTA the same
+// plan (trivial digits skipped, the inverse transform on the last pass).
 //
-// Measured on one B200 (globaltimer stamps per phase, 2^20 u32 keys on 147
-// CTAs): a barrier built from a generation word cost 2.2-3.9 us (four
-// dependent L2 round trips), and one global OR per warp made the first
-// barrier 6.6 us (4704 atomics on one word).  Here a barrier is one release
-// reduction on a counter that only grows within a launch (the k-th barrier
-// waits for k * gridDim.x arrivals) and the OR/AND words take one atomic per
-// CTA.
+// Measured on one B200 (globaltimer stamps and clock64 laps per phase, 2^20
+// u32 keys on 147 CTAs): a barrier built from a generation word cost 2.2-3.9
+// us (four dependent L2 round trips), and one global OR per warp made the
+// first barrier 6.6 us (4704 atomics on one word).  Here a barrier is one
+// release reduction on a counter that only grows within a launch (the k-th
+// barrier waits for k * gridDim.x arrivals) and the OR/AND words take one
+// atomic per CTA.  Sorting segments with four local LSD passes cost ~6 us a
+// pass (ranking at 70 instructions per 32 keys plus ~3 us of fixed scans
+// and barriers); the merge sort replaced them.
 //
 // The accumulators (group sums, OR/AND words, barrier counter) come in two
 // sets used by alternate launches: each launch clears the set the next one
@@ -139,7 +143,6 @@ struct ResShared {
   uint32_t* tstart; // [RADIX] tile-local start of each digit
   uint32_t* off;    // [RADIX] global position - staging index, per digit
   uint32_t* wsum;   // [RADIX / 32]
-  uint32_t* orw;    // [4] OR / ~AND of the CTA's ordered keys
 };
 
 // Warp-local ranks of `rows` rows of 32 keys: lane l's k-th key is element
@@ -239,13 +242,11 @@ __device__ __forceinline__ void res_warp_starts(const ResShared& sh, F&& on_tota
 }
 
 // After a grid barrier: the output base of each digit of accumulator slot
-// `slot` for CTA c, minus the tile-local digit start (sh.off), and the digit
-// totals' exclusive scan (sh.q2[0], when `starts`).  Loads first (at most
-// MAXG + MAXW a thread), then two block barriers.  Returns the largest digit
-// total (threads tid < RADIX; the caller reduces it if it needs it).
+// `slot` for CTA c, minus the tile-local digit start (sh.off).  Loads first
+// (at most MAXG + MAXW a thread), then two block barriers.
 template <int BLOCK, int MAXG, int MAXW>
-__device__ __forceinline__ uint32_t res_offsets(const ResShared& sh, const uint32_t* grp, const uint32_t* counts,
-                                                uint32_t groups, int slot, bool starts) {
+__device__ __forceinline__ void res_offsets(const ResShared& sh, const uint32_t* grp, const uint32_t* counts,
+                                            uint32_t groups, int slot) {
   constexpr int Q = BLOCK / RADIX;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t d = tid % RADIX, q = tid / RADIX;
@@ -280,9 +281,8 @@ __device__ __forceinline__ uint32_t res_offsets(const ResShared& sh, const uint3
     sh.q2[q][d] = tot;
   }
   __syncthreads();
-  uint32_t tot = 0, dstart = 0;
   if (tid < RADIX) {
-    uint32_t pre = 0;
+    uint32_t tot = 0, pre = 0;
 #pragma unroll
     for (int qq = 0; qq < Q; ++qq) {
       tot += sh.q2[qq][tid];
@@ -295,17 +295,14 @@ __device__ __forceinline__ uint32_t res_offsets(const ResShared& sh, const uint3
       if ((int)lane >= o) x += y;
     }
     if (lane == 31) sh.wsum[warp] = x;
-    dstart = x - tot;
-    sh.off[tid] = dstart + pre - sh.tstart[tid];
+    sh.off[tid] = x - tot + pre - sh.tstart[tid];
   }
   __syncthreads();
   if (tid < RADIX) {
     uint32_t add = 0;
     for (uint32_t w = 0; w < (tid >> 5); ++w) add += sh.wsum[w];
     sh.off[tid] += add;
-    if (starts) sh.q2[0][tid] = dstart + add;
   }
-  return tot;
 }
 
 // Stage the tile's keys in digit order (warp starts in sh.cnt plus ranks),
@@ -494,7 +491,7 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
   const uint32_t tile_n = n - tbase < (uint64_t)Ly::TILE ? (uint32_t)(n - tbase) : (uint32_t)Ly::TILE;
   const uint32_t wofs = warp * Ly::SEG + lane;
   const ResShared sh{reinterpret_cast<uint32_t*>(dsm + Ly::CNT_OFF), dsm + Ly::REP_OFF, s_q, s_q2, s_tpart,
-                     s_tstart, s_off, s_wsum, s_or};
+                     s_tstart, s_off, s_wsum};
   uint32_t* wcnt = sh.cnt + warp * RADIX;
   uint8_t* wrep = sh.rep + warp * RADIX;
   K* stage = reinterpret_cast<K*>(dsm + Ly::STAGE_OFF);
@@ -792,7 +789,7 @@ __global__ void __launch_bounds__(BLOCK, 1) k_resident_sort(const ResArgs a) {
         continue;
       }
     }
-    res_offsets<BLOCK, Ly::MAXG, Ly::MAXW>(sh, grp, a.counts, a.groups, p, false);
+    res_offsets<BLOCK, Ly::MAXG, Ly::MAXW>(sh, grp, a.counts, a.groups, p);
     res_scatter<K, XF, BLOCK, IPT, Ly::STAGE_KEYS, true>(sh, stage, key, rank, wofs, tile_n, shift, kout, n,
                                                           (uint32_t)p == last_exec, ctl);
     moved = true;
