@@ -150,10 +150,14 @@ def measured_peak_hbm():
         return 6650.0, "fallback"
 
 
-def committed_traffic(dtype: str):
-    """Per-key DRAM bytes (read + write) of one stable k_scatter launch from
-    the committed ncu summary, scaled by the caller; None if absent."""
-    p = os.path.join(ROOT, "profiles", "k_scatter_stable_traffic.json")
+def committed_traffic(dtype: str, kernel: str = "k_scatter, stable"):
+    """Per-key DRAM bytes (read + write) of one launch of `kernel` from the
+    committed ncu summaries (profiles/*_traffic.json: the stable k_scatter,
+    the histogram fill), scaled by the caller; None if absent."""
+    name = "k_hf_local_traffic.json" if kernel.startswith("k_hf_local") else "k_scatter_stable_traffic.json"
+    if not kernel.startswith(("k_hf_local", "k_scatter, stable")):
+        return None, None
+    p = os.path.join(ROOT, "profiles", name)
     try:
         with open(p) as f:
             d = json.load(f)
@@ -231,6 +235,87 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ ours
+# Kernels of one sort as the library times them (fs_last_kernel_times), with
+# the algorithmic bytes each moves per key.  Two layouts:
+#   LSD chain (2 + 2P + 1 entries): first count, plan, (count + scan,
+#     scatter) per pass, finalize
+#   keys-only 32-bit sorts from FORGESORT_H16_MIN_KEYS keys (10 entries):
+#     first count (digit 2), plan, scan + scatter (digit 2, unstable),
+#     count + scan + scatter (digit 3, stable), group bounds, group fill,
+#     large groups, finalize
+def kernel_table(times, kb):
+    P = kb
+    if len(times) == 10 and kb == 4:
+        return [
+            ("k_first_count (digit-2 slice counts + OR/AND of all keys, reads every key)", times[0], kb),
+            ("k_scatter, unstable ranking (digit 2, first pass of the top 16 bits)", times[3], 2 * kb),
+            ("k_count + k_slice_scan (digit 3)", times[4], kb),
+            ("k_scatter, stable ranking (digit 3)", times[5], 2 * kb),
+            ("k_hf_local (histogram fill: each top-16-bit group sorted by counting its low 16 bits; "
+             "reads and writes every key)", times[7], 2 * kb),
+            ("k_hf_bounds + k_hf_plan (group starts)", times[6], 0),
+            ("k_hf_big_* (groups over 126975 keys)", times[8], 0),
+        ]
+    rows = [("k_first_count (digit-0 slice counts + OR/AND of all keys, reads every key)", times[0], kb)]
+    rows.append(("k_scatter, unstable ranking (first executed pass, keys only)", times[3], 2 * kb))
+    for p in range(1, P):
+        rows.append(("k_count + k_slice_scan (per-slice digit counts, reads every key)", times[2 + 2 * p], kb))
+        rows.append(("k_scatter, stable ranking (one 8-bit LSD pass: rank, stage, scatter)", times[3 + 2 * p],
+                     2 * kb))
+    return rows
+
+
+def kernel_roofline(sorter, step, stream, m, kb, ms, profile_steps, dt):
+    """Roofline of the dominant kernel (most device time per sort among the
+    kernels that move keys), every kernel's share, and the whole sort against
+    the K(1 + 2P) bytes-per-key model."""
+    import torch
+
+    sorter.set_kernel_timing(True)
+    runs = []
+    with torch.cuda.stream(stream):
+        for _ in range(max(profile_steps, 1)):
+            step()
+            runs.append(sorter.last_kernel_times())
+    sorter.set_kernel_timing(False)
+    avg = [sum(r[i] for r in runs) / len(runs) for i in range(len(runs[0]))]
+    peak, peak_kind = measured_peak_hbm()
+    frac = lambda b, t_ms: round(b / (t_ms * 1e-3) / 1e9 / peak, 4) if t_ms > 0 else None
+    rows = kernel_table(avg, kb)
+    # merge repeated kernels (the LSD chain's passes) by name
+    merged = {}
+    for name, t, bpk in rows:
+        e = merged.setdefault(name, {"ms": 0.0, "launches": 0, "bpk": bpk})
+        e["ms"] += t
+        e["launches"] += 1
+    dom_name = max((k for k in merged if merged[k]["bpk"] > 0), key=lambda k: merged[k]["ms"])
+    dom = merged[dom_name]
+    launch_ms = dom["ms"] / dom["launches"]
+    alg = m * dom["bpk"]
+    achieved = alg / (launch_ms * 1e-3) / 1e9
+    tr_per_key, tr_rec = committed_traffic(dt, dom_name)
+    P = kb
+    total = sum(e["ms"] for e in merged.values())
+    roofline = {
+        "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+        "traffic": round(tr_per_key * m) if tr_per_key else None,
+        "kernel": dom_name,
+        "alg_bytes_per_launch": alg,
+        "launch_ms": round(launch_ms, 4),
+        "kernels": [{"kernel": k, "launches": e["launches"], "ms": round(e["ms"], 4),
+                     "share": round(e["ms"] / total, 4) if total else None,
+                     "frac": frac(m * e["bpk"] * e["launches"], e["ms"]) if e["bpk"] else None}
+                    for k, e in merged.items()],
+        "sort_alg_bytes_per_key": kb * (1 + 2 * P),
+        "sort_frac": frac(m * kb * (1 + 2 * P), ms),
+        "sort_bytes_moved_per_key": sum(e["bpk"] * e["launches"] for e in merged.values()),
+    }
+    if tr_rec:
+        roofline["traffic_source"] = tr_rec.get("source")
+    return roofline
+
+
 def run_ours(args):
     import torch
     import torch.distributed as tdist
@@ -284,47 +369,7 @@ def run_ours(args):
     tail = keys_out[: 1 << 20].cpu().numpy().view("u4" if kb == 4 else "u8")
     assert (tail[1:] >= tail[:-1]).all(), "bench output not sorted"
 
-    # roofline of the dominant kernel: the stable k_scatter of passes 1..P-1
-    # (the first executed pass of a keys-only sort ranks unstably and is
-    # timed separately).  Kernel timing order: histogram, plan,
-    # (count+scan, scatter pair) x P, finalize.
-    sorter.set_kernel_timing(True)
-    P = kb
-    stable_ms, first_ms, count_ms, hist_l = [], [], [], []
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.profile_steps, 1)):
-            step()
-            t = sorter.last_kernel_times()
-            hist_l.append(t[0])
-            count_ms.extend(t[2 + 2 * p] for p in range(1, P))
-            first_ms.append(t[3])
-            stable_ms.extend(t[3 + 2 * p] for p in range(1, P))
-    sorter.set_kernel_timing(False)
-    avg = lambda v: sum(v) / len(v)
-    hist_ms, count_avg, first_avg, stable_avg = avg(hist_l), avg(count_ms), avg(first_ms), avg(stable_ms)
-    peak, peak_kind = measured_peak_hbm()
-    alg_bytes_pass = m * 2 * kb  # read every key once, write it once
-    achieved = alg_bytes_pass / (stable_avg * 1e-3) / 1e9
-    tr_per_key, tr_rec = committed_traffic(dt)
-    frac = lambda b, t_ms: round(b / (t_ms * 1e-3) / 1e9 / peak, 4)
-    roofline = {
-        "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-        "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-        "traffic": round(tr_per_key * m) if tr_per_key else None,
-        "kernel": "k_scatter, stable ranking (one 8-bit LSD pass: rank, stage, scatter)",
-        "alg_bytes_per_launch": alg_bytes_pass,
-        "launch_ms": round(stable_avg, 4),
-        "first_pass": {"kernel": "k_scatter, unstable ranking (first executed pass, keys only)",
-                       "ms": round(first_avg, 4), "frac": frac(alg_bytes_pass, first_avg)},
-        "count": {"kernel": "k_count + k_slice_scan (per-slice digit counts, reads every key)",
-                  "ms": round(count_avg, 4), "frac": frac(m * kb, count_avg)},
-        "hist": {"kernel": "k_first_count (digit-0 slice counts + OR/AND of all keys, reads every key)",
-                 "ms": round(hist_ms, 4), "frac": frac(m * kb, hist_ms)},
-        "sort_alg_bytes_per_key": kb * (1 + 2 * P),
-        "sort_frac": frac(m * kb * (1 + 2 * P), ms),
-    }
-    if tr_rec:
-        roofline["traffic_source"] = tr_rec.get("source")
+    roofline = kernel_roofline(sorter, step, stream, m, kb, ms, args.profile_steps, dt)
 
     value = m * world / (ms * 1e-3) / 1e6
 
@@ -490,7 +535,10 @@ def run_multi(args):
     t = sorter.last_kernel_times()
     sorter.set_kernel_timing(False)
     P = kb
-    pass_ms = [t[3 + 2 * p] for p in range(1, P)]  # stable passes (pass 0 of keys-only ranks unstably)
+    if op == "keys" and len(t) == 10 and kb == 4:  # histogram-fill form: the stable digit-3 pass
+        pass_ms = [t[5]]
+    else:
+        pass_ms = [t[3 + 2 * p] for p in range(1, P)]  # stable passes (pass 0 of keys-only ranks unstably)
     pass_avg = sum(pass_ms) / len(pass_ms)
     peak, peak_kind = measured_peak_hbm()
     piece = out.numel()

@@ -122,6 +122,13 @@ struct FinalDesc {
 constexpr int DEV_ERR_TIMEOUT = 1;  // a bounded wait (bulk-copy barrier) ran out
 constexpr int DEV_ERR_BOUNDS = 2;  // a scatter position fell outside [0, n)
 
+// Histogram-fill stage of a keys-only 32-bit sort (plan with `h16`): where
+// the keys grouped by their top 16 bits are, and how to read them.
+enum HfFlags : uint32_t {
+  HF_ON = 1u << 0,     // the stage runs
+  HF_XF_IN = 1u << 1,  // no pass ran: the source holds the caller's keys (apply the forward transform)
+};
+
 struct SortCtl {
   // Accumulators, cleared before every sort (the first CTL_ACCUM_BYTES):
   unsigned long long hist[MAX_PASSES][RADIX];  // global digit counts of each pass
@@ -129,6 +136,11 @@ struct SortCtl {
   unsigned long long kandn;  // OR of all complemented ordered keys (= ~AND)
   PassDesc pass[MAX_PASSES];
   FinalDesc fin;
+  const void* hf_src;  // keys grouped by their top 16 bits (ordered unless HF_XF_IN)
+  void* hf_dst;        // where the histogram fill writes the sorted keys
+  void* hf_pool;       // a buffer of n keys that is free during the fill: the
+                       // histograms of the groups too large for one CTA
+  uint32_t hf_flags;   // HfFlags
   int err;  // first device-side failure (DEV_ERR_*)
 };
 
@@ -167,6 +179,10 @@ struct PlanArgs {
                                    // digit holding all n keys (single-pass plans)
   int test_withhold;               // failure-path test (fs_test_inject): mark the
                                    // first executed pass PD_TEST_WITHHOLD
+  int h16;                         // keys-only 32-bit sort: only the passes of the
+                                   // top two digits run (the first may rank
+                                   // unstably); the histogram fill sorts each
+                                   // top-16-bit group by its low 16 bits
 };
 
 }  // namespace fs

@@ -264,8 +264,9 @@ __device__ __forceinline__ void for_each_key(const K* __restrict__ keys, uint64_
 
 // --------------------------------------------------------------------------
 // First count: one read of the keys gives
-//   - the slice counts of digit 0 of the ordered keys (counts[c][d]) and
-//     their global totals (ctl->hist[0]),
+//   - the slice counts of the digit of pass `fpass` (0 for an LSD sort, 2
+//     when only the top two digits are sorted by passes) of the ordered keys
+//     (counts[c][d]) and their global totals (ctl->hist[fpass]),
 //   - the OR of the ordered keys and the OR of their complements: a digit
 //     whose bits never vary marks a pass that would be the identity, which the
 //     plan skips before any scatter runs.
@@ -279,7 +280,7 @@ __device__ __forceinline__ void for_each_key(const K* __restrict__ keys, uint64_
 template <typename K, int XF, int BLOCK, bool VEC>
 __global__ void __launch_bounds__(BLOCK)
     k_first_count(const K* __restrict__ keys, const uint64_t n, SortCtl* __restrict__ ctl, const Slices sl,
-                  uint32_t* __restrict__ counts /* [count][RADIX] */) {
+                  uint32_t* __restrict__ counts /* [count][RADIX] */, const int fpass) {
   chain_wait();
   constexpr int WARPS = BLOCK / 32;
   __shared__ uint32_t hw[WARPS][RADIX];
@@ -289,7 +290,7 @@ __global__ void __launch_bounds__(BLOCK)
   for (int i = threadIdx.x; i < RADIX; i += BLOCK) tot[i] = 0;
   __syncthreads();
   K kor = 0, kandn = 0;
-  const RadixDigit dg{0};
+  const RadixDigit dg{fpass * RADIX_BITS};
   for (uint32_t c = blockIdx.x; c < sl.count; c += gridDim.x) {
     const uint64_t lo = (uint64_t)c * sl.keys_per_slice;
     const uint64_t hi = lo + sl.keys_per_slice < n ? lo + sl.keys_per_slice : n;
@@ -315,7 +316,7 @@ __global__ void __launch_bounds__(BLOCK)
     __syncthreads();
   }
   for (int b = threadIdx.x; b < RADIX; b += BLOCK)
-    if (tot[b]) atomicAdd(&ctl->hist[0][b], (unsigned long long)tot[b]);
+    if (tot[b]) atomicAdd(&ctl->hist[fpass][b], (unsigned long long)tot[b]);
   // bitwise reductions: warp, then one atomic pair per warp
   uint32_t lo_or = __reduce_or_sync(0xffffffffu, (uint32_t)kor);
   uint32_t lo_an = __reduce_or_sync(0xffffffffu, (uint32_t)kandn);
@@ -468,6 +469,7 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
   if (a.trivial_from_bits) {
     const unsigned long long varying = ctl->kor & ctl->kandn;
     if (d < a.passes) s_exec[d] = ((varying >> (RADIX_BITS * d)) & (RADIX - 1)) != 0;
+    if (a.h16 && d < 2) s_exec[d] = 0;  // the low 16 bits belong to the histogram fill
   } else {
     const int trivial = __syncthreads_or(c0 == a.n);
     if (d == 0) s_exec[0] = a.force_exec || !trivial;
@@ -495,11 +497,11 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
       uint32_t* vdst = slot_final ? a.vfinal : a.vother;
       uint32_t f = PD_EXEC;
       if (i == 1) f |= PD_XF_IN | PD_FIRST;
-      if (i == 1 && p == 0 && !a.has_vals && a.unstable_first) f |= PD_UNSTABLE;
+      if (i == 1 && (p == 0 || a.h16) && !a.has_vals && a.unstable_first) f |= PD_UNSTABLE;
       if (i == 1 && a.has_vals && a.vin == nullptr) f |= PD_SYNTH_IDX;
       if (i == 1 && a.test_withhold) f |= PD_TEST_WITHHOLD;
-      if (i == m) f |= PD_XF_OUT;
-      if (a.write_keys || i < m) f |= PD_WRITE_KEYS;
+      if (i == m && !a.h16) f |= PD_XF_OUT;  // h16: the histogram fill writes the caller's form
+      if (a.write_keys || i < m || a.h16) f |= PD_WRITE_KEYS;
       pd.kin = kprev;
       pd.kout = kdst;
       pd.vin = vprev;
@@ -513,6 +515,36 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
   }
   FinalDesc fin{};
   fin.executed_passes = (uint32_t)m;
+  if (a.h16) {
+    // The histogram fill reads the grouped keys wherever the passes left
+    // them (in place is safe: each group is read whole before it is
+    // written) and writes kfinal.  Keys that are all equal need neither.
+    // The pool for the large groups' histograms takes the n-key buffer the
+    // fill neither reads nor writes; a pass that sorted in place into OTHER
+    // is filled there in place and copied back.
+    const bool all_equal = (ctl->kor & ctl->kandn & 0xffffffffull) == 0;
+    ctl->hf_src = kprev;
+    ctl->hf_flags = all_equal ? 0u : (HF_ON | (m == 0 ? HF_XF_IN : 0u));
+    if (kprev == a.kother) {  // in place, one pass
+      ctl->hf_dst = a.kother;
+      ctl->hf_pool = a.kfinal;
+      if (!all_equal) {
+        fin.ops |= FIN_COPY_KEYS;
+        fin.ksrc = a.kother;
+        fin.kdst = a.kfinal;
+      }
+    } else {
+      ctl->hf_dst = a.kfinal;
+      ctl->hf_pool = a.kother;
+    }
+    if (all_equal && a.kin != a.kfinal) {
+      fin.ops |= FIN_COPY_KEYS;
+      fin.ksrc = a.kin;
+      fin.kdst = a.kfinal;
+    }
+    ctl->fin = fin;
+    return;
+  }
   if (m > 0) {
     if (kprev != a.kfinal) {  // ended in OTHER
       if (a.write_keys) {
@@ -838,6 +870,31 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       const bool valid = FULL || (wofs + k * 32) < tile_n;
       const uint32_t d = digit(k);
       rank.set(k, valid ? atomicAdd(&wcnt[d], 1u) : 0u);
+    }
+  } else if constexpr (FS_RANK_BALLOT == 4 && R > 32) {
+    // Owner election as below, but the owner advances the warp's count with
+    // one shared atomic that returns the old count, and the group reads it
+    // from the owner by shuffle: one random shared access per group instead
+    // of a load by every lane plus the owner's store.
+#pragma unroll
+    for (int k = 0; k < IPT; ++k) {
+      const bool valid = FULL || (wofs + k * 32) < tile_n;
+      const uint32_t d = digit(k);
+      if (valid) wrep[d] = (uint8_t)lane;
+      __syncwarp();
+      const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
+      uint32_t diff = 0;
+#pragma unroll
+      for (int b = 0; b < 5; ++b) {
+        const uint32_t bit = (own >> b) & 1u;
+        diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
+      }
+      const uint32_t peers = ~diff;
+      uint32_t old = 0;
+      if (valid && lane == own) old = atomicAdd(&wcnt[d], (uint32_t)__popc(peers));
+      old = __shfl_sync(0xffffffffu, old, own);
+      __syncwarp();  // this round's owner-byte reads precede the next round's writes
+      rank.set(k, old + __popc(peers & lt_mask));
     }
   } else if constexpr (FS_RANK_BALLOT == 3 && R > 32) {
     // Owner election: every lane writes its lane number into its digit's

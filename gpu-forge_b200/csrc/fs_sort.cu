@@ -9,6 +9,7 @@
 #include "fs_resident.cuh"
 #include "fs_hoststage.h"
 #include "fs_kernels.cuh"
+#include "fs_histfill.cuh"
 
 #include <cstdarg>
 #include <atomic>
@@ -51,6 +52,11 @@ struct fs_sorter {
   void* res_counts = nullptr;
   size_t res_counts_bytes = 0;
   int res_parity = 0;
+  void* hf = nullptr;  // histogram fill of keys-only 32-bit sorts (HfCtl)
+  size_t hf_bytes = 0;
+  uint64_t h16_min = 1ull << 31;  // keys-only 32-bit sorts of at least this many keys sort the top 16
+                                  // bits by passes and the low 16 by the histogram fill
+                                  // (FORGESORT_H16_MIN_KEYS; 0: never)
   // after a failure the device error word may be left set: the next sort
   // clears it first
   bool ctl_dirty = true;
@@ -373,6 +379,7 @@ struct Exec {
   int* err_out;
   uint32_t* counts;      // >= slices * 256 words
   uint32_t* offsets;     // >= slices * 256 words
+  HfCtl* hf;             // histogram fill scratch (h16 plans only)
   fs_sorter* s;
 };
 
@@ -491,10 +498,10 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
   FS_CUDA(e.s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
   if ((reinterpret_cast<uintptr_t>(a.kin) & 15) == 0)
     k_first_count<K, XF, HIST_BLOCK, true>
-        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts);
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts, 0);
   else
     k_first_count<K, XF, HIST_BLOCK, false>
-        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts);
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts, 0);
   t_end(e);
   // 2. plan
   PlanArgs pa = a;
@@ -538,6 +545,94 @@ int enqueue_sort(const Exec& e, const PlanArgs& a, const Slices& sl, int* launch
     return rc;
   t_end(e);
   if (launches) *launches = nl + 1;
+  FS_CUDA(e.s, cudaGetLastError());
+  return FS_OK;
+}
+
+// Keys-only 32-bit sort of many keys: the passes of digits 2 and 3 group the
+// keys by their top 16 bits (digit 2 ranks unstably, being the first pass
+// that can run; digit 3 stably), then the histogram fill sorts every group by
+// its low 16 bits (fs_histfill.cuh).  Launches: first count (digit 2), plan,
+// scan + scatter (digit 2), count + scan + scatter (digit 3), bounds, plan of
+// the large groups, the per-group fill, the large groups' zero / count / scan
+// / fill, finalize.
+template <int XF>
+int enqueue_h16(const Exec& e, const PlanArgs& a, const Slices& sl, int* launches) {
+  using K = uint32_t;
+  const uint64_t n = a.n;
+  const unsigned sg = stream_grid(e, sl);
+  if (e.s) e.s->ev_used = 0;
+  t_begin(e);
+  FS_CUDA(e.s, cudaMemsetAsync(e.ctl, 0, CTL_ACCUM_BYTES, e.stream));
+  if ((reinterpret_cast<uintptr_t>(a.kin) & 15) == 0)
+    k_first_count<K, XF, HIST_BLOCK, true>
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts, 2);
+  else
+    k_first_count<K, XF, HIST_BLOCK, false>
+        <<<sg, HIST_BLOCK, 0, e.stream>>>(static_cast<const K*>(a.kin), n, e.ctl, sl, e.counts, 2);
+  t_end(e);
+  PlanArgs pa = a;
+  pa.trivial_from_bits = 1;
+  pa.h16 = 1;
+  int rc;
+  t_begin(e);
+  if ((rc = chain_launch(e, k_plan, 1, RADIX, 0, e.ctl, pa))) return rc;
+  t_end(e);
+  for (int p = 2; p < 4; ++p) {
+    t_begin(e);
+    if (p == 3 && (rc = chain_launch(e, k_count<K, XF, HIST_BLOCK>, sg, HIST_BLOCK, 0, e.ctl, p, n, sl, e.counts)))
+      return rc;
+    if ((rc = chain_launch(e, k_slice_scan, SCAN_GROUPS, SCAN_WARPS * 32, 0, e.ctl, p, sl,
+                           static_cast<const uint32_t*>(e.counts), e.offsets, 0)))
+      return rc;
+    t_end(e);
+    t_begin(e);
+    const RadixDigit dg{p * RADIX_BITS};
+    rc = p == 2 ? launch_scatter<K, false, XF, UnstableCfg<K>, SCATTER_UNSTABLE>(e, p, n, sl, dg, 0ull)
+                : launch_scatter<K, false, XF, StableCfg<K, false>, SCATTER_ANY>(e, p, n, sl, dg, 0ull);
+    t_end(e);
+    if (rc) return rc;
+  }
+  // histogram fill: one CTA per SM (136 KiB of counters each)
+  static std::atomic<bool> configured[MAX_DEVICES];
+  if (e.device < 0 || e.device >= MAX_DEVICES)
+    return fail(e.s, FS_E_INVALID, "device %d outside [0, %d)", e.device, MAX_DEVICES);
+  if (!configured[e.device].load()) {
+    FS_CUDA(e.s, cudaFuncSetAttribute(k_hf_local<XF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)HF_LOCAL_SMEM_STAGED));
+    FS_CUDA(e.s, cudaFuncSetAttribute(k_hf_big_count<XF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)HF_BIG_SMEM));
+    configured[e.device].store(true);
+  }
+  t_begin(e);
+  if ((rc = chain_launch(e, k_hf_bounds<XF>, (HF_GROUPS + 1 + 255) / 256, 256, 0, (const SortCtl*)e.ctl, e.hf, n)))
+    return rc;
+  if ((rc = chain_launch(e, k_hf_plan, 1, HF_BLOCK, 0, (const SortCtl*)e.ctl, e.hf))) return rc;
+  t_end(e);
+  t_begin(e);
+  if ((rc = chain_launch(e, k_hf_local<XF>, (unsigned)e.sm_count, HF_BLOCK, HF_LOCAL_SMEM_STAGED, (const SortCtl*)e.ctl,
+                         (const HfCtl*)e.hf)))
+    return rc;
+  t_end(e);
+  t_begin(e);
+  if ((rc = chain_launch(e, k_hf_big_zero, (unsigned)e.sm_count * 4, 256, 0, (const SortCtl*)e.ctl,
+                         (const HfCtl*)e.hf)))
+    return rc;
+  if ((rc = chain_launch(e, k_hf_big_count<XF>, (unsigned)e.sm_count, HF_BLOCK, HF_BIG_SMEM, (const SortCtl*)e.ctl,
+                         (const HfCtl*)e.hf)))
+    return rc;
+  if ((rc = chain_launch(e, k_hf_big_scan, (unsigned)e.sm_count, HF_BLOCK, 0, (const SortCtl*)e.ctl, e.hf)))
+    return rc;
+  if ((rc = chain_launch(e, k_hf_big_fill<XF>, (unsigned)e.sm_count, HF_BLOCK, 0, (const SortCtl*)e.ctl,
+                         (const HfCtl*)e.hf)))
+    return rc;
+  t_end(e);
+  uint64_t fb = (n + 255) / 256;
+  const uint64_t fcap = (uint64_t)e.sm_count * 4;
+  t_begin(e);
+  if ((rc = chain_launch(e, k_finalize<K>, (unsigned)(fb < fcap ? fb : fcap), 256, 0, e.ctl, n, e.err_out)))
+    return rc;
+  t_end(e);
+  if (launches) *launches = 15;
   FS_CUDA(e.s, cudaGetLastError());
   return FS_OK;
 }
@@ -756,6 +851,16 @@ int dispatch(fs_sorter* s, int dtype, const PlanArgs& a) {
   PlanArgs pa = a;
   pa.test_withhold = s->test_withhold;
   s->test_withhold = 0;  // one-shot
+  if (!a.has_vals && a.unstable_first && a.write_keys && key_bytes_of(dtype) == 4 && s->h16_min > 0 &&
+      a.n >= s->h16_min && a.kother != nullptr && a.kother != a.kfinal) {
+    if ((rc = grow(s, &s->hf, &s->hf_bytes, sizeof(HfCtl), false))) return rc;
+    e.hf = static_cast<HfCtl*>(s->hf);
+    switch (dtype) {
+      case FS_U32: return enqueue_h16<XF_NONE>(e, pa, sl, &s->last_launches);
+      case FS_I32: return enqueue_h16<XF_SIGN>(e, pa, sl, &s->last_launches);
+      default: return enqueue_h16<XF_FLOAT>(e, pa, sl, &s->last_launches);
+    }
+  }
   return dispatch_enqueue(e, dtype, pa, sl, &s->last_launches);
 }
 
@@ -1101,6 +1206,10 @@ int fs_create(int device, void* stream, fs_sorter** out) {
     const long long v = atoll(t);
     s->coop_max_bytes = v <= 0 ? 0ull : (uint64_t)v;
   }
+  if (const char* t = getenv("FORGESORT_H16_MIN_KEYS")) {  // keys; 0: never the histogram fill
+    const long long v = atoll(t);
+    s->h16_min = v <= 0 ? 0ull : (uint64_t)v;
+  }
   *out = s;
   return FS_OK;
 }
@@ -1126,7 +1235,8 @@ int fs_destroy(fs_sorter* s) {
   if (s->d2h) cudaStreamSynchronize(s->d2h), cudaStreamDestroy(s->d2h);
   if (s->pipe_start) cudaEventDestroy(s->pipe_start);
   s->stage.release();
-  void* bufs[] = {s->counts, s->offsets, s->kother, s->kfinal2, s->vother, s->dkeys, s->dvals, s->dst_tab, s->ctl};
+  void* bufs[] = {s->counts, s->offsets, s->kother, s->kfinal2, s->vother,    s->dkeys,
+                  s->dvals,  s->dst_tab, s->ctl,    s->res_acc, s->res_counts, s->hf};
   for (void* b : bufs)
     if (b) cudaFree(b);
   if (s->host_err) cudaFreeHost(s->host_err);
