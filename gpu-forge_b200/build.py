@@ -25,7 +25,7 @@ FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
 TARGETS = {
     os.path.join(PKG, "forge_sort", "libforgesort.so"): {
         "srcs": ["fs_sort.cu", "fs_multi.cu", "fs_datagen.cu"],
-        "deps": ["fs_device.cuh", "fs_kernels.cuh", "fs_resident.cuh", "fs_hoststage.h"],
+        "deps": ["fs_device.cuh", "fs_kernels.cuh", "fs_histfill.cuh", "fs_resident.cuh", "fs_hoststage.h"],
         "hdrs": ["forgesort.h", "forgesort_bench.h"],
         "libs": [],
     },
