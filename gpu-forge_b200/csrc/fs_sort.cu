@@ -54,7 +54,7 @@ struct fs_sorter {
   int res_parity = 0;
   void* hf = nullptr;  // histogram fill of keys-only 32-bit sorts (HfCtl)
   size_t hf_bytes = 0;
-  uint64_t h16_min = 1ull << 31;  // keys-only 32-bit sorts of at least this many keys sort the top 16
+  uint64_t h16_min = 1ull << 30;  // keys-only 32-bit sorts of at least this many keys sort the top 16
                                   // bits by passes and the low 16 by the histogram fill
                                   // (FORGESORT_H16_MIN_KEYS; 0: never)
   // after a failure the device error word may be left set: the next sort
