@@ -92,6 +92,8 @@ enum PassFlags : uint32_t {
   PD_FIRST = 1u << 5,       // first executed pass (reads the caller's keys)
   PD_UNSTABLE = 1u << 6,    // keys-only first pass: order among equal digits is free
   PD_TEST_WITHHOLD = 1u << 7,  // failure-path test: CTA 0 never issues its first bulk copy
+  PD_SORTED_BELOW = 1u << 8,   // keys only: the input is sorted by the bits in `below`, and
+                               // only their order has to survive among equal digits
 };
 
 struct PassDesc {
@@ -100,7 +102,7 @@ struct PassDesc {
   const uint32_t* vin;
   uint32_t* vout;
   uint32_t flags;
-  uint32_t pad;
+  uint32_t below;  // PD_SORTED_BELOW: bits of the (32-bit, ordered) key whose order the pass keeps
 };
 
 enum FinalOps : uint32_t {

@@ -502,6 +502,14 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
       if (i == 1 && a.test_withhold) f |= PD_TEST_WITHHOLD;
       if (i == m && !a.h16) f |= PD_XF_OUT;  // h16: the histogram fill writes the caller's form
       if (a.write_keys || i < m || a.h16) f |= PD_WRITE_KEYS;
+      // Keys only, not the first pass: the input is sorted by the digits
+      // below (LSD: all lower bits; h16: digit 2 -- the fill orders the rest),
+      // and equal keys are identical bits, so a warp round whose keys agree
+      // on those bits may rank its equal digits in any order.
+      if (i > 1 && !a.has_vals && a.key_bytes == 4) {
+        f |= PD_SORTED_BELOW;
+        pd.below = a.h16 ? 0x00ff0000u : (uint32_t)((1ull << (RADIX_BITS * p)) - 1ull);
+      }
       pd.kin = kprev;
       pd.kout = kdst;
       pd.vin = vprev;
@@ -801,7 +809,8 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
                                              unsigned char* dsm, uint32_t* s_run, uint32_t* s_off,
                                              uint32_t* s_wsum, SortCtl* __restrict__ ctl, const D& dfn,
                                              const uint64_t gpos_base, K* const* s_dst, const uint32_t* s_lim,
-                                             uint32_t* const* s_vdst, const Hook& on_loaded = Hook{}) {
+                                             uint32_t* const* s_vdst, const uint32_t below,
+                                             const Hook& on_loaded = Hook{}) {
   constexpr int R = D::DIGITS;
   using Ly = ScatterLayout<K, VALS, BLOCK, IPT, D::STAGE, R, SLOTS>;
   const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -876,10 +885,24 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     // one shared atomic that returns the old count, and the group reads it
     // from the owner by shuffle: one random shared access per group instead
     // of a load by every lane plus the owner's store.
+    const bool sorted_below = !VALS && sizeof(K) == 4 && (flags & PD_SORTED_BELOW) != 0;
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
       const uint32_t d = digit(k);
+      if (sorted_below) {
+        // the round's 32 consecutive keys agree on the bits below: any order
+        // among equal digits is the stable one up to equal keys, so one
+        // shared atomic per key ranks the round
+        const uint32_t lb = (uint32_t)key[k] & below;
+        const uint32_t mn = __reduce_min_sync(0xffffffffu, valid ? lb : 0xffffffffu);
+        const uint32_t mx = __reduce_max_sync(0xffffffffu, valid ? lb : 0u);
+        if (mn >= mx) {
+          rank.set(k, valid ? atomicAdd(&wcnt[d], 1u) : 0u);
+          __syncwarp();
+          continue;
+        }
+      }
       if (valid) wrep[d] = (uint8_t)lane;
       __syncwarp();
       const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
@@ -902,10 +925,24 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
     // (whichever write landed).  Lanes sharing a digit are then exactly the
     // lanes sharing an owner: five ballots over the owner's bits instead of
     // eight over the digit's.  The owner advances the running count.
+    const bool sorted_below = !VALS && sizeof(K) == 4 && (flags & PD_SORTED_BELOW) != 0;
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
       const uint32_t d = digit(k);
+      if (sorted_below) {
+        // the round's 32 consecutive keys agree on the bits below: any order
+        // among equal digits is the stable one up to equal keys, so one
+        // shared atomic per key ranks the round
+        const uint32_t lb = (uint32_t)key[k] & below;
+        const uint32_t mn = __reduce_min_sync(0xffffffffu, valid ? lb : 0xffffffffu);
+        const uint32_t mx = __reduce_max_sync(0xffffffffu, valid ? lb : 0u);
+        if (mn >= mx) {
+          rank.set(k, valid ? atomicAdd(&wcnt[d], 1u) : 0u);
+          __syncwarp();
+          continue;
+        }
+      }
       if (valid) wrep[d] = (uint8_t)lane;
       __syncwarp();
       const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
@@ -1151,15 +1188,15 @@ __global__ void __launch_bounds__(BLOCK, MINB)
       if (from_slot)
         scatter_tile<K, VALS, XF, BLOCK, IPT, true, true, MODE == SCATTER_UNSTABLE, D, SLOTS, decltype(refill), PACK>(
             t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
-            s_dst, s_lim, s_vdst, refill);
+            s_dst, s_lim, s_vdst, pd.below, refill);
       else if (full)
         scatter_tile<K, VALS, XF, BLOCK, IPT, true, false, MODE == SCATTER_UNSTABLE, D, SLOTS, decltype(refill), PACK>(
             t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
-            s_dst, s_lim, s_vdst, refill);
+            s_dst, s_lim, s_vdst, pd.below, refill);
       else
         scatter_tile<K, VALS, XF, BLOCK, IPT, false, false, MODE == SCATTER_UNSTABLE, D, SLOTS, decltype(refill), PACK>(
             t0, tile_n, n, pd.flags, kin, kout, pd.vin, pd.vout, slot, dsm, s_run, s_off, s_wsum, ctl, dfn, gpos_base,
-            s_dst, s_lim, s_vdst, refill);
+            s_dst, s_lim, s_vdst, pd.below, refill);
     }
   }
   // never leave a bulk copy into this CTA's shared memory in flight
