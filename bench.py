@@ -250,7 +250,8 @@ def kernel_table(times, kb):
             ("k_first_count (digit-2 slice counts + OR/AND of all keys, reads every key)", times[0], kb),
             ("k_scatter, unstable ranking (digit 2, first pass of the top 16 bits)", times[3], 2 * kb),
             ("k_count + k_slice_scan (digit 3)", times[4], kb),
-            ("k_scatter, stable ranking (digit 3)", times[5], 2 * kb),
+            ("k_scatter, digit 3 (keeps digit-2 order: atomic ranks where a warp round agrees on digit 2)",
+             times[5], 2 * kb),
             ("k_hf_local (histogram fill: each top-16-bit group sorted by counting its low 16 bits; "
              "reads and writes every key)", times[7], 2 * kb),
             ("k_hf_bounds + k_hf_plan (group starts)", times[6], 0),
