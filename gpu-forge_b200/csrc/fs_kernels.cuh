@@ -506,7 +506,12 @@ __global__ void __launch_bounds__(RADIX) k_plan(SortCtl* __restrict__ ctl, PlanA
       // below (LSD: all lower bits; h16: digit 2 -- the fill orders the rest),
       // and equal keys are identical bits, so a warp round whose keys agree
       // on those bits may rank its equal digits in any order.
-      if (i > 1 && !a.has_vals && a.key_bytes == 4) {
+      // (64-bit keys: passes 1-3, whose lower bits fit the 32-bit mask).
+      // Only where a value of those bits spans 64 keys or more on average;
+      // with shorter runs few rounds agree and the check only costs
+      // (2^26 u64 keys, pass 3: 0.395 ms with it, 0.375 without).
+      const uint64_t run = a.n >> (a.h16 ? RADIX_BITS * 2 : RADIX_BITS * p);
+      if (i > 1 && !a.has_vals && (a.key_bytes == 4 || p < 4) && run >= 64) {
         f |= PD_SORTED_BELOW;
         pd.below = a.h16 ? 0x00ff0000u : (uint32_t)((1ull << (RADIX_BITS * p)) - 1ull);
       }
@@ -725,7 +730,8 @@ __global__ void __launch_bounds__(SCAN_WARPS * 32)
 //   FS_RANK_BALLOT=2: eight ballots over the digit's bits  4.75 ms/pass
 //   FS_RANK_BALLOT=0: __match_any_sync                      ~2x slower again
 // (The owner byte folded into the counter word, saving one shared load per
-// key, measured 4.01 ms: not kept.)
+// key, measured 4.01 ms; the owner advancing the count with one shared atomic
+// and the group reading it by shuffle, 4.03 ms: neither kept.)
 // warp_peers serves 2 and 0; owner election is written out in scatter_tile.
 // Invalid lanes of a partial tile match nobody but themselves.
 template <bool FULL, int BITS = RADIX_BITS>
@@ -880,52 +886,13 @@ __device__ __forceinline__ void scatter_tile(const uint64_t tbase, const uint32_
       const uint32_t d = digit(k);
       rank.set(k, valid ? atomicAdd(&wcnt[d], 1u) : 0u);
     }
-  } else if constexpr (FS_RANK_BALLOT == 4 && R > 32) {
-    // Owner election as below, but the owner advances the warp's count with
-    // one shared atomic that returns the old count, and the group reads it
-    // from the owner by shuffle: one random shared access per group instead
-    // of a load by every lane plus the owner's store.
-    const bool sorted_below = !VALS && sizeof(K) == 4 && (flags & PD_SORTED_BELOW) != 0;
-#pragma unroll
-    for (int k = 0; k < IPT; ++k) {
-      const bool valid = FULL || (wofs + k * 32) < tile_n;
-      const uint32_t d = digit(k);
-      if (sorted_below) {
-        // the round's 32 consecutive keys agree on the bits below: any order
-        // among equal digits is the stable one up to equal keys, so one
-        // shared atomic per key ranks the round
-        const uint32_t lb = (uint32_t)key[k] & below;
-        const uint32_t mn = __reduce_min_sync(0xffffffffu, valid ? lb : 0xffffffffu);
-        const uint32_t mx = __reduce_max_sync(0xffffffffu, valid ? lb : 0u);
-        if (mn >= mx) {
-          rank.set(k, valid ? atomicAdd(&wcnt[d], 1u) : 0u);
-          __syncwarp();
-          continue;
-        }
-      }
-      if (valid) wrep[d] = (uint8_t)lane;
-      __syncwarp();
-      const uint32_t own = valid ? wrep[d] : lane;  // invalid lanes: groups of one
-      uint32_t diff = 0;
-#pragma unroll
-      for (int b = 0; b < 5; ++b) {
-        const uint32_t bit = (own >> b) & 1u;
-        diff |= __ballot_sync(0xffffffffu, bit) ^ (0u - bit);
-      }
-      const uint32_t peers = ~diff;
-      uint32_t old = 0;
-      if (valid && lane == own) old = atomicAdd(&wcnt[d], (uint32_t)__popc(peers));
-      old = __shfl_sync(0xffffffffu, old, own);
-      __syncwarp();  // this round's owner-byte reads precede the next round's writes
-      rank.set(k, old + __popc(peers & lt_mask));
-    }
   } else if constexpr (FS_RANK_BALLOT == 3 && R > 32) {
     // Owner election: every lane writes its lane number into its digit's
     // byte; after the warp syncs, all lanes of a digit read the same owner
     // (whichever write landed).  Lanes sharing a digit are then exactly the
     // lanes sharing an owner: five ballots over the owner's bits instead of
     // eight over the digit's.  The owner advances the running count.
-    const bool sorted_below = !VALS && sizeof(K) == 4 && (flags & PD_SORTED_BELOW) != 0;
+    const bool sorted_below = !VALS && (flags & PD_SORTED_BELOW) != 0;
 #pragma unroll
     for (int k = 0; k < IPT; ++k) {
       const bool valid = FULL || (wofs + k * 32) < tile_n;
