@@ -80,6 +80,11 @@ int fs_create(int device, void* stream, fs_sorter** out);
  *                              14336 keys per SM) run as one cooperative
  *                              launch with grid barriers instead of the
  *                              chained kernels; 0: always chained
+ *   FORGESORT_H16_MIN_KEYS     keys-only sorts of 32-bit keys of at least
+ *                              this many keys (default 2^30) run only the
+ *                              radix passes of the top two digits and then
+ *                              sort each top-16-bit group by counting its
+ *                              low 16 bits; 0: always the four passes
  * and once per process:
  *   FORGESORT_CHAIN_LAUNCH     0: launch a sort's kernels without programmatic
  *                              stream serialization (default: chained) */
